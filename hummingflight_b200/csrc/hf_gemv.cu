@@ -1,0 +1,374 @@
+// hf_gemv.cu -- decode grouped GEMV over expert segments, weighted combine,
+// and the device twin of gemv_bf16_f32.
+//
+// Reference: expertFFNRaw (model/glm_forward.cpp:434-449): g = G x, u = U x,
+// mid = g / (1 + exp(-g)) * u in fp32, y = D mid; the sm_86 offload replaced
+// here is matvecStreamKernel + siluScaleKernel (compute/cuda_kernels.cu:125-153,
+// one block per row, 2-byte loads, x and y crossing PCIe per expert).
+//
+// B200 design: a segment (the tokens routed to one expert) is cut into chunks
+// of up to kGemvTE tokens. A unit of work is (expert, row block, chunk); units
+// of one expert are adjacent with the chunk index fastest, so a weight row is
+// fetched from HBM once and re-served from L2 to the other chunks. Persistent
+// CTAs (a multiple of the SM count) stride over the unit list the routing
+// kernel wrote. Each warp streams 2 gate + 2 up rows (GEMV1) or 4 down rows
+// (GEMV2) with 16-byte L1-bypassing loads, 8 loads in flight per lane, the
+// chunk's activations sitting in shared memory; fp32 accumulation, butterfly
+// shuffles, SwiGLU in the GEMV1 epilogue, mid kept fp32.
+#include "hf_internal.cuh"
+
+namespace hf {
+
+constexpr int kUnroll = 2;
+
+template <bool XF32>
+__device__ __forceinline__ void lds_x8(const void* xs, int j, int H, int c, float (&o)[8]) {
+    if constexpr (XF32) {
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(xs) +
+                                                          size_t(j) * H + c * 8);
+        const float4 a = p[0], b = p[1];
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+        o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xs) +
+                                                        size_t(j) * H + c * 8);
+        unpack8(v, o);
+    }
+}
+
+// Two gate rows and two up rows (r0, r0+1) against NT tokens held in shared memory.
+template <bool XF32, int NT>
+__device__ __forceinline__ void gemv1_rows(const GroupW& W, int H, int r0, const void* xs,
+                                           int lane, float* mid, int p0, int mid_stride) {
+    const int I = W.inter;
+    if (r0 >= I) return;
+    const bool v1 = (r0 + 1) < I;
+    const uint16_t* pr[4] = {W.gate + size_t(r0) * H, W.gate + size_t(v1 ? r0 + 1 : r0) * H,
+                             W.up + size_t(r0) * H, W.up + size_t(v1 ? r0 + 1 : r0) * H};
+    float acc[4][NT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[r][j] = 0.0f;
+    const int nc = H >> 3;
+    int c = lane;
+    for (; c + 32 * (kUnroll - 1) < nc; c += 32 * kUnroll) {
+        uint4 wv[kUnroll][4];
+#pragma unroll
+        for (int q = 0; q < kUnroll; ++q)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) wv[q][r] = ld_stream_u4(pr[r] + size_t(c + 32 * q) * 8);
+#pragma unroll
+        for (int q = 0; q < kUnroll; ++q) {
+            float wf[4][8];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) unpack8(wv[q][r], wf[r]);
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                float xf[8];
+                lds_x8<XF32>(xs, j, H, c + 32 * q, xf);
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[r][j] = fmaf(wf[r][e], xf[e], acc[r][j]);
+            }
+        }
+    }
+    for (; c < nc; c += 32) {
+        uint4 wv[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) wv[r] = ld_stream_u4(pr[r] + size_t(c) * 8);
+        float wf[4][8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) unpack8(wv[r], wf[r]);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            float xf[8];
+            lds_x8<XF32>(xs, j, H, c, xf);
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[r][j] = fmaf(wf[r][e], xf[e], acc[r][j]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[r][j] = warp_sum(acc[r][j]);
+    // lane q < 2*NT writes (row r0 + (q & 1), token q >> 1)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            if (lane == 2 * j + rr && (rr == 0 || v1)) {
+                const float g = acc[rr][j], u = acc[2 + rr][j];
+                mid[size_t(p0 + j) * mid_stride + r0 + rr] = swiglu(g, u);
+            }
+        }
+    }
+}
+
+template <bool XF32>
+__global__ void __launch_bounds__(256) k_gemv1(GemvArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    void* xs = smem_raw;
+    const int G = a.pl.G;
+    const int32_t* u1 = a.plan + a.pl.u1;
+    const int total = u1[G];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = a.H;
+    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+        const int g = find_group(u1, G, u);
+        const int cnt = a.plan[a.pl.counts + g];
+        const int nch = (cnt + kGemvTE - 1) / kGemvTE;
+        const int local = u - u1[g];
+        const int rb = local / nch, ch = local % nch;
+        const int p0 = a.plan[a.pl.offsets + g] + ch * kGemvTE;
+        const int te = min(kGemvTE, cnt - ch * kGemvTE);
+        __syncthreads();
+        // stage the chunk's activation rows: te x H elements, 16 bytes per thread-step
+        const int vec = XF32 ? 4 : 8;
+        const int per_row = H / vec;
+        for (int i = threadIdx.x; i < te * per_row; i += blockDim.x) {
+            const int j = i / per_row, c = i % per_row;
+            const int t = token_of_slot(a.perm[p0 + j], a.T, a.k);
+            const uint4 v = ld_nc_u4(static_cast<const char*>(a.x) +
+                                     (size_t(t) * H + size_t(c) * vec) * (XF32 ? 4 : 2));
+            reinterpret_cast<uint4*>(xs)[size_t(j) * per_row + c] = v;
+        }
+        __syncthreads();
+        const GroupW W = a.groups[g];
+        const int r0 = rb * kGemv1Rows + warp * 2;
+        switch (te) {
+            case 1: gemv1_rows<XF32, 1>(W, H, r0, xs, lane, a.mid, p0, a.inter_max); break;
+            case 2: gemv1_rows<XF32, 2>(W, H, r0, xs, lane, a.mid, p0, a.inter_max); break;
+            case 3: gemv1_rows<XF32, 3>(W, H, r0, xs, lane, a.mid, p0, a.inter_max); break;
+            default: gemv1_rows<XF32, 4>(W, H, r0, xs, lane, a.mid, p0, a.inter_max); break;
+        }
+    }
+}
+
+// Four down rows (h0..h0+3) against NT mid vectors (fp32, shared memory).
+template <int NT>
+__device__ __forceinline__ void gemv2_rows(const GroupW& W, int H, int h0, const float* ms,
+                                           int lane, float* y, int p0) {
+    const int I = W.inter;
+    if (h0 >= H) return;
+    const uint16_t* pr[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) pr[r] = W.down + size_t(min(h0 + r, H - 1)) * I;
+    float acc[4][NT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[r][j] = 0.0f;
+    const int nc = I >> 3;
+    int c = lane;
+    for (; c + 32 * (kUnroll - 1) < nc; c += 32 * kUnroll) {
+        uint4 wv[kUnroll][4];
+#pragma unroll
+        for (int q = 0; q < kUnroll; ++q)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) wv[q][r] = ld_stream_u4(pr[r] + size_t(c + 32 * q) * 8);
+#pragma unroll
+        for (int q = 0; q < kUnroll; ++q) {
+            float wf[4][8];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) unpack8(wv[q][r], wf[r]);
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                float xf[8];
+                lds_x8<true>(ms, j, I, c + 32 * q, xf);
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[r][j] = fmaf(wf[r][e], xf[e], acc[r][j]);
+            }
+        }
+    }
+    for (; c < nc; c += 32) {
+        uint4 wv[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) wv[r] = ld_stream_u4(pr[r] + size_t(c) * 8);
+        float wf[4][8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) unpack8(wv[r], wf[r]);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            float xf[8];
+            lds_x8<true>(ms, j, I, c, xf);
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[r][j] = fmaf(wf[r][e], xf[e], acc[r][j]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[r][j] = warp_sum(acc[r][j]);
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            if (lane == 4 * j + r && h0 + r < H) y[size_t(p0 + j) * H + h0 + r] = acc[r][j];
+}
+
+__global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float* ms = reinterpret_cast<float*>(smem_raw);
+    const int G = a.pl.G;
+    const int32_t* u2 = a.plan + a.pl.u2;
+    const int total = u2[G];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = a.H;
+    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+        const int g = find_group(u2, G, u);
+        const int cnt = a.plan[a.pl.counts + g];
+        const int nch = (cnt + kGemvTE - 1) / kGemvTE;
+        const int local = u - u2[g];
+        const int rb = local / nch, ch = local % nch;
+        const int p0 = a.plan[a.pl.offsets + g] + ch * kGemvTE;
+        const int te = min(kGemvTE, cnt - ch * kGemvTE);
+        const GroupW W = a.groups[g];
+        const int I = W.inter;
+        __syncthreads();
+        const int per_row = I / 4;
+        for (int i = threadIdx.x; i < te * per_row; i += blockDim.x) {
+            const int j = i / per_row, c = i % per_row;
+            reinterpret_cast<float4*>(ms)[size_t(j) * per_row + c] =
+                *reinterpret_cast<const float4*>(a.mid + size_t(p0 + j) * a.inter_max + c * 4);
+        }
+        __syncthreads();
+        const int h0 = rb * kGemv2Rows + warp * 4;
+        switch (te) {
+            case 1: gemv2_rows<1>(W, H, h0, ms, lane, a.y, p0); break;
+            case 2: gemv2_rows<2>(W, H, h0, ms, lane, a.y, p0); break;
+            case 3: gemv2_rows<3>(W, H, h0, ms, lane, a.y, p0); break;
+            default: gemv2_rows<4>(W, H, h0, ms, lane, a.y, p0); break;
+        }
+    }
+}
+
+size_t gemv1_smem(int H, bool xf32) { return size_t(kGemvTE) * H * (xf32 ? 4 : 2); }
+size_t gemv2_smem(int inter_max) { return size_t(kGemvTE) * inter_max * 4; }
+
+hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st) {
+    const size_t s1 = gemv1_smem(a.H, a.x_f32 != 0);
+    if (a.x_f32) {
+        HF_CUDA(cudaFuncSetAttribute(k_gemv1<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)s1));
+        k_gemv1<true><<<a.grid1, 256, s1, st>>>(a);
+    } else {
+        HF_CUDA(cudaFuncSetAttribute(k_gemv1<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)s1));
+        k_gemv1<false><<<a.grid1, 256, s1, st>>>(a);
+    }
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+hf_status launch_gemv2(const GemvArgs& a, cudaStream_t st) {
+    const size_t s2 = gemv2_smem(a.inter_max);
+    HF_CUDA(cudaFuncSetAttribute(k_gemv2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2));
+    k_gemv2<<<a.grid2, 256, s2, st>>>(a);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+int gemv_grid(int device, bool first, bool xf32, int H, int inter_max) {
+    int per_sm = 1;
+    if (first) {
+        const size_t s = gemv1_smem(H, xf32);
+        auto kern = xf32 ? k_gemv1<true> : k_gemv1<false>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, s);
+    } else {
+        const size_t s = gemv2_smem(inter_max);
+        cudaFuncSetAttribute(k_gemv2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv2, 256, s);
+    }
+    if (per_sm < 1) per_sm = 1;
+    return per_sm * num_sms(device);
+}
+
+// ============================================================ combine
+// glm_forward.cpp:555-556, 639-640, 658-660: moeOut = 0; moeOut += w_i * y_i in
+// top-k rank order (separate multiply and add); output = moeOut + sharedOut.
+__global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
+    const int H4 = a.H >> 2;
+    const size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= size_t(a.T) * H4) return;
+    const int t = int(idx / H4), h = int(idx % H4) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < a.k; ++i) {
+        const int slot = t * a.k + i;
+        const int pos = a.slot_pos[slot];
+        const float wi = a.w[slot];
+        const float4 y = *reinterpret_cast<const float4*>(a.y + size_t(pos) * a.H + h);
+        acc.x = __fadd_rn(acc.x, __fmul_rn(wi, y.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(wi, y.y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(wi, y.z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(wi, y.w));
+        if (a.slot_out) *reinterpret_cast<float4*>(a.slot_out + size_t(slot) * a.H + h) = y;
+    }
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.has_shared) {
+        const int slot = a.T * a.k + t;
+        s = *reinterpret_cast<const float4*>(a.y + size_t(a.slot_pos[slot]) * a.H + h);
+        if (a.slot_out) *reinterpret_cast<float4*>(a.slot_out + size_t(slot) * a.H + h) = s;
+    }
+    acc.x = __fadd_rn(acc.x, s.x);
+    acc.y = __fadd_rn(acc.y, s.y);
+    acc.z = __fadd_rn(acc.z, s.z);
+    acc.w = __fadd_rn(acc.w, s.w);
+    *reinterpret_cast<float4*>(a.out + size_t(t) * a.H + h) = acc;
+}
+
+hf_status launch_combine(const CombineArgs& a, cudaStream_t st) {
+    const size_t n = size_t(a.T) * (a.H >> 2);
+    if (n == 0) return HF_OK;
+    k_combine<<<unsigned((n + 255) / 256), 256, 0, st>>>(a);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+// ============================================================ gemv_bf16_f32 twin
+// compute/cpu_kernels.cpp:43-94: y[i] = alpha * dot(A[i,:], x) + beta * y[i].
+__global__ void __launch_bounds__(256) k_gemv_plain(const uint16_t* A, const float* x, float* y,
+                                                    int M, int K, float alpha, float beta,
+                                                    int vec) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + warp;
+    if (row >= M) return;
+    const uint16_t* ar = A + size_t(row) * K;
+    float acc = 0.0f;
+    if (vec) {
+        for (int c = lane; c < (K >> 3); c += 32) {
+            float wf[8];
+            unpack8(ld_stream_u4(ar + size_t(c) * 8), wf);
+            const float4 x0 = __ldg(reinterpret_cast<const float4*>(x + c * 8));
+            const float4 x1 = __ldg(reinterpret_cast<const float4*>(x + c * 8) + 1);
+            acc = fmaf(wf[0], x0.x, acc); acc = fmaf(wf[1], x0.y, acc);
+            acc = fmaf(wf[2], x0.z, acc); acc = fmaf(wf[3], x0.w, acc);
+            acc = fmaf(wf[4], x1.x, acc); acc = fmaf(wf[5], x1.y, acc);
+            acc = fmaf(wf[6], x1.z, acc); acc = fmaf(wf[7], x1.w, acc);
+        }
+    } else {
+        for (int j = lane; j < K; j += 32) acc = fmaf(bf16_to_f32(ar[j]), __ldg(x + j), acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) y[row] = __fadd_rn(__fmul_rn(alpha, acc), __fmul_rn(beta, y[row]));
+}
+
+hf_status launch_gemv_plain(const uint16_t* A, const float* x, float* y, int M, int K,
+                            float alpha, float beta, cudaStream_t st) {
+    if (M == 0) return HF_OK;
+    const int vec = (K % 8 == 0) && (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
+                    (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+    k_gemv_plain<<<(M + 7) / 8, 256, 0, st>>>(A, x, y, M, K, alpha, beta, vec);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+}  // namespace hf

@@ -1,0 +1,214 @@
+// hf_internal.cuh -- shared device helpers and host plumbing of libhf_moe.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "hf_moe.h"
+
+namespace hf {
+
+// ------------------------------------------------------------------ errors
+void set_error(const std::string& msg);
+hf_status fail(hf_status s, const std::string& msg);
+hf_status cuda_fail(cudaError_t e, const char* what);
+
+#define HF_CUDA(call)                                                        \
+    do {                                                                     \
+        cudaError_t _e = (call);                                             \
+        if (_e != cudaSuccess) return ::hf::cuda_fail(_e, #call);            \
+    } while (0)
+
+#define HF_TRY(call)                                                         \
+    do {                                                                     \
+        hf_status _s = (call);                                               \
+        if (_s != HF_OK) return _s;                                          \
+    } while (0)
+
+inline cudaStream_t as_cuda(hf_stream s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ------------------------------------------------------------------ limits
+constexpr int kMaxTopK = 8;        // TopKResult holds 8 (compute/moe_router.h:12-16)
+constexpr int kMaxExperts = 1024;  // top-k kernel keeps E/32 scores per lane
+constexpr int kSmallRouteT = 128;  // single-CTA routing up to this many tokens
+constexpr int kGemvTE = 4;         // tokens per grouped-GEMV chunk
+constexpr int kGemv1Rows = 16;     // gate/up rows per GEMV1 unit (8 warps x 2)
+constexpr int kGemv2Rows = 32;     // down rows per GEMV2 unit (8 warps x 4)
+constexpr int kGemvDefaultMax = 16;// AUTO: segments <= this many tokens use the GEMV
+
+// Weights of one expert group (routed expert or the shared expert).
+struct GroupW {
+    const uint16_t* gate;  // [inter x H]
+    const uint16_t* up;    // [inter x H]
+    const uint16_t* down;  // [H x inter]
+    int inter;
+    int pad;
+};
+
+// Device plan of one forward, written by the routing kernels.
+// Offsets are in int32 words from the start of the plan buffer.
+struct PlanLayout {
+    int G;            // groups = E + 1 (shared last, count 0 when absent)
+    int counts;       // [G]
+    int offsets;      // [G+1] positions
+    int u1;           // [G+1] GEMV1 unit prefix
+    int u2;           // [G+1] GEMV2 unit prefix
+    int gemm_seg;     // [G+1] GEMM segment prefix (segments routed to the GEMM)
+    int stats;        // [4]: active experts, gemv segments, gemm segments, error word
+    int words;        // total
+    static PlanLayout make(int G) {
+        PlanLayout p;
+        p.G = G;
+        p.counts = 0;
+        p.offsets = p.counts + G;
+        p.u1 = p.offsets + G + 1;
+        p.u2 = p.u1 + G + 1;
+        p.gemm_seg = p.u2 + G + 1;
+        p.stats = p.gemm_seg + G + 1;
+        p.words = p.stats + 4;
+        return p;
+    }
+};
+
+// Everything the routing kernels need.
+struct RouteArgs {
+    const void* x;            // [T x H] bf16 or f32
+    int x_f32;
+    int T, H, E, k;           // k = min(top_k, E)
+    const uint16_t* router;   // [E x H]
+    const float* bias;        // [E] or null
+    float scale;
+    int norm;
+    float* logits;            // [T x E]
+    int32_t* ids;             // [T x k]
+    float* w;                 // [T x k]
+    float* margins;           // [T]
+    int32_t* plan;            // PlanLayout
+    PlanLayout pl;
+    int has_shared;
+    int shared_inter, inter;
+    int32_t* perm;            // [T*k + T]
+    int32_t* slot_pos;        // [T*k + T]
+    uint32_t* masks;          // [nb x E x 4] (multi-block path)
+    int32_t* blk_counts;      // [nb x E]
+    int path;                 // hf_path
+    int gemv_max;             // AUTO threshold
+};
+
+// ------------------------------------------------------------------ device helpers
+// Read-only 16-byte loads (weights and activations never change during a
+// kernel); not volatile, so the compiler may batch them for memory-level
+// parallelism.
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint4 ld_nc_u4(const void* p) {
+    uint4 r;
+    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+__device__ __forceinline__ float bf16_to_f32(uint16_t h) {
+    return __uint_as_float(uint32_t(h) << 16);
+}
+
+// BFloat16::fromF32 (compute/dtype_bf16.h:27-33): RNE without a NaN case.
+__device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u = __float_as_uint(f);
+    return uint16_t((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+// 8 consecutive elements of x as fp32 (bf16 widened exactly).
+__device__ __forceinline__ void unpack8(const uint4 v, float (&o)[8]) {
+    o[0] = bf16lo(v.x); o[1] = bf16hi(v.x);
+    o[2] = bf16lo(v.y); o[3] = bf16hi(v.y);
+    o[4] = bf16lo(v.z); o[5] = bf16hi(v.z);
+    o[6] = bf16lo(v.w); o[7] = bf16hi(v.w);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// SiLU-gated product of the reference (glm_forward.cpp:444-446), IEEE ops.
+__device__ __forceinline__ float swiglu(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+__device__ __forceinline__ int token_of_slot(int slot, int T, int k) {
+    return slot < T * k ? slot / k : slot - T * k;
+}
+
+// Largest g with prefix[g] <= u (prefix non-decreasing, prefix[0] = 0).
+__device__ __forceinline__ int find_group(const int32_t* prefix, int G, int u) {
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// ------------------------------------------------------------------ launchers
+int num_sms(int device);
+
+hf_status launch_router_logits(const RouteArgs& a, cudaStream_t st);
+// Top-k + permutation + plan; *launches receives the number of kernels.
+hf_status launch_route(const RouteArgs& a, cudaStream_t st, int* launches);
+hf_status launch_topk(const float* scores, int T, int E, const float* bias, int k, float scale,
+                      int norm, int32_t* idx, float* w, int apply_sigmoid, float* margins,
+                      cudaStream_t st);
+
+struct GemvArgs {
+    const GroupW* groups;   // [G] device
+    const int32_t* plan;
+    PlanLayout pl;
+    const int32_t* perm;
+    const void* x;          // [T x H]
+    int x_f32;
+    int T, H, k;
+    int inter_max;          // mid row stride
+    float* mid;             // [(T*k+T) x inter_max] fp32
+    float* y;               // [(T*k+T) x H] fp32
+    int grid1, grid2;
+};
+hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st);
+hf_status launch_gemv2(const GemvArgs& a, cudaStream_t st);
+// Persistent grid (SM count x resident blocks) of GEMV1 (first) or GEMV2.
+int gemv_grid(int device, bool first, bool xf32, int H, int inter_max);
+size_t gemv1_smem(int H, bool xf32);
+size_t gemv2_smem(int inter_max);
+
+// Device generator (hf_synth.cu).
+hf_status synth_bf16(uint16_t* dst, uint64_t n, uint64_t key, float scale, cudaStream_t st);
+hf_status synth_f32u(float* dst, uint64_t n, uint64_t key, float lo, float hi, cudaStream_t st);
+uint64_t synth_key(uint64_t seed, uint32_t layer, uint32_t kind, uint32_t expert);
+float synth_normal_scale(double sigma);
+
+struct CombineArgs {
+    const float* y;        // [(T*k+T) x H]
+    const int32_t* slot_pos;
+    const float* w;        // [T x k]
+    int T, H, k, has_shared;
+    float* out;            // [T x H]
+    float* slot_out;       // optional [(T*k+T) x H] by slot id
+};
+hf_status launch_combine(const CombineArgs& a, cudaStream_t st);
+
+hf_status launch_gemv_plain(const uint16_t* A, const float* x, float* y, int M, int K,
+                            float alpha, float beta, cudaStream_t st);
+
+}  // namespace hf

@@ -1,0 +1,648 @@
+// hf_moe.cu -- C ABI of the MoE layer: context, weights, forward orchestration.
+//
+// Host side of the drop-in for GLMForward::moeLayer (model/glm_forward.cpp:
+// 509-661) and the sm_86 expert cache it offloaded to (compute/cuda_backend.cpp:
+// 196-492). Differences by design: all weights of a layer stay resident in HBM
+// (no per-token staging over PCIe), a forward covers T tokens at once, every
+// error is returned (no CPU fallback), and kernels run asynchronously on the
+// caller's stream.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "hf_internal.cuh"
+#include "hf_synth.h"
+
+namespace hf {
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+hf_status fail(hf_status s, const std::string& msg) {
+    g_last_error = msg;
+    return s;
+}
+
+hf_status cuda_fail(cudaError_t e, const char* what) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+    return e == cudaErrorMemoryAllocation ? HF_ERR_OOM : HF_ERR_CUDA;
+}
+
+int num_sms(int device) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+        n = 148;
+    return n;
+}
+
+// Makes the context's device current for one API call and restores the
+// caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+struct LayerBuf {
+    uint16_t* router = nullptr;  // [E x H]
+    float* bias = nullptr;       // [E]
+    bool has_bias = false;
+    uint16_t* experts = nullptr; // [E_local][gate|up|down]
+    uint16_t* shared = nullptr;  // [gate|up|down] of the shared expert
+    GroupW* groups = nullptr;    // [G] device table
+    bool loaded = false;
+};
+
+template <typename T>
+static hf_status dalloc(T** p, size_t count) {
+    *p = nullptr;
+    if (count == 0) return HF_OK;
+    HF_CUDA(cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T)));
+    return HF_OK;
+}
+
+}  // namespace hf
+
+struct hf_moe_ctx {
+    hf_moe_config cfg{};
+    int H = 0, E = 0, K = 0, k = 0, I = 0, Is = 0;
+    int E_local = 0, e_begin = 0, G = 0, inter_max = 0;
+    size_t expert_elems = 0;
+    std::vector<hf::LayerBuf> layers;
+    hf::PlanLayout pl{};
+    int T_max = 0;
+    // scratch
+    float* logits = nullptr;
+    int32_t* ids = nullptr;
+    float* w = nullptr;
+    float* margins = nullptr;
+    int32_t* plan = nullptr;
+    int32_t* perm = nullptr;
+    int32_t* slot_pos = nullptr;
+    uint32_t* masks = nullptr;
+    int32_t* blk_counts = nullptr;
+    float* mid = nullptr;
+    float* y = nullptr;
+    void* x_dev = nullptr;   // host-buffer API staging [T_max x H] fp32-sized
+    float* out_dev = nullptr;
+    int grid1_bf16 = 0, grid1_f32 = 0, grid2 = 0;
+    cudaStream_t last_stream = nullptr;
+    // profiling: event pairs per phase, launch counters
+    bool profiling = false;
+    std::vector<cudaEvent_t> ev_pool;
+    struct Mark { int phase; cudaEvent_t a, b; };
+    std::vector<Mark> marks;
+    long long launches[HF_MOE_PHASES] = {0, 0, 0, 0, 0, 0, 0};
+};
+
+namespace {
+
+// Brackets one phase of a forward with events (when profiling) and counts its
+// kernel launches.
+struct PhaseTimer {
+    hf_moe_ctx* c;
+    cudaStream_t st;
+    int phase;
+    cudaEvent_t a = nullptr;
+    PhaseTimer(hf_moe_ctx* ctx, cudaStream_t s, int p) : c(ctx), st(s), phase(p) {
+        if (c->profiling) {
+            a = take();
+            if (a) cudaEventRecord(a, st);
+        }
+    }
+    cudaEvent_t take() {
+        cudaEvent_t e = nullptr;
+        if (!c->ev_pool.empty()) {
+            e = c->ev_pool.back();
+            c->ev_pool.pop_back();
+        } else if (cudaEventCreate(&e) != cudaSuccess) {
+            e = nullptr;
+        }
+        return e;
+    }
+    void done(int nlaunch) {
+        c->launches[phase] += nlaunch;
+        if (!a) return;
+        cudaEvent_t b = take();
+        if (!b) return;
+        cudaEventRecord(b, st);
+        c->marks.push_back({phase, a, b});
+        a = nullptr;
+    }
+    ~PhaseTimer() {
+        if (a) c->ev_pool.push_back(a);
+    }
+};
+
+}  // namespace
+
+using namespace hf;
+
+extern "C" {
+
+int hf_abi_version(void) { return HF_MOE_ABI_VERSION; }
+
+const char* hf_status_string(hf_status s) {
+    switch (s) {
+        case HF_OK: return "HF_OK";
+        case HF_ERR_ARG: return "HF_ERR_ARG";
+        case HF_ERR_CUDA: return "HF_ERR_CUDA";
+        case HF_ERR_NCCL: return "HF_ERR_NCCL";
+        case HF_ERR_TIMEOUT: return "HF_ERR_TIMEOUT";
+        case HF_ERR_OOM: return "HF_ERR_OOM";
+        case HF_ERR_STATE: return "HF_ERR_STATE";
+        case HF_ERR_UNSUPPORTED: return "HF_ERR_UNSUPPORTED";
+    }
+    return "HF_ERR_UNKNOWN";
+}
+
+const char* hf_last_error(void) { return g_last_error.c_str(); }
+
+static void free_ctx(hf_moe_ctx* c) {
+    for (auto& L : c->layers) {
+        cudaFree(L.router);
+        cudaFree(L.bias);
+        cudaFree(L.experts);
+        cudaFree(L.shared);
+        cudaFree(L.groups);
+    }
+    for (auto& m : c->marks) {
+        cudaEventDestroy(m.a);
+        cudaEventDestroy(m.b);
+    }
+    for (auto e : c->ev_pool) cudaEventDestroy(e);
+    void* bufs[] = {c->logits, c->ids, c->w, c->margins, c->plan, c->perm, c->slot_pos,
+                    c->masks, c->blk_counts, c->mid, c->y, c->x_dev, c->out_dev};
+    for (void* p : bufs) cudaFree(p);
+    delete c;
+}
+
+hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
+    if (!out || !cfg) return fail(HF_ERR_ARG, "hf_moe_create: null argument");
+    *out = nullptr;
+    const hf_moe_config& c = *cfg;
+    if (c.hidden_size <= 0 || c.hidden_size % 8)
+        return fail(HF_ERR_ARG, "hidden_size must be a positive multiple of 8");
+    if (c.num_experts <= 0 || c.num_experts > kMaxExperts)
+        return fail(HF_ERR_ARG, "num_experts must be in 1..1024");
+    if (c.num_experts_per_tok <= 0 || c.num_experts_per_tok > kMaxTopK)
+        return fail(HF_ERR_ARG, "num_experts_per_tok must be in 1..8 (TopKResult holds 8)");
+    if (c.moe_intermediate_size <= 0 || c.moe_intermediate_size % 8)
+        return fail(HF_ERR_ARG, "moe_intermediate_size must be a positive multiple of 8");
+    if (c.shared_intermediate_size < 0 || c.shared_intermediate_size % 8)
+        return fail(HF_ERR_ARG, "shared_intermediate_size must be a non-negative multiple of 8");
+    if (c.num_layers <= 0) return fail(HF_ERR_ARG, "num_layers must be positive");
+    if (c.max_tokens < 0) return fail(HF_ERR_ARG, "max_tokens must be >= 0");
+    if (c.path < HF_PATH_AUTO || c.path > HF_PATH_GEMM) return fail(HF_ERR_ARG, "bad path");
+    const int world = c.ep_world <= 0 ? 1 : c.ep_world;
+    if (world != 1)
+        return fail(HF_ERR_UNSUPPORTED, "expert parallelism is not available in this build");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return fail(HF_ERR_UNSUPPORTED, "no CUDA device");
+    if (c.device < 0 || c.device >= ndev) return fail(HF_ERR_ARG, "device ordinal out of range");
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, c.device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, c.device);
+    if (major != 10 || minor != 0)
+        return fail(HF_ERR_UNSUPPORTED, "libhf_moe is built for sm_100a (B200) only");
+    DeviceGuard dg(c.device);
+    if (!dg.ok) return fail(HF_ERR_CUDA, "cudaSetDevice failed");
+
+    auto* x = new hf_moe_ctx();
+    x->cfg = c;
+    x->cfg.ep_world = world;
+    x->H = c.hidden_size;
+    x->E = c.num_experts;
+    x->K = c.num_experts_per_tok;
+    x->k = std::min(x->K, x->E);
+    x->I = c.moe_intermediate_size;
+    x->Is = c.shared_intermediate_size;
+    x->E_local = x->E / world;
+    x->e_begin = 0;
+    x->G = x->E + 1;
+    x->inter_max = std::max(x->I, x->Is);
+    x->expert_elems = size_t(3) * x->I * x->H;
+    x->pl = PlanLayout::make(x->G);
+    x->T_max = c.max_tokens;
+    if (x->cfg.gemv_max_tokens <= 0) x->cfg.gemv_max_tokens = kGemvDefaultMax;
+    if (gemv1_smem(x->H, true) > 227 * 1024 || gemv2_smem(x->inter_max) > 227 * 1024) {
+        free_ctx(x);
+        return fail(HF_ERR_ARG, "hidden/intermediate size too large for the GEMV staging");
+    }
+    x->layers.resize(c.num_layers);
+    const size_t T = size_t(std::max(1, c.max_tokens));
+    const size_t slots = T * x->k + T;
+    const size_t nb = (T + kSmallRouteT - 1) / kSmallRouteT;
+    hf_status s = HF_OK;
+    auto A = [&](hf_status r) { if (s == HF_OK) s = r; };
+    A(dalloc(&x->logits, T * x->E));
+    A(dalloc(&x->ids, T * x->k));
+    A(dalloc(&x->w, T * x->k));
+    A(dalloc(&x->margins, T));
+    A(dalloc(&x->plan, size_t(x->pl.words)));
+    A(dalloc(&x->perm, slots));
+    A(dalloc(&x->slot_pos, slots));
+    A(dalloc(&x->masks, nb * 4 * x->E));
+    A(dalloc(&x->blk_counts, nb * x->E));
+    A(dalloc(&x->mid, slots * x->inter_max));
+    A(dalloc(&x->y, slots * x->H));
+    A(dalloc(reinterpret_cast<float**>(&x->x_dev), T * x->H));
+    A(dalloc(&x->out_dev, T * x->H));
+    if (s != HF_OK) {
+        std::string m = g_last_error;
+        free_ctx(x);
+        return fail(s, "hf_moe_create scratch: " + m);
+    }
+    x->grid1_bf16 = gemv_grid(c.device, true, false, x->H, x->inter_max);
+    x->grid1_f32 = gemv_grid(c.device, true, true, x->H, x->inter_max);
+    x->grid2 = gemv_grid(c.device, false, false, x->H, x->inter_max);
+    *out = x;
+    return HF_OK;
+}
+
+hf_status hf_moe_destroy(hf_moe_ctx* ctx) {
+    if (!ctx) return HF_OK;
+    DeviceGuard dg(ctx->cfg.device);
+    cudaDeviceSynchronize();
+    free_ctx(ctx);
+    return HF_OK;
+}
+
+static hf_status layer_alloc(hf_moe_ctx* c, int layer) {
+    LayerBuf& L = c->layers[layer];
+    if (L.router) return HF_OK;
+    HF_TRY(dalloc(&L.router, size_t(c->E) * c->H));
+    HF_TRY(dalloc(&L.bias, size_t(c->E)));
+    HF_CUDA(cudaMemset(L.bias, 0, sizeof(float) * c->E));
+    HF_TRY(dalloc(&L.experts, size_t(c->E_local) * c->expert_elems));
+    if (c->Is > 0) HF_TRY(dalloc(&L.shared, size_t(3) * c->Is * c->H));
+    HF_TRY(dalloc(&L.groups, size_t(c->G)));
+    std::vector<GroupW> tab(c->G);
+    for (int g = 0; g < c->G; ++g) {
+        GroupW& w = tab[g];
+        if (g < c->E_local) {
+            const uint16_t* b = L.experts + size_t(g) * c->expert_elems;
+            w.gate = b;
+            w.up = b + size_t(c->I) * c->H;
+            w.down = b + size_t(2) * c->I * c->H;
+            w.inter = c->I;
+        } else if (g == c->G - 1 && c->Is > 0) {
+            w.gate = L.shared;
+            w.up = L.shared + size_t(c->Is) * c->H;
+            w.down = L.shared + size_t(2) * c->Is * c->H;
+            w.inter = c->Is;
+        } else {
+            w.gate = w.up = w.down = nullptr;
+            w.inter = 0;
+        }
+        w.pad = 0;
+    }
+    HF_CUDA(cudaMemcpy(L.groups, tab.data(), sizeof(GroupW) * c->G, cudaMemcpyHostToDevice));
+    return HF_OK;
+}
+
+static hf_status check_layer(hf_moe_ctx* c, int layer, const char* fn) {
+    if (!c) return fail(HF_ERR_ARG, std::string(fn) + ": null context");
+    if (layer < 0 || layer >= (int)c->layers.size())
+        return fail(HF_ERR_ARG, std::string(fn) + ": layer out of range");
+    return HF_OK;
+}
+
+static cudaMemcpyKind kind_of(hf_mem_kind k) {
+    return k == HF_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+}
+
+hf_status hf_moe_set_router(hf_moe_ctx* ctx, int layer, const uint16_t* router_bf16,
+                            const float* bias, hf_mem_kind kind) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_set_router"));
+    if (!router_bf16) return fail(HF_ERR_ARG, "hf_moe_set_router: null router weight");
+    DeviceGuard dg(ctx->cfg.device);
+    HF_TRY(layer_alloc(ctx, layer));
+    LayerBuf& L = ctx->layers[layer];
+    HF_CUDA(cudaMemcpy(L.router, router_bf16, sizeof(uint16_t) * ctx->E * ctx->H, kind_of(kind)));
+    if (bias) HF_CUDA(cudaMemcpy(L.bias, bias, sizeof(float) * ctx->E, kind_of(kind)));
+    else HF_CUDA(cudaMemset(L.bias, 0, sizeof(float) * ctx->E));
+    L.has_bias = bias != nullptr;
+    L.loaded = true;
+    return HF_OK;
+}
+
+hf_status hf_moe_set_expert(hf_moe_ctx* ctx, int layer, int eid, const uint16_t* gud,
+                            hf_mem_kind kind) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_set_expert"));
+    if (!gud) return fail(HF_ERR_ARG, "hf_moe_set_expert: null weights");
+    if (eid < ctx->e_begin || eid >= ctx->e_begin + ctx->E_local)
+        return fail(HF_ERR_ARG, "hf_moe_set_expert: expert id not owned by this context");
+    DeviceGuard dg(ctx->cfg.device);
+    HF_TRY(layer_alloc(ctx, layer));
+    LayerBuf& L = ctx->layers[layer];
+    HF_CUDA(cudaMemcpy(L.experts + size_t(eid - ctx->e_begin) * ctx->expert_elems, gud,
+                       sizeof(uint16_t) * ctx->expert_elems, kind_of(kind)));
+    return HF_OK;
+}
+
+hf_status hf_moe_set_shared(hf_moe_ctx* ctx, int layer, const uint16_t* gate, const uint16_t* up,
+                            const uint16_t* down, hf_mem_kind kind) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_set_shared"));
+    if (ctx->Is == 0) return fail(HF_ERR_STATE, "hf_moe_set_shared: config has no shared expert");
+    if (!gate || !up || !down) return fail(HF_ERR_ARG, "hf_moe_set_shared: null projection");
+    DeviceGuard dg(ctx->cfg.device);
+    HF_TRY(layer_alloc(ctx, layer));
+    LayerBuf& L = ctx->layers[layer];
+    const size_t n = size_t(ctx->Is) * ctx->H;
+    HF_CUDA(cudaMemcpy(L.shared, gate, sizeof(uint16_t) * n, kind_of(kind)));
+    HF_CUDA(cudaMemcpy(L.shared + n, up, sizeof(uint16_t) * n, kind_of(kind)));
+    HF_CUDA(cudaMemcpy(L.shared + 2 * n, down, sizeof(uint16_t) * n, kind_of(kind)));
+    return HF_OK;
+}
+
+hf_status hf_moe_expert_device_ptr(hf_moe_ctx* ctx, int layer, int eid, uint16_t** dev_ptr) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_expert_device_ptr"));
+    if (!dev_ptr) return fail(HF_ERR_ARG, "hf_moe_expert_device_ptr: null output");
+    DeviceGuard dg(ctx->cfg.device);
+    HF_TRY(layer_alloc(ctx, layer));
+    LayerBuf& L = ctx->layers[layer];
+    if (eid == ctx->E) {
+        if (!L.shared) return fail(HF_ERR_STATE, "no shared expert in this config");
+        *dev_ptr = L.shared;
+        return HF_OK;
+    }
+    if (eid < ctx->e_begin || eid >= ctx->e_begin + ctx->E_local)
+        return fail(HF_ERR_ARG, "hf_moe_expert_device_ptr: expert id not owned by this context");
+    *dev_ptr = L.experts + size_t(eid - ctx->e_begin) * ctx->expert_elems;
+    return HF_OK;
+}
+
+hf_status hf_moe_router_device_ptr(hf_moe_ctx* ctx, int layer, uint16_t** router, float** bias) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_router_device_ptr"));
+    DeviceGuard dg(ctx->cfg.device);
+    HF_TRY(layer_alloc(ctx, layer));
+    LayerBuf& L = ctx->layers[layer];
+    if (router) *router = L.router;
+    if (bias) *bias = L.bias;
+    L.has_bias = true;
+    return HF_OK;
+}
+
+hf_status hf_moe_mark_loaded(hf_moe_ctx* ctx, int layer) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_mark_loaded"));
+    if (!ctx->layers[layer].router) return fail(HF_ERR_STATE, "layer has no weights");
+    ctx->layers[layer].loaded = true;
+    return HF_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype xd, int T,
+                             float* out, const hf_moe_routing* r, cudaStream_t st, bool route_only) {
+    LayerBuf& L = c->layers[layer];
+    if (!L.loaded) return fail(HF_ERR_STATE, "layer weights not set (hf_moe_set_router first)");
+    if (T < 0 || T > c->T_max) return fail(HF_ERR_ARG, "T out of range (0..max_tokens)");
+    if (xd != HF_BF16 && xd != HF_F32) return fail(HF_ERR_ARG, "x_dtype must be HF_BF16 or HF_F32");
+    if (T > 0 && (!x || !aligned16(x))) return fail(HF_ERR_ARG, "x must be a 16-byte aligned device pointer");
+    if (!route_only && T > 0 && (!out || !aligned16(out)))
+        return fail(HF_ERR_ARG, "out must be a 16-byte aligned device pointer");
+    c->last_stream = st;
+    if (T == 0) return HF_OK;
+    const int k = c->k;
+    RouteArgs ra{};
+    ra.x = x;
+    ra.x_f32 = xd == HF_F32;
+    ra.T = T;
+    ra.H = c->H;
+    ra.E = c->E;
+    ra.k = k;
+    ra.router = L.router;
+    ra.bias = L.has_bias ? L.bias : nullptr;
+    ra.scale = c->cfg.routed_scaling_factor;
+    ra.norm = c->cfg.norm_topk_prob;
+    ra.logits = c->logits;
+    ra.ids = c->ids;
+    ra.w = c->w;
+    ra.margins = c->margins;
+    ra.plan = c->plan;
+    ra.pl = c->pl;
+    ra.has_shared = c->Is > 0;
+    ra.shared_inter = c->Is;
+    ra.inter = c->I;
+    ra.perm = c->perm;
+    ra.slot_pos = c->slot_pos;
+    ra.masks = c->masks;
+    ra.blk_counts = c->blk_counts;
+    ra.path = HF_PATH_GEMV;  // the tcgen05 grouped GEMM is not built yet
+    ra.gemv_max = c->cfg.gemv_max_tokens;
+    {
+        PhaseTimer p0(c, st, 0);
+        HF_TRY(launch_router_logits(ra, st));
+        p0.done(1);
+    }
+    {
+        PhaseTimer p1(c, st, 1);
+        int n = 0;
+        HF_TRY(launch_route(ra, st, &n));
+        p1.done(n);
+    }
+    const size_t nslots = size_t(T) * k + (c->Is > 0 ? T : 0);
+    if (!route_only) {
+        GemvArgs ga{};
+        ga.groups = L.groups;
+        ga.plan = c->plan;
+        ga.pl = c->pl;
+        ga.perm = c->perm;
+        ga.x = x;
+        ga.x_f32 = xd == HF_F32;
+        ga.T = T;
+        ga.H = c->H;
+        ga.k = k;
+        ga.inter_max = c->inter_max;
+        ga.mid = c->mid;
+        ga.y = c->y;
+        ga.grid1 = xd == HF_F32 ? c->grid1_f32 : c->grid1_bf16;
+        ga.grid2 = c->grid2;
+        {
+            PhaseTimer p2(c, st, 2);
+            HF_TRY(launch_gemv1(ga, st));
+            p2.done(1);
+        }
+        {
+            PhaseTimer p3(c, st, 3);
+            HF_TRY(launch_gemv2(ga, st));
+            p3.done(1);
+        }
+        CombineArgs ca{};
+        ca.y = c->y;
+        ca.slot_pos = c->slot_pos;
+        ca.w = c->w;
+        ca.T = T;
+        ca.H = c->H;
+        ca.k = k;
+        ca.has_shared = c->Is > 0;
+        ca.out = out;
+        ca.slot_out = r ? r->slot_out : nullptr;
+        PhaseTimer p6(c, st, 6);
+        HF_TRY(launch_combine(ca, st));
+        p6.done(1);
+    }
+    if (r) {
+        if (r->topk_ids) HF_CUDA(cudaMemcpyAsync(r->topk_ids, c->ids, sizeof(int32_t) * T * k, cudaMemcpyDeviceToDevice, st));
+        if (r->topk_weights) HF_CUDA(cudaMemcpyAsync(r->topk_weights, c->w, sizeof(float) * T * k, cudaMemcpyDeviceToDevice, st));
+        if (r->margins) HF_CUDA(cudaMemcpyAsync(r->margins, c->margins, sizeof(float) * T, cudaMemcpyDeviceToDevice, st));
+        if (r->counts) HF_CUDA(cudaMemcpyAsync(r->counts, c->plan + c->pl.counts, sizeof(int32_t) * c->G, cudaMemcpyDeviceToDevice, st));
+        if (r->offsets) HF_CUDA(cudaMemcpyAsync(r->offsets, c->plan + c->pl.offsets, sizeof(int32_t) * (c->G + 1), cudaMemcpyDeviceToDevice, st));
+        if (r->perm) HF_CUDA(cudaMemcpyAsync(r->perm, c->perm, sizeof(int32_t) * nslots, cudaMemcpyDeviceToDevice, st));
+    }
+    return HF_OK;
+}
+
+hf_status hf_moe_forward(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_dtype, int T,
+                         float* out, const hf_moe_routing* routing, hf_stream stream) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_forward"));
+    DeviceGuard dg(ctx->cfg.device);
+    return run_forward(ctx, layer, x, x_dtype, T, out, routing, as_cuda(stream), false);
+}
+
+hf_status hf_moe_route(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_dtype, int T,
+                       const hf_moe_routing* routing, hf_stream stream) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_route"));
+    DeviceGuard dg(ctx->cfg.device);
+    return run_forward(ctx, layer, x, x_dtype, T, nullptr, routing, as_cuda(stream), true);
+}
+
+hf_status hf_moe_forward_host(hf_moe_ctx* ctx, int layer, const void* x_host, hf_dtype x_dtype,
+                              int T, float* out_host, hf_stream stream) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_forward_host"));
+    if (T < 0 || T > ctx->T_max) return fail(HF_ERR_ARG, "T out of range (0..max_tokens)");
+    if (T > 0 && (!x_host || !out_host)) return fail(HF_ERR_ARG, "null host buffer");
+    DeviceGuard dg(ctx->cfg.device);
+    cudaStream_t st = as_cuda(stream);
+    const size_t xb = size_t(T) * ctx->H * (x_dtype == HF_F32 ? 4 : 2);
+    if (T > 0) HF_CUDA(cudaMemcpyAsync(ctx->x_dev, x_host, xb, cudaMemcpyHostToDevice, st));
+    HF_TRY(run_forward(ctx, layer, ctx->x_dev, x_dtype, T, ctx->out_dev, nullptr, st, false));
+    if (T > 0)
+        HF_CUDA(cudaMemcpyAsync(out_host, ctx->out_dev, sizeof(float) * T * ctx->H,
+                                cudaMemcpyDeviceToHost, st));
+    HF_CUDA(cudaStreamSynchronize(st));
+    return HF_OK;
+}
+
+hf_status hf_moe_layer(hf_moe_ctx* ctx, int layer, const float* input, float* output) {
+    return hf_moe_forward_host(ctx, layer, input, HF_F32, 1, output, nullptr);
+}
+
+hf_status hf_moe_last_stats(hf_moe_ctx* ctx, int* active, int* gemv_segments, int* gemm_segments) {
+    if (!ctx) return fail(HF_ERR_ARG, "hf_moe_last_stats: null context");
+    DeviceGuard dg(ctx->cfg.device);
+    int st[4] = {0, 0, 0, 0};
+    HF_CUDA(cudaStreamSynchronize(ctx->last_stream));
+    HF_CUDA(cudaMemcpy(st, ctx->plan + ctx->pl.stats, sizeof(st), cudaMemcpyDeviceToHost));
+    if (active) *active = st[0];
+    if (gemv_segments) *gemv_segments = st[1];
+    if (gemm_segments) *gemm_segments = st[2];
+    return HF_OK;
+}
+
+hf_status hf_moe_profile(hf_moe_ctx* ctx, int enable) {
+    if (!ctx) return fail(HF_ERR_ARG, "hf_moe_profile: null context");
+    ctx->profiling = enable != 0;
+    return HF_OK;
+}
+
+hf_status hf_moe_profile_read(hf_moe_ctx* ctx, double* phase_ms, long long* launches) {
+    if (!ctx) return fail(HF_ERR_ARG, "hf_moe_profile_read: null context");
+    DeviceGuard dg(ctx->cfg.device);
+    double ms[HF_MOE_PHASES] = {0, 0, 0, 0, 0, 0, 0};
+    hf_status s = HF_OK;
+    for (auto& m : ctx->marks) {
+        float t = 0.f;
+        cudaError_t e = cudaEventSynchronize(m.b);
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&t, m.a, m.b);
+        if (e != cudaSuccess && s == HF_OK) s = cuda_fail(e, "cudaEventElapsedTime");
+        ms[m.phase] += t;
+        ctx->ev_pool.push_back(m.a);
+        ctx->ev_pool.push_back(m.b);
+    }
+    ctx->marks.clear();
+    for (int i = 0; i < HF_MOE_PHASES; ++i) {
+        if (phase_ms) phase_ms[i] = ms[i];
+        if (launches) launches[i] = ctx->launches[i];
+        ctx->launches[i] = 0;
+    }
+    return s;
+}
+
+hf_status hf_gemv_bf16_f32(const uint16_t* A, const float* x, float* y, int M, int K, float alpha,
+                           float beta, hf_stream stream) {
+    if (M < 0 || K < 0) return fail(HF_ERR_ARG, "hf_gemv_bf16_f32: negative size");
+    if (M > 0 && (!y || (K > 0 && (!A || !x)))) return fail(HF_ERR_ARG, "hf_gemv_bf16_f32: null pointer");
+    return launch_gemv_plain(A, x, y, M, K, alpha, beta, as_cuda(stream));
+}
+
+hf_status hf_topk_scores(const float* scores, int T, int E, const float* bias, int k, float scale,
+                         int norm, int32_t* idx, float* weights, hf_stream stream) {
+    if (T < 0 || E <= 0 || E > kMaxExperts || k <= 0 || k > kMaxTopK)
+        return fail(HF_ERR_ARG, "hf_topk_scores: need T >= 0, 1 <= E <= 1024, 1 <= k <= 8");
+    if (T > 0 && (!scores || !idx || !weights)) return fail(HF_ERR_ARG, "hf_topk_scores: null pointer");
+    return launch_topk(scores, T, E, bias, std::min(k, E), scale, norm, idx, weights, 0, nullptr,
+                       as_cuda(stream));
+}
+
+size_t hf_dense_mlp_workspace_size(int T, int H, int I) {
+    (void)T; (void)H; (void)I;
+    return 0;
+}
+
+hf_status hf_dense_mlp_forward(const uint16_t*, const uint16_t*, const uint16_t*, const void*,
+                               hf_dtype, int, int, int, float*, void*, size_t, hf_stream) {
+    return fail(HF_ERR_UNSUPPORTED, "hf_dense_mlp_forward is not available in this build");
+}
+
+hf_status hf_moe_synth_layer(hf_moe_ctx* ctx, int layer, uint64_t seed, uint32_t gen_layer,
+                             const float* bias_override, hf_stream stream) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_synth_layer"));
+    DeviceGuard dg(ctx->cfg.device);
+    HF_TRY(layer_alloc(ctx, layer));
+    LayerBuf& L = ctx->layers[layer];
+    cudaStream_t st = as_cuda(stream);
+    const float sc = synth_normal_scale(0.02);
+    HF_TRY(synth_bf16(L.router, size_t(ctx->E) * ctx->H,
+                      synth_key(seed, gen_layer, HF_SYNTH_ROUTER, 0), sc, st));
+    if (bias_override)
+        HF_CUDA(cudaMemcpyAsync(L.bias, bias_override, sizeof(float) * ctx->E,
+                                cudaMemcpyHostToDevice, st));
+    else
+        HF_TRY(synth_f32u(L.bias, size_t(ctx->E), synth_key(seed, gen_layer, HF_SYNTH_BIAS, 0),
+                          -0.1f, 0.1f, st));
+    L.has_bias = true;
+    const size_t n = size_t(ctx->I) * ctx->H;
+    for (int e = 0; e < ctx->E_local; ++e) {
+        uint16_t* b = L.experts + size_t(e) * ctx->expert_elems;
+        const uint32_t eid = uint32_t(ctx->e_begin + e);
+        HF_TRY(synth_bf16(b, n, synth_key(seed, gen_layer, HF_SYNTH_GATE, eid), sc, st));
+        HF_TRY(synth_bf16(b + n, n, synth_key(seed, gen_layer, HF_SYNTH_UP, eid), sc, st));
+        HF_TRY(synth_bf16(b + 2 * n, n, synth_key(seed, gen_layer, HF_SYNTH_DOWN, eid), sc, st));
+    }
+    if (ctx->Is > 0) {
+        const size_t ns = size_t(ctx->Is) * ctx->H;
+        const uint32_t eid = uint32_t(ctx->E);
+        HF_TRY(synth_bf16(L.shared, ns, synth_key(seed, gen_layer, HF_SYNTH_GATE, eid), sc, st));
+        HF_TRY(synth_bf16(L.shared + ns, ns, synth_key(seed, gen_layer, HF_SYNTH_UP, eid), sc, st));
+        HF_TRY(synth_bf16(L.shared + 2 * ns, ns, synth_key(seed, gen_layer, HF_SYNTH_DOWN, eid), sc, st));
+    }
+    if (bias_override) HF_CUDA(cudaStreamSynchronize(st));  // host array may go away
+    L.loaded = true;
+    return HF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,544 @@
+// hf_route.cu -- router logits, noaux_tc top-k, canonical permutation, work plan.
+//
+// Reference: GLMForward::moeLayer router section (model/glm_forward.cpp:517-541)
+// and topKScores (compute/moe_router.h:29-57). The permutation into per-expert
+// segments and the work plan have no reference counterpart (the reference runs
+// one token at a time and loops its 8 experts, glm_forward.cpp:581).
+//
+// Permutation: positions are ordered (group asc, token asc). Each block of 128
+// tokens builds, per expert, a 128-bit mask of the tokens that picked it
+// (atomicOr: order-independent). A slot's rank inside its segment is the
+// popcount of the mask bits below its token, so the result is deterministic
+// without sorting.
+#include "hf_internal.cuh"
+
+#include <math.h>
+
+namespace hf {
+
+// ============================================================ router logits
+// Small T: block = 2 router rows x 4 K-slices (8 warps). Each lane keeps up to
+// 8 16-byte chunks of its row slice in registers and applies them to every
+// token, so the 3 MB router weight is read from HBM once.
+constexpr int kRouterRowsPerBlock = 2;
+constexpr int kRouterSlices = 4;
+constexpr int kRouterMaxT = 64;
+constexpr int kRouterRegChunks = 8;
+
+template <bool XF32>
+__device__ __forceinline__ void load_x8(const void* x, size_t elem, float (&o)[8]) {
+    if constexpr (XF32) {
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + elem);
+        float4 a = __ldg(p), b = __ldg(p + 1);
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+        o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+    } else {
+        uint4 v = ld_nc_u4(static_cast<const uint16_t*>(x) + elem);
+        unpack8(v, o);
+    }
+}
+
+template <bool XF32>
+__global__ void __launch_bounds__(256) k_router_gemv(RouteArgs a) {
+    __shared__ float part[kRouterSlices][kRouterRowsPerBlock][kRouterMaxT];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rloc = warp / kRouterSlices, slice = warp % kRouterSlices;
+    const int row = blockIdx.x * kRouterRowsPerBlock + rloc;
+    const int H = a.H, T = a.T;
+    float* P = &part[slice][rloc][0];
+    for (int t = lane; t < T; t += 32) P[t] = 0.0f;
+    __syncwarp();
+    if (row < a.E) {
+        const int nchunk = H / 8;
+        const int per = (nchunk + kRouterSlices - 1) / kRouterSlices;
+        const int c0 = slice * per, c1 = min(nchunk, c0 + per);
+        const uint16_t* wrow = a.router + size_t(row) * H;
+        for (int cb = c0; cb < c1; cb += 32 * kRouterRegChunks) {
+            uint4 wv[kRouterRegChunks];
+#pragma unroll
+            for (int j = 0; j < kRouterRegChunks; ++j) {
+                const int c = cb + lane + 32 * j;
+                wv[j] = (c < c1) ? ld_stream_u4(wrow + size_t(c) * 8) : make_uint4(0, 0, 0, 0);
+            }
+            for (int t = 0; t < T; ++t) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int j = 0; j < kRouterRegChunks; ++j) {
+                    const int c = cb + lane + 32 * j;
+                    if (c < c1) {
+                        float xf[8], wf[8];
+                        load_x8<XF32>(a.x, size_t(t) * H + size_t(c) * 8, xf);
+                        unpack8(wv[j], wf);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) acc = fmaf(wf[q], xf[q], acc);
+                    }
+                }
+                acc = warp_sum(acc);
+                if (lane == 0) P[t] += acc;
+            }
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kRouterRowsPerBlock * T; i += blockDim.x) {
+        const int rl = i / T, t = i % T;
+        const int r = blockIdx.x * kRouterRowsPerBlock + rl;
+        if (r < a.E) {
+            float s = part[0][rl][t];
+#pragma unroll
+            for (int q = 1; q < kRouterSlices; ++q) s += part[q][rl][t];
+            a.logits[size_t(t) * a.E + r] = s;
+        }
+    }
+}
+
+// Large T: 64 tokens x 64 experts per block, K in steps of 32, 4x4 per thread.
+template <bool XF32>
+__global__ void __launch_bounds__(256) k_router_tile(RouteArgs a) {
+    __shared__ __align__(16) float xs[32][68];
+    __shared__ __align__(16) float ws[32][68];
+    const int tid = threadIdx.x;
+    const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
+    const int ty = tid / 16, tx = tid % 16;
+    const int lr = tid / 4, lk = (tid % 4) * 8;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < a.H; k0 += 32) {
+        float xv[8], wv[8];
+        const int t = t0 + lr, e = e0 + lr, kk = k0 + lk;
+        if (t < a.T && kk < a.H) load_x8<XF32>(a.x, size_t(t) * a.H + kk, xv);
+        else
+#pragma unroll
+            for (int q = 0; q < 8; ++q) xv[q] = 0.0f;
+        if (e < a.E && kk < a.H) unpack8(ld_nc_u4(a.router + size_t(e) * a.H + kk), wv);
+        else
+#pragma unroll
+            for (int q = 0; q < 8; ++q) wv[q] = 0.0f;
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            xs[lk + q][lr] = xv[q];
+            ws[lk + q][lr] = wv[q];
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int q = 0; q < 32; ++q) {
+            const float4 xa = *reinterpret_cast<const float4*>(&xs[q][ty * 4]);
+            const float4 wb = *reinterpret_cast<const float4*>(&ws[q][tx * 4]);
+            const float xr[4] = {xa.x, xa.y, xa.z, xa.w};
+            const float wr[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xr[i], wr[j], acc[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + ty * 4 + i;
+        if (t >= a.T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = e0 + tx * 4 + j;
+            if (e < a.E) a.logits[size_t(t) * a.E + e] = acc[i][j];
+        }
+    }
+}
+
+// ============================================================ top-k (one warp per token)
+// compute/moe_router.h:29-57: rank by score + bias, descending; weights are
+// the unbiased scores, divided by their rank-order fp32 sum when normTopkProb
+// and that sum > 0, then multiplied by routedScalingFactor. Sigmoid as
+// glm_forward.cpp:522-524. Ties go to the lower expert id.
+template <int NPL>
+__device__ __forceinline__ void topk_warp(const float* row, int apply_sigmoid, const float* bias,
+                                          int E, int k, float scale, int norm, int lane,
+                                          int32_t* ids_out, float* w_out, float* margin_out,
+                                          int32_t* ids_smem) {
+    float v[NPL], s[NPL];
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+        const int e = j * 32 + lane;
+        if (e < E) {
+            const float l = row[e];
+            const float sc = apply_sigmoid ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-l))) : l;
+            s[j] = sc;
+            v[j] = __fadd_rn(sc, bias ? bias[e] : 0.0f);
+        } else {
+            s[j] = 0.0f;
+            v[j] = -INFINITY;
+        }
+    }
+    uint32_t taken = 0;
+    int sel_i[kMaxTopK];
+    float sel_s[kMaxTopK];
+    float kth = 0.0f, next = -INFINITY;
+    const int rounds = (k < E) ? k + 1 : k;
+#pragma unroll
+    for (int r = 0; r < kMaxTopK + 1; ++r) {
+        if (r >= rounds) break;
+        float bv = -INFINITY, bs = 0.0f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) {
+            const int e = j * 32 + lane;
+            if (!((taken >> j) & 1u) && e < E && (v[j] > bv || (v[j] == bv && e < bi))) {
+                bv = v[j];
+                bi = e;
+                bs = s[j];
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+                bs = os;
+            }
+        }
+        if (r < k) {
+            sel_i[r] = bi;
+            sel_s[r] = bs;
+            kth = bv;
+            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        } else {
+            next = bv;
+        }
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxTopK; ++i)
+        if (i < k) sum = __fadd_rn(sum, sel_s[i]);
+#pragma unroll
+    for (int i = 0; i < kMaxTopK; ++i) {
+        if (i < k && lane == i) {
+            float wi = sel_s[i];
+            if (norm && sum > 0.0f) wi = __fdiv_rn(wi, sum);
+            wi = __fmul_rn(wi, scale);
+            ids_out[i] = sel_i[i];
+            w_out[i] = wi;
+            if (ids_smem) ids_smem[i] = sel_i[i];
+        }
+    }
+    if (lane == 0 && margin_out) *margin_out = (k < E) ? __fsub_rn(kth, next) : INFINITY;
+}
+
+template <int NPL>
+__global__ void __launch_bounds__(256) k_topk(const float* scores, int T, int E, const float* bias,
+                                              int k, float scale, int norm, int apply_sigmoid,
+                                              int32_t* ids, float* w, float* margins) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    topk_warp<NPL>(scores + size_t(t) * E, apply_sigmoid, bias, E, k, scale, norm, lane,
+                   ids + size_t(t) * k, w + size_t(t) * k, margins ? margins + t : nullptr,
+                   nullptr);
+}
+
+// ============================================================ block helpers (1024 threads)
+// Exclusive scan of n <= 2048 ints in shared memory (in place), returns total.
+__device__ int block_scan_excl(int* data, int n, int* warp_tot) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int i0 = 2 * tid, i1 = 2 * tid + 1;
+    const int v0 = (i0 < n) ? data[i0] : 0;
+    const int v1 = (i1 < n) ? data[i1] : 0;
+    int s = v0 + v1;
+    int incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int wv = (lane < (int)(blockDim.x >> 5)) ? warp_tot[lane] : 0;
+        int wi = wv;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += y;
+        }
+        warp_tot[lane] = wi - wv;  // exclusive prefix of warps
+        if (lane == 31) warp_tot[32] = wi;
+    }
+    __syncthreads();
+    const int base = warp_tot[warp] + incl - s;
+    if (i0 < n) data[i0] = base;
+    if (i1 < n) data[i1] = base + v0;
+    __syncthreads();
+    const int total = warp_tot[32];
+    __syncthreads();
+    return total;
+}
+
+// From per-group counts (shared memory, s_cnt[G]) write counts, offsets, the
+// GEMV/GEMM work plan and the stats into the plan buffer. s_tmp: >= G+1 ints.
+__device__ void plan_from_counts(const RouteArgs& a, const int* s_cnt, int* s_tmp, int* warp_tot) {
+    const int G = a.pl.G;
+    int32_t* plan = a.plan;
+    const int H = a.H;
+    // offsets
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+        plan[a.pl.counts + g] = s_cnt[g];
+        s_tmp[g] = s_cnt[g];
+    }
+    __syncthreads();
+    int tot = block_scan_excl(s_tmp, G, warp_tot);
+    for (int g = threadIdx.x; g < G; g += blockDim.x) plan[a.pl.offsets + g] = s_tmp[g];
+    if (threadIdx.x == 0) plan[a.pl.offsets + G] = tot;
+    __syncthreads();
+    // GEMV1 units
+    for (int pass = 0; pass < 3; ++pass) {
+        for (int g = threadIdx.x; g < G; g += blockDim.x) {
+            const int c = s_cnt[g];
+            const int I = (g == G - 1) ? a.shared_inter : a.inter;
+            const bool gemv = c > 0 && I > 0 &&
+                              (a.path == HF_PATH_GEMV || (a.path == HF_PATH_AUTO && c <= a.gemv_max));
+            const int nch = (c + kGemvTE - 1) / kGemvTE;
+            int v = 0;
+            if (pass == 0) v = gemv ? nch * ((I + kGemv1Rows - 1) / kGemv1Rows) : 0;
+            if (pass == 1) v = gemv ? nch * ((H + kGemv2Rows - 1) / kGemv2Rows) : 0;
+            if (pass == 2) v = (!gemv && c > 0 && I > 0) ? 1 : 0;
+            s_tmp[g] = v;
+        }
+        __syncthreads();
+        tot = block_scan_excl(s_tmp, G, warp_tot);
+        const int dst = pass == 0 ? a.pl.u1 : (pass == 1 ? a.pl.u2 : a.pl.gemm_seg);
+        for (int g = threadIdx.x; g < G; g += blockDim.x) plan[dst + g] = s_tmp[g];
+        if (threadIdx.x == 0) plan[dst + G] = tot;
+        __syncthreads();
+    }
+    // stats: active routed experts, gemv segments, gemm segments
+    if (threadIdx.x < 32) {
+        int act = 0, gv = 0, gm = 0;
+        for (int g = threadIdx.x; g < G; g += 32) {
+            const int c = s_cnt[g];
+            const int I = (g == G - 1) ? a.shared_inter : a.inter;
+            if (c > 0 && g < G - 1) ++act;
+            const bool gemv = c > 0 && I > 0 &&
+                              (a.path == HF_PATH_GEMV || (a.path == HF_PATH_AUTO && c <= a.gemv_max));
+            if (gemv) ++gv;
+            else if (c > 0 && I > 0) ++gm;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            act += __shfl_xor_sync(0xffffffffu, act, o);
+            gv += __shfl_xor_sync(0xffffffffu, gv, o);
+            gm += __shfl_xor_sync(0xffffffffu, gm, o);
+        }
+        if (threadIdx.x == 0) {
+            plan[a.pl.stats + 0] = act;
+            plan[a.pl.stats + 1] = gv;
+            plan[a.pl.stats + 2] = gm;
+        }
+    }
+    __syncthreads();
+}
+
+// Rank of token tl (0..127) among the set bits of a 128-bit mask.
+__device__ __forceinline__ int mask_rank(const uint32_t* m, int tl) {
+    int r = 0;
+    const int w = tl >> 5;
+    for (int q = 0; q < w; ++q) r += __popc(m[q]);
+    return r + __popc(m[w] & ((1u << (tl & 31)) - 1u));
+}
+
+// ============================================================ T <= 128: one block does it all
+template <int NPL>
+__global__ void __launch_bounds__(1024) k_route_small(RouteArgs a) {
+    extern __shared__ __align__(16) uint32_t sm[];
+    const int E = a.E, T = a.T, k = a.k, G = a.pl.G;
+    uint32_t* masks = sm;                                   // [E][4]
+    int* s_cnt = reinterpret_cast<int*>(masks + 4 * E);     // [G]
+    int* s_off = s_cnt + G;                                  // [G+1]
+    int* s_ids = s_off + G + 1;                              // [128 * 8]
+    int* warp_tot = s_ids + kSmallRouteT * kMaxTopK;         // [33]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    for (int i = threadIdx.x; i < 4 * E; i += blockDim.x) masks[i] = 0u;
+    for (int t = warp; t < T; t += 32)
+        topk_warp<NPL>(a.logits + size_t(t) * E, 1, a.bias, E, k, a.scale, a.norm, lane,
+                       a.ids + size_t(t) * k, a.w + size_t(t) * k,
+                       a.margins ? a.margins + t : nullptr, s_ids + t * kMaxTopK);
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * k; i += blockDim.x) {
+        const int t = i / k, e = s_ids[t * kMaxTopK + i % k];
+        atomicOr(&masks[4 * e + (t >> 5)], 1u << (t & 31));
+    }
+    __syncthreads();
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+        int c = 0;
+        if (g < E) c = __popc(masks[4 * g]) + __popc(masks[4 * g + 1]) + __popc(masks[4 * g + 2]) +
+                       __popc(masks[4 * g + 3]);
+        else c = a.has_shared ? T : 0;
+        s_cnt[g] = c;
+    }
+    __syncthreads();
+    plan_from_counts(a, s_cnt, s_off, warp_tot);
+    // s_off now holds the last scan (gemm segments); reload offsets from plan
+    for (int g = threadIdx.x; g <= G; g += blockDim.x) s_off[g] = a.plan[a.pl.offsets + g];
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * k; i += blockDim.x) {
+        const int t = i / k, e = s_ids[t * kMaxTopK + i % k];
+        const int pos = s_off[e] + mask_rank(&masks[4 * e], t);
+        a.perm[pos] = i;
+        a.slot_pos[i] = pos;
+    }
+    if (a.has_shared)
+        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+            const int pos = s_off[G - 1] + t, slot = T * k + t;
+            a.perm[pos] = slot;
+            a.slot_pos[slot] = pos;
+        }
+}
+
+// ============================================================ T > 128: four launches
+// (1) k_topk, (2) masks + per-block counts, (3) scan + plan + per-block bases,
+// (4) scatter.
+__global__ void __launch_bounds__(256) k_perm_masks(RouteArgs a) {
+    __shared__ uint32_t masks[4 * kMaxExperts];
+    const int b = blockIdx.x, E = a.E, k = a.k;
+    const int t0 = b * kSmallRouteT;
+    const int nt = min(kSmallRouteT, a.T - t0);
+    for (int i = threadIdx.x; i < 4 * E; i += blockDim.x) masks[i] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * k; i += blockDim.x) {
+        const int tl = i / k, e = a.ids[size_t(t0 + tl) * k + i % k];
+        atomicOr(&masks[4 * e + (tl >> 5)], 1u << (tl & 31));
+    }
+    __syncthreads();
+    uint32_t* gm = a.masks + size_t(b) * 4 * E;
+    for (int i = threadIdx.x; i < 4 * E; i += blockDim.x) gm[i] = masks[i];
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+        a.blk_counts[size_t(b) * E + e] = __popc(masks[4 * e]) + __popc(masks[4 * e + 1]) +
+                                          __popc(masks[4 * e + 2]) + __popc(masks[4 * e + 3]);
+}
+
+__global__ void __launch_bounds__(1024) k_perm_plan(RouteArgs a, int nb) {
+    extern __shared__ __align__(16) uint32_t sm[];
+    const int E = a.E, G = a.pl.G;
+    int* s_cnt = reinterpret_cast<int*>(sm);
+    int* s_tmp = s_cnt + G;
+    int* warp_tot = s_tmp + G + 1;
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+        int c = 0;
+        if (g < E) for (int b = 0; b < nb; ++b) c += a.blk_counts[size_t(b) * E + g];
+        else c = a.has_shared ? a.T : 0;
+        s_cnt[g] = c;
+    }
+    __syncthreads();
+    plan_from_counts(a, s_cnt, s_tmp, warp_tot);
+    // per-block bases (in place over blk_counts)
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int run = a.plan[a.pl.offsets + e];
+        for (int b = 0; b < nb; ++b) {
+            const int c = a.blk_counts[size_t(b) * E + e];
+            a.blk_counts[size_t(b) * E + e] = run;
+            run += c;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) k_perm_scatter(RouteArgs a) {
+    const int b = blockIdx.x, E = a.E, k = a.k, T = a.T;
+    const int t0 = b * kSmallRouteT;
+    const int nt = min(kSmallRouteT, T - t0);
+    const uint32_t* gm = a.masks + size_t(b) * 4 * E;
+    const int32_t* base = a.blk_counts + size_t(b) * E;
+    for (int i = threadIdx.x; i < nt * k; i += blockDim.x) {
+        const int tl = i / k;
+        const int slot = (t0 + tl) * k + i % k;
+        const int e = a.ids[slot];
+        const int pos = base[e] + mask_rank(gm + 4 * e, tl);
+        a.perm[pos] = slot;
+        a.slot_pos[slot] = pos;
+    }
+    if (a.has_shared) {
+        const int off = a.plan[a.pl.offsets + a.pl.G - 1];
+        for (int tl = threadIdx.x; tl < nt; tl += blockDim.x) {
+            const int t = t0 + tl, pos = off + t, slot = T * k + t;
+            a.perm[pos] = slot;
+            a.slot_pos[slot] = pos;
+        }
+    }
+}
+
+// ============================================================ launchers
+// Runs the statement with NPL = scores per lane (E/32 rounded up to a power of 2).
+#define HF_NPL_SWITCH(E, ...)                                      \
+    do {                                                           \
+        const int _n = ((E) + 31) / 32;                            \
+        if (_n <= 1) { constexpr int NPL = 1; __VA_ARGS__; }        \
+        else if (_n <= 2) { constexpr int NPL = 2; __VA_ARGS__; }   \
+        else if (_n <= 4) { constexpr int NPL = 4; __VA_ARGS__; }   \
+        else if (_n <= 8) { constexpr int NPL = 8; __VA_ARGS__; }   \
+        else if (_n <= 16) { constexpr int NPL = 16; __VA_ARGS__; } \
+        else { constexpr int NPL = 32; __VA_ARGS__; }              \
+    } while (0)
+
+hf_status launch_router_logits(const RouteArgs& a, cudaStream_t st) {
+    if (a.T == 0) return HF_OK;
+    if (a.T <= kRouterMaxT) {
+        const int grid = (a.E + kRouterRowsPerBlock - 1) / kRouterRowsPerBlock;
+        if (a.x_f32) k_router_gemv<true><<<grid, 256, 0, st>>>(a);
+        else k_router_gemv<false><<<grid, 256, 0, st>>>(a);
+    } else {
+        dim3 grid((a.T + 63) / 64, (a.E + 63) / 64);
+        if (a.x_f32) k_router_tile<true><<<grid, 256, 0, st>>>(a);
+        else k_router_tile<false><<<grid, 256, 0, st>>>(a);
+    }
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+hf_status launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
+    *launches = 0;
+    if (a.T == 0) return HF_OK;
+    const int G = a.pl.G;
+    *launches = a.T <= kSmallRouteT ? 1 : 4;
+    if (a.T <= kSmallRouteT) {
+        const size_t smem = sizeof(uint32_t) * (4 * a.E + G + G + 1 + kSmallRouteT * kMaxTopK + 33);
+        HF_NPL_SWITCH(a.E, {
+            auto kern = k_route_small<NPL>;
+            HF_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+            kern<<<1, 1024, smem, st>>>(a);
+        });
+        HF_CUDA(cudaGetLastError());
+        return HF_OK;
+    }
+    const int nb = (a.T + kSmallRouteT - 1) / kSmallRouteT;
+    HF_NPL_SWITCH(a.E, {
+        k_topk<NPL><<<(a.T + 7) / 8, 256, 0, st>>>(a.logits, a.T, a.E, a.bias, a.k, a.scale,
+                                                   a.norm, 1, a.ids, a.w, a.margins);
+    });
+    HF_CUDA(cudaGetLastError());
+    k_perm_masks<<<nb, 256, 0, st>>>(a);
+    HF_CUDA(cudaGetLastError());
+    const size_t smem = sizeof(int) * (G + G + 1 + 33);
+    k_perm_plan<<<1, 1024, smem, st>>>(a, nb);
+    HF_CUDA(cudaGetLastError());
+    k_perm_scatter<<<nb, 256, 0, st>>>(a);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+hf_status launch_topk(const float* scores, int T, int E, const float* bias, int k, float scale,
+                      int norm, int32_t* idx, float* w, int apply_sigmoid, float* margins,
+                      cudaStream_t st) {
+    if (T == 0) return HF_OK;
+    HF_NPL_SWITCH(E, {
+        k_topk<NPL><<<(T + 7) / 8, 256, 0, st>>>(scores, T, E, bias, k, scale, norm,
+                                                 apply_sigmoid, idx, w, margins);
+    });
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+}  // namespace hf

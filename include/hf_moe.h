@@ -1,0 +1,192 @@
+/*
+ * hf_moe.h -- C ABI of the B200 (sm_100a) MoE layer for HummingFlight.
+ *
+ * One shared library (hummingflight_b200/libhf_moe.so) replaces the engine's
+ * CPU MoE path and its sm_86 expert offload. Plain C types only: pointers,
+ * sizes, an opaque context; CUDA streams are passed as hf_stream (the same
+ * object as cudaStream_t, declared opaquely so callers need no CUDA headers).
+ *
+ * Every call returns an hf_status; nothing falls back to the CPU. A failed
+ * call leaves a message for hf_last_error() (per thread). One context per
+ * device; a context is used by one host thread at a time, as the reference's
+ * single generation thread does (engine/scheduler.h:162-166).
+ *
+ * Reference interfaces replaced (paths in the HummingFlight source tree):
+ *   GLMForward::moeLayer          model/glm_forward.h:93, glm_forward.cpp:509-661
+ *   gemv_bf16_f32                 compute/cpu_kernels.h:16-17
+ *   topKScores / TopKResult       compute/moe_router.h:12-16, :29-57
+ *   gpuExpertCacheConfig / gpuExpertStage / gpuExpertFFN
+ *                                 compute/cuda_backend.h:64-85
+ *   Scheduler::getExpertPtr       engine/scheduler.h:80-84 ([gate|up|down] layout)
+ *   Scheduler::getSharedProjectionPtr  engine/scheduler.h:93-96 (3 pointers)
+ */
+#ifndef HF_MOE_H
+#define HF_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HF_MOE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define HF_API __attribute__((visibility("default")))
+#else
+#define HF_API
+#endif
+
+typedef struct CUstream_st* hf_stream; /* == cudaStream_t; NULL = legacy default stream */
+
+typedef enum hf_status {
+    HF_OK = 0,
+    HF_ERR_ARG = 1,         /* bad argument, shape or unsupported size          */
+    HF_ERR_CUDA = 2,        /* a CUDA runtime/driver call or kernel failed      */
+    HF_ERR_NCCL = 3,        /* expert-parallel exchange failed                  */
+    HF_ERR_TIMEOUT = 4,     /* a bounded device wait gave up (error word set)   */
+    HF_ERR_OOM = 5,         /* device allocation failed                         */
+    HF_ERR_STATE = 6,       /* call out of order (e.g. weights not set)         */
+    HF_ERR_UNSUPPORTED = 7  /* no device / wrong architecture                   */
+} hf_status;
+
+typedef enum hf_mem_kind { HF_MEM_HOST = 0, HF_MEM_DEVICE = 1 } hf_mem_kind;
+typedef enum hf_dtype { HF_BF16 = 0, HF_F32 = 1 } hf_dtype;
+
+/* Expert-path selection per expert segment (by its token count). */
+typedef enum hf_path {
+    HF_PATH_AUTO = 0,       /* grouped GEMV for short segments, tcgen05 GEMM else */
+    HF_PATH_GEMV = 1,       /* always the CUDA-core grouped GEMV                   */
+    HF_PATH_GEMM = 2        /* always the tcgen05 grouped GEMM                     */
+} hf_path;
+
+/* Layer shape and placement. Field names follow ModelConfig's MoE keys
+ * (model/config.h; parsed at model/config.cpp:108-117). */
+typedef struct hf_moe_config {
+    int hidden_size;               /* hiddenSize (multiple of 8)                   */
+    int num_experts;               /* numLocalExperts = n_routed_experts           */
+    int num_experts_per_tok;       /* top-k, 1..8 (TopKResult holds 8)             */
+    int moe_intermediate_size;     /* moeIntermediateSize (multiple of 8)          */
+    int shared_intermediate_size;  /* nSharedExperts * moeIntermediateSize; 0=none */
+    float routed_scaling_factor;   /* routedScalingFactor                          */
+    int norm_topk_prob;            /* normTopkProb                                 */
+    int num_layers;                /* layers this context holds weights for        */
+    int max_tokens;                /* largest T of any forward (scratch sizing)    */
+    int device;                    /* CUDA device ordinal                          */
+    int path;                      /* hf_path                                      */
+    int gemv_max_tokens;           /* AUTO: segments up to this use the GEMV; 0=default */
+    /* expert parallelism (experts [r*E/W, (r+1)*E/W) on rank r); W=1: none */
+    int ep_rank;
+    int ep_world;
+    const unsigned char* ep_unique_id; /* 128-byte NCCL unique id when ep_world > 1 */
+} hf_moe_config;
+
+/* Optional device outputs of a forward (any field may be NULL).
+ * Routed slot (t, i) has slot id t*k + i; the shared expert's slot of token t
+ * is T*k + t. Groups are the routed experts 0..E-1 then the shared expert E.
+ * Positions order every slot by (group asc, token asc): the canonical
+ * permutation into per-expert contiguous segments. */
+typedef struct hf_moe_routing {
+    int32_t* topk_ids;      /* [T*k]  TopKResult::indices per token, rank order */
+    float* topk_weights;    /* [T*k]  TopKResult::weights                       */
+    float* margins;         /* [T]    biased score of rank k-1 minus rank k     */
+    int32_t* counts;        /* [E+1]  tokens per group (shared = T or 0)        */
+    int32_t* offsets;       /* [E+2]  exclusive scan of counts                  */
+    int32_t* perm;          /* [T*k+T] slot id at each position                 */
+    float* slot_out;        /* [(T*k+T) x H] expert output of each slot, by slot id */
+} hf_moe_routing;
+
+typedef struct hf_moe_ctx hf_moe_ctx;
+
+HF_API int hf_abi_version(void);
+HF_API const char* hf_status_string(hf_status s);
+/* Message of the last failed call on this thread ("" if none). */
+HF_API const char* hf_last_error(void);
+
+/* Replaces gpuExpertCacheConfig (compute/cuda_backend.h:64): allocates the
+ * layer weights and the scratch for max_tokens on cfg->device. */
+HF_API hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg);
+HF_API hf_status hf_moe_destroy(hf_moe_ctx* ctx);
+
+/* Router weight mlp.gate.weight [E x H] BF16 and e_score_correction_bias [E]
+ * fp32 (bias may be NULL: no correction), model/weight_index.cpp:20-27,222-236. */
+HF_API hf_status hf_moe_set_router(hf_moe_ctx* ctx, int layer, const uint16_t* router_bf16,
+                            const float* bias, hf_mem_kind kind);
+/* One routed expert in Scheduler::getExpertPtr's layout [gate I*H | up I*H |
+ * down H*I] BF16 (engine/scheduler.h:80-84); copied, so the caller may reuse
+ * the buffer on return, as gpuExpertStage allows (cuda_backend.h:72-78).
+ * Under expert parallelism only the owning rank accepts an eid. */
+HF_API hf_status hf_moe_set_expert(hf_moe_ctx* ctx, int layer, int eid, const uint16_t* gate_up_down,
+                            hf_mem_kind kind);
+/* Shared expert from the three pointers of getSharedProjectionPtr
+ * (engine/scheduler.h:93-96): gate [Is x H], up [Is x H], down [H x Is]. */
+HF_API hf_status hf_moe_set_shared(hf_moe_ctx* ctx, int layer, const uint16_t* gate,
+                            const uint16_t* up, const uint16_t* down, hf_mem_kind kind);
+/* Device address of the resident [gate|up|down] block of expert eid
+ * (eid == E: the shared expert), for loaders that write in place. */
+HF_API hf_status hf_moe_expert_device_ptr(hf_moe_ctx* ctx, int layer, int eid, uint16_t** dev_ptr);
+/* Device addresses of the router weight and bias. */
+HF_API hf_status hf_moe_router_device_ptr(hf_moe_ctx* ctx, int layer, uint16_t** router, float** bias);
+/* Marks a layer's weights complete (after in-place writes). set_* mark it too. */
+HF_API hf_status hf_moe_mark_loaded(hf_moe_ctx* ctx, int layer);
+
+/* The MoE layer over T tokens, asynchronous on `stream`: router GEMV ->
+ * sigmoid -> + bias -> top-k -> permutation -> routed + shared SwiGLU experts
+ * -> weighted combine (glm_forward.cpp:509-661). x: device [T x H], BF16 or
+ * fp32 (x_dtype); out: device fp32 [T x H]. 0 <= T <= max_tokens. */
+HF_API hf_status hf_moe_forward(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_dtype, int T,
+                         float* out, const hf_moe_routing* routing, hf_stream stream);
+/* The same with HOST buffers: copies x in, runs the layer, copies out back and
+ * waits. Pinned host memory makes the copies asynchronous DMA. */
+HF_API hf_status hf_moe_forward_host(hf_moe_ctx* ctx, int layer, const void* x_host, hf_dtype x_dtype,
+                              int T, float* out_host, hf_stream stream);
+/* Drop-in for GLMForward::moeLayer(layer, input, output): one token, fp32 host
+ * vectors of hidden_size, synchronous (model/glm_forward.h:93). */
+HF_API hf_status hf_moe_layer(hf_moe_ctx* ctx, int layer, const float* input, float* output);
+
+/* Routing only (router GEMV, sigmoid, bias, top-k, permutation) into `routing`. */
+HF_API hf_status hf_moe_route(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_dtype, int T,
+                       const hf_moe_routing* routing, hf_stream stream);
+
+/* Statistics of the most recent forward/route on this context (waits for it):
+ * experts with at least one token, and segments on each expert path. */
+HF_API hf_status hf_moe_last_stats(hf_moe_ctx* ctx, int* active_experts, int* gemv_segments,
+                            int* gemm_segments);
+
+/* Per-phase device time of forwards, from CUDA events recorded on the
+ * forward's stream between its kernels (off by default; no counterpart in the
+ * reference, whose GPU timing is one event pair per expert,
+ * cuda_backend.cpp:464-477). Phases: 0 router logits, 1 top-k + permutation
+ * + plan, 2 GEMV gate/up, 3 GEMV down, 4 GEMM gate/up, 5 GEMM down,
+ * 6 combine. Kernel launches are counted whether or not timing is on. */
+#define HF_MOE_PHASES 7
+HF_API hf_status hf_moe_profile(hf_moe_ctx* ctx, int enable);
+/* Waits for the recorded work, writes each phase's milliseconds and kernel
+ * launches since the previous read (either pointer may be NULL), then resets. */
+HF_API hf_status hf_moe_profile_read(hf_moe_ctx* ctx, double* phase_ms, long long* launches);
+
+/* Device twin of gemv_bf16_f32 (compute/cpu_kernels.h:16-17):
+ * y = alpha * A x + beta * y, A BF16 [M x K] row-major, x/y fp32, all device
+ * pointers. Like the reference, y is read even when beta == 0. Any M, K >= 0. */
+HF_API hf_status hf_gemv_bf16_f32(const uint16_t* A, const float* x, float* y, int M, int K, float alpha,
+                           float beta, hf_stream stream);
+
+/* Device twin of topKScores over T score rows (compute/moe_router.h:29-57):
+ * scores [T x E] fp32 (post-sigmoid), bias [E] or NULL, writes idx/weights
+ * [T x min(k,E)]. Ties go to the lower expert id. */
+HF_API hf_status hf_topk_scores(const float* scores, int T, int E, const float* bias, int k, float scale,
+                         int norm, int32_t* idx, float* weights, hf_stream stream);
+
+/* Dense SwiGLU MLP (GLMForward::denseMlp, glm_forward.cpp:411-432) over T
+ * tokens with device weights gate/up [I x H], down [H x I]. workspace: device
+ * scratch of at least hf_dense_mlp_workspace_size(T, H, I) bytes. */
+HF_API size_t hf_dense_mlp_workspace_size(int T, int H, int I);
+HF_API hf_status hf_dense_mlp_forward(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                               const void* x, hf_dtype x_dtype, int T, int H, int I, float* out,
+                               void* workspace, size_t workspace_bytes, hf_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HF_MOE_H */

@@ -75,6 +75,7 @@ def lib():
         L.hfo_topk_scores.argtypes = [_c_f32p, ctypes.c_int, _c_f32p, ctypes.c_int,
                                       ctypes.c_float, ctypes.c_int, _c_i32p, _c_f32p, _c_f32p]
         L.hfo_topk_scores.restype = ctypes.c_int
+        L.hfo_router_scores.argtypes = [_c_u16p, _c_f32p, ctypes.c_int, ctypes.c_int, _c_f32p]
         L.hfo_expert_ffn.argtypes = [_c_u16p, _c_u16p, _c_u16p, _c_f32p, _c_f32p, ctypes.c_int,
                                      ctypes.c_int]
         L.hfo_permute.argtypes = [_c_i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -206,6 +207,35 @@ def gemv_bf16_f32(A_bf16, x, y=None, alpha=1.0, beta=0.0):
     y = np.zeros(M, np.float32) if y is None else np.array(y, dtype=np.float32)
     lib().hfo_gemv_bf16_f32(_p(A, _c_u16p), _p(x, _c_f32p), _p(y, _c_f32p), M, K, alpha, beta)
     return y
+
+
+def router_scores(router_bf16, x_f32):
+    """Router GEMV + sigmoid for one token (glm_forward.cpp:519-524)."""
+    W = np.ascontiguousarray(router_bf16, dtype=np.uint16)
+    E, H = W.shape
+    x = np.ascontiguousarray(x_f32, dtype=np.float32)
+    s = np.zeros(E, np.float32)
+    lib().hfo_router_scores(_p(W, _c_u16p), _p(x, _c_f32p), E, H, _p(s, _c_f32p))
+    return s
+
+
+def route_synth(d: Dims, wseed: int, layer: int, x_f32, bias=None):
+    """Router + top-k for every token on generated router weights.
+    Returns (ids [T x k], weights [T x k], margins [T])."""
+    router = gen_bf16_normal(wseed, layer, KIND_ROUTER, 0, 0.02, d.num_experts * d.hidden)
+    router = router.reshape(d.num_experts, d.hidden)
+    if bias is None:
+        bias = gen_f32_uniform(wseed, layer, KIND_BIAS, 0, -0.1, 0.1, d.num_experts)
+    x = np.ascontiguousarray(x_f32, dtype=np.float32)
+    T = x.shape[0]
+    k = min(d.top_k, d.num_experts)
+    ids = np.zeros((T, k), np.int32)
+    w = np.zeros((T, k), np.float32)
+    mg = np.zeros(T, np.float32)
+    for t in range(T):
+        i, ww, m = topk_scores(router_scores(router, x[t]), bias, d.top_k, d.scale, d.norm_topk)
+        ids[t], w[t], mg[t] = i, ww, m
+    return ids, w, mg
 
 
 def topk_scores(scores, bias, top_k, scale=2.5, norm=True):

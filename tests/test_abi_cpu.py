@@ -1,0 +1,67 @@
+"""C-ABI checks that need no GPU: the library loads, exports every entry point
+declared in include/*.h, and reports errors through statuses (no device here
+means HF_ERR_UNSUPPORTED, never a silent fallback)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from hummingflight_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for h in ("hf_moe.h", "hf_synth.h"):
+        src = open(os.path.join(ROOT, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:[A-Za-z_][\w\s\*]*?)\b(hf_\w+)\s*\(", src, flags=re.M):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_functions()
+    assert len(names) >= 20
+    L = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    # and the ctypes table covers them all
+    assert set(names) <= set(_lib.SIGNATURES), set(names) - set(_lib.SIGNATURES)
+
+
+def test_abi_version_and_status_strings():
+    L = _lib.lib()
+    assert L.hf_abi_version() == 1
+    assert L.hf_status_string(_lib.HF_ERR_TIMEOUT) == b"HF_ERR_TIMEOUT"
+
+
+def test_create_without_device_fails_loudly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a device is present")
+    cfg = _lib.HfMoeConfig(64, 8, 2, 32, 32, 2.5, 1, 1, 4, 0, 0, 0, 0, 1, None)
+    h = ctypes.c_void_p()
+    st = _lib.lib().hf_moe_create(ctypes.byref(h), ctypes.byref(cfg))
+    assert st == _lib.HF_ERR_UNSUPPORTED
+    assert b"device" in _lib.lib().hf_last_error()
+
+
+def test_create_rejects_bad_shapes_before_touching_a_device():
+    L = _lib.lib()
+    h = ctypes.c_void_p()
+    for bad in [dict(hidden=60), dict(k=9), dict(k=0), dict(inter=30), dict(E=0), dict(layers=0)]:
+        p = dict(hidden=64, E=8, k=2, inter=32, layers=1)
+        p.update(bad)
+        cfg = _lib.HfMoeConfig(p["hidden"], p["E"], p["k"], p["inter"], 32, 2.5, 1, p["layers"],
+                               4, 0, 0, 0, 0, 1, None)
+        assert L.hf_moe_create(ctypes.byref(h), ctypes.byref(cfg)) == _lib.HF_ERR_ARG, bad
+
+
+def test_null_arguments_are_rejected():
+    L = _lib.lib()
+    assert L.hf_gemv_bf16_f32(None, None, None, 4, 4, 1.0, 0.0, None) == _lib.HF_ERR_ARG
+    assert L.hf_topk_scores(None, 1, 8, None, 9, 1.0, 1, None, None, None) == _lib.HF_ERR_ARG
+    assert L.hf_moe_forward(None, 0, None, 0, 1, None, None, None) == _lib.HF_ERR_ARG
