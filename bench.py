@@ -193,9 +193,19 @@ def main():
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--ref-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--experts", type=int, default=0,
+                    help="profiling case: fewer routed experts (same per-expert shape)")
+    ap.add_argument("--tokens", type=int, default=0, help="profiling case: override T")
+    ap.add_argument("--gemv-max", type=int, default=0,
+                    help="AUTO path: segments up to this many tokens use the GEMV (0 = default)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     wl = WORKLOADS[args.config]
+    if args.experts or args.tokens:
+        from dataclasses import replace
+        shape = replace(wl.shape, num_experts=args.experts or wl.shape.num_experts)
+        wl = replace(wl, shape=shape, tokens=args.tokens or wl.tokens,
+                     name=f"{wl.name}_E{shape.num_experts}_T{args.tokens or wl.tokens}")
     if args.impl == "reference":
         run_reference(args, wl)
         return
@@ -215,7 +225,7 @@ def main():
                                 device_id=torch.device("cuda", local))
     shape = wl.shape
     T, H = wl.tokens, shape.hidden
-    L = MoELayer(shape, wl.layers, T, local, args.path)
+    L = MoELayer(shape, wl.layers, T, local, args.path, args.gemv_max)
     bias = zipf_bias(shape.num_experts, wl.weight_seeds[0]) if wl.bias == "zipf" else None
     for l, seed in enumerate(wl.weight_seeds):
         L.synth_layer(l, seed, 0, bias)

@@ -60,6 +60,9 @@ SIGNATURES = {
     "hf_moe_layer": (c_int, [c_vp, c_int, c_vp, c_vp]),
     "hf_moe_route": (c_int, [c_vp, c_int, c_vp, c_int, c_int, ctypes.POINTER(HfMoeRouting), c_vp]),
     "hf_moe_last_stats": (c_int, [c_vp, ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "hf_moe_synchronize": (c_int, [c_vp]),
+    "hf_moe_set_wait_timeout": (c_int, [c_vp, c_u64]),
+    "hf_moe_debug_stall": (c_int, [c_vp, c_int]),
     "hf_moe_profile": (c_int, [c_vp, c_int]),
     "hf_moe_profile_read": (c_int, [c_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]),
     "hf_gemv_bf16_f32": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_float, c_float, c_vp]),

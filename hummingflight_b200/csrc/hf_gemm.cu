@@ -1,0 +1,398 @@
+// hf_gemm.cu -- tcgen05 grouped GEMM over expert segments (prefill path).
+//
+// Replaces, for segments with many tokens, the per-token GEMVs of expertFFNRaw
+// (model/glm_forward.cpp:434-449); the reference has no batched or
+// tensor-core code at all.
+//
+// Orientation ("swap AB"): the MMA's M = 128 rows of an expert weight matrix,
+// N = the segment's tokens (up to BN per tile, rounded up to 16 at run time),
+// K = hidden (gate/up) or intermediate (down). Both operands are K-major, so
+// the reference's [gate | up | down] row-major weights feed the tensor cores
+// unchanged: one TMA box of 64 bf16 x 128 rows per weight matrix and k-block,
+// and boxes of 64 x 16 token rows for the activations.
+//
+//   GEMM1  acc_g = Wg x^T, acc_u = Wu x^T (two TMEM accumulators); epilogue
+//          mid = g / (1 + exp(-g)) * u in fp32, stored as a BF16 hi + lo pair
+//          (hi = bf16(mid), lo = bf16(mid - hi)) so the next GEMM sees ~16
+//          mantissa bits instead of 8.
+//   GEMM2  acc = Wd mid_hi^T + Wd mid_lo^T; epilogue stores fp32 expert
+//          outputs y[position][h] for the deterministic combine.
+//
+// CTA = 6 warps, one CTA per SM, persistent over a static tile list:
+// warp 0 issues TMA loads into a STAGES-deep shared-memory ring, warp 1 owns
+// TMEM and issues tcgen05.mma from one thread, warps 2-5 drain the double-
+// buffered TMEM accumulators. Every wait is bounded (see hf_sm100.cuh): on
+// timeout the CTA drains its TMA loads and MMAs, frees TMEM and reports
+// HF_ERR_TIMEOUT through the error word instead of hanging.
+#include "hf_internal.cuh"
+#include "hf_sm100.cuh"
+
+namespace hf {
+
+using namespace sm100;
+
+constexpr int kGemmThreads = 192;
+constexpr int kBoxRowsB = 16;
+constexpr uint32_t kTileABytes = 128 * 64 * 2;  // 128 rows x 64 bf16
+constexpr uint64_t kDrainNs = 500ull * 1000 * 1000;
+
+template <int NUM_A, int NUM_B, int BN>
+struct GemmCfg {
+    static constexpr int kStageBytes = NUM_A * kTileABytes + NUM_B * BN * 128;
+    static constexpr int kStages0 = (220 * 1024) / kStageBytes;
+    static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
+    static constexpr int kAccCols = NUM_A * BN;
+    static constexpr int kCols0 = 2 * kAccCols;
+    static constexpr uint32_t kTmemCols = kCols0 <= 32 ? 32 : kCols0 <= 64 ? 64 : kCols0 <= 128 ? 128
+                                          : kCols0 <= 256 ? 256 : 512;
+    static constexpr int kBarOff = kStages * kStageBytes;
+    static constexpr int kSmem = 1024 + kBarOff + 256;
+    static_assert(kCols0 <= 512, "TMEM holds 512 columns");
+    static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
+};
+
+struct TileInfo {
+    int seg, n0, n, m0, mvalid, kblocks;
+    int rowA0, rowA1;
+    bool shared;
+};
+
+__device__ __forceinline__ void decode_tile(const GemmArgs& a, int u, TileInfo& t) {
+    const int G = a.pl.G;
+    const int32_t* pref = a.plan + (a.which == 1 ? a.pl.g1 : a.pl.g2);
+    const int g = find_group(pref, G, u);
+    const int c = a.plan[a.pl.counts + g];
+    const int nt = (c + a.bn - 1) / a.bn;
+    const int local = u - pref[g];
+    const int mi = local / nt, ni = local % nt;
+    t.shared = (g == G - 1);
+    const int Ig = t.shared ? a.Is : a.I;
+    t.seg = a.plan[a.pl.offsets + g];
+    t.n0 = ni * a.bn;
+    t.n = min(a.bn, c - t.n0);
+    t.m0 = mi * 128;
+    if (a.which == 1) {
+        const int base = t.shared ? 0 : g * 3 * a.I;
+        t.rowA0 = base + t.m0;
+        t.rowA1 = base + Ig + t.m0;
+        t.mvalid = Ig - t.m0;
+        t.kblocks = (a.H + 63) / 64;
+    } else {
+        t.rowA0 = (t.shared ? 0 : g * 3 * a.H) + 2 * a.H + t.m0;
+        t.rowA1 = 0;
+        t.mvalid = a.H - t.m0;
+        t.kblocks = (Ig + 63) / 64;
+    }
+}
+
+__device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
+    const uint64_t dl = globaltimer() + kDrainNs;
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer() > dl) return false;
+    return true;
+}
+
+template <int NUM_A, int NUM_B, int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    k_moe_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_sh,
+               const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
+               const __grid_constant__ CUtensorMap tmB0_sh,
+               const __grid_constant__ CUtensorMap tmB1_sh, GemmArgs a) {
+    using C = GemmCfg<NUM_A, NUM_B, BN>;
+    constexpr int S = C::kStages;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+    uint64_t* empty = full + S;
+    uint64_t* tfull = empty + S;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* final_bar = tempty + 2;
+    uint64_t* stall_bar = final_bar + 1;  // never signalled (test hook)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stall_bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t deadline = globaltimer() + a.timeout_ns;
+    const int total = a.plan[(a.which == 1 ? a.pl.g1 : a.pl.g2) + a.pl.G];
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(final_bar, 1);
+        mbar_init(stall_bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------------------------------------------------- TMA producer
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB0);
+        uint32_t it = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+            TileInfo t;
+            decode_tile(a, u, t);
+            const int nb = (t.n + kBoxRowsB - 1) / kBoxRowsB;
+            const uint32_t bytes = NUM_A * kTileABytes + NUM_B * nb * (kBoxRowsB * 128);
+            const CUtensorMap* mA = t.shared ? &tmA_sh : &tmA;
+            const CUtensorMap* mB0 = (a.which == 2 && t.shared) ? &tmB0_sh : &tmB0;
+            const CUtensorMap* mB1 = (a.which == 2 && t.shared) ? &tmB1_sh : &tmB1;
+            for (int kb = 0; kb < t.kblocks; ++kb, ++it) {
+                const uint32_t s = it % S, ph = (it / S) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, deadline)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = smem + s * C::kStageBytes;
+                mbar_arrive_expect_tx(&full[s], bytes);
+                tma_load_2d(st, mA, &full[s], kb * 64, t.rowA0);
+                if (NUM_A == 2) tma_load_2d(st + kTileABytes, mA, &full[s], kb * 64, t.rowA1);
+                uint8_t* sb = st + NUM_A * kTileABytes;
+                for (int j = 0; j < nb; ++j) {
+                    const int row = t.seg + t.n0 + j * kBoxRowsB;
+                    tma_load_2d(sb + j * (kBoxRowsB * 128), mB0, &full[s], kb * 64, row);
+                    if (NUM_B == 2)
+                        tma_load_2d(sb + BN * 128 + j * (kBoxRowsB * 128), mB1, &full[s], kb * 64,
+                                    row);
+                }
+            }
+        }
+        if (!ok) {  // drain: let every issued load land before the CTA exits
+            const uint32_t first = it > uint32_t(S) ? it - S : 0;
+            for (uint32_t i = first; i < it; ++i) drain_wait(&full[i % S], (i / S) & 1);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------------------------------------------------- MMA issuer
+        uint32_t it = 0, lt = 0;
+        bool ok = true;
+        if (a.test_stall) ok = mbar_wait(stall_bar, 0, abort_flag, deadline);
+        for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lt) {
+            TileInfo t;
+            decode_tile(a, u, t);
+            const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
+            if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, deadline)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t nmma = uint32_t((t.n + 15) & ~15);
+            const uint32_t idesc = idesc_bf16_m128(nmma);
+            const uint32_t d0 = tmem_base + acc * C::kAccCols;
+            for (int kb = 0; kb < t.kblocks; ++kb, ++it) {
+                const uint32_t s = it % S, ph = (it / S) & 1;
+                if (!mbar_wait(&full[s], ph, abort_flag, deadline)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = smem_u32(smem + s * C::kStageBytes);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+                    for (int ai = 0; ai < NUM_A; ++ai) {
+                        const uint64_t ad = desc_k_sw128(st + ai * kTileABytes) + 2 * kk;
+#pragma unroll
+                        for (int bi = 0; bi < NUM_B; ++bi) {
+                            const uint64_t bd =
+                                desc_k_sw128(st + NUM_A * kTileABytes + bi * BN * 128) + 2 * kk;
+                            mma_bf16(d0 + ai * BN, ad, bd, idesc, (kb | kk | bi) != 0);
+                        }
+                    }
+                }
+                mma_commit(&empty[s]);
+            }
+            if (!ok) break;
+            mma_commit(&tfull[acc]);
+        }
+        mma_commit(final_bar);  // completes once every MMA issued above is done
+        drain_wait(final_bar, 0);
+    } else if (warp >= 2) {
+        // ---------------------------------------------------------- epilogue
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const int r = q * 32 + lane;
+        uint32_t lt = 0;
+        for (int u = blockIdx.x; u < total; u += gridDim.x, ++lt) {
+            TileInfo t;
+            decode_tile(a, u, t);
+            const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], aph, abort_flag, deadline)) break;
+            tc_fence_after();
+            const uint32_t ta = tmem_base + (uint32_t(q * 32) << 16) + acc * C::kAccCols;
+            const bool rv = r < t.mvalid;
+            for (int c0 = 0; c0 < t.n; c0 += 32) {
+                uint32_t v0[32], v1[32];
+                tmem_ld32(ta + c0, v0);
+                if constexpr (NUM_A == 2) tmem_ld32(ta + BN + c0, v1);
+                tmem_ld_wait();
+                if (rv) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int col = c0 + j;
+                        if (col < t.n) {
+                            const size_t pos = size_t(t.seg + t.n0 + col);
+                            if constexpr (NUM_A == 2) {
+                                const float m = swiglu(__uint_as_float(v0[j]), __uint_as_float(v1[j]));
+                                const uint16_t hi = f32_to_bf16_rne(m);
+                                const uint16_t lo = f32_to_bf16_rne(__fsub_rn(m, bf16_to_f32(hi)));
+                                a.mid_hi[pos * a.Imax + t.m0 + r] = hi;
+                                a.mid_lo[pos * a.Imax + t.m0 + r] = lo;
+                            } else {
+                                a.y[pos * a.H + t.m0 + r] = __uint_as_float(v0[j]);
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+    }
+    __syncwarp();  // reconverge warps 0 and 1 (one lane of each ran a role loop)
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+    if (threadIdx.x == 0 && *abort_flag) atomicOr(a.err, 1);
+}
+
+// ============================================================ activation gather
+// xp[pos] = x[token(perm[pos])] for every position of a GEMM segment, as BF16
+// (hi plane) plus, for fp32 activations, the residual BF16 lo plane.
+template <bool XF32>
+__global__ void __launch_bounds__(256) k_gather_x(GatherArgs a) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    const int G = a.pl.G;
+    const int total = a.plan[a.pl.offsets + G];
+    const int32_t* g1 = a.plan + a.pl.g1;
+    for (int p = warp; p < total; p += nw) {
+        const int g = find_group(a.plan + a.pl.offsets, G, p);
+        if (g1[g + 1] == g1[g]) continue;  // GEMV segment
+        const int t = token_of_slot(a.perm[p], a.T, a.k);
+        uint4* dh = reinterpret_cast<uint4*>(a.xp_hi + size_t(p) * a.H);
+        if constexpr (XF32) {
+            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.x) +
+                                                                size_t(t) * a.H);
+            uint4* dl = reinterpret_cast<uint4*>(a.xp_lo + size_t(p) * a.H);
+            for (int c = lane; c < a.H / 8; c += 32) {
+                const float4 u0 = __ldg(src + 2 * c), u1 = __ldg(src + 2 * c + 1);
+                const float f[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+                uint32_t h[4], l[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint16_t h0 = f32_to_bf16_rne(f[2 * q]), h1 = f32_to_bf16_rne(f[2 * q + 1]);
+                    const uint16_t l0 = f32_to_bf16_rne(__fsub_rn(f[2 * q], bf16_to_f32(h0)));
+                    const uint16_t l1 = f32_to_bf16_rne(__fsub_rn(f[2 * q + 1], bf16_to_f32(h1)));
+                    h[q] = uint32_t(h0) | (uint32_t(h1) << 16);
+                    l[q] = uint32_t(l0) | (uint32_t(l1) << 16);
+                }
+                dh[c] = make_uint4(h[0], h[1], h[2], h[3]);
+                dl[c] = make_uint4(l[0], l[1], l[2], l[3]);
+            }
+        } else {
+            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) +
+                                                              size_t(t) * a.H);
+            for (int c = lane; c < a.H / 8; c += 32) dh[c] = ld_nc_u4(src + c);
+        }
+    }
+}
+
+// ============================================================ host launchers
+template <int NUM_A, int NUM_B, int BN>
+static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cudaStream_t st) {
+    using C = GemmCfg<NUM_A, NUM_B, BN>;
+    auto kern = k_moe_gemm<NUM_A, NUM_B, BN>;
+    HF_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+    kern<<<grid, kGemmThreads, C::kSmem, st>>>(m.A, m.A_sh, m.B0, m.B1, m.B0_sh, m.B1_sh, a);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid, cudaStream_t st) {
+    if (a.which == 1) {
+        if (a.bn == 64) return num_b == 1 ? launch_one<2, 1, 64>(m, a, grid, st)
+                                          : launch_one<2, 2, 64>(m, a, grid, st);
+        if (a.bn == 128) return num_b == 1 ? launch_one<2, 1, 128>(m, a, grid, st)
+                                           : launch_one<2, 2, 128>(m, a, grid, st);
+    } else {
+        if (a.bn == 64) return launch_one<1, 2, 64>(m, a, grid, st);
+        if (a.bn == 128) return launch_one<1, 2, 128>(m, a, grid, st);
+    }
+    return fail(HF_ERR_ARG, "unsupported GEMM token tile");
+}
+
+hf_status launch_gather(const GatherArgs& a, int x_f32, cudaStream_t st) {
+    const int grid = num_sms(a.device) * 4;
+    if (x_f32) k_gather_x<true><<<grid, 256, 0, st>>>(a);
+    else k_gather_x<false><<<grid, 256, 0, st>>>(a);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+// ------------------------------------------------------------------ tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D BF16 view: `rows` rows of `cols` elements, `pitch` elements apart;
+// box of 64 elements x box_rows rows, 128-byte swizzle, OOB reads as zero.
+hf_status make_map_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows,
+                        uint64_t pitch, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(HF_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch * 2) % 16)
+        return fail(HF_ERR_ARG, "tensor map base/pitch not 16-byte aligned");
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {pitch * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(HF_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return HF_OK;
+}
+
+int gemm_smem_bytes(int which, int num_b, int bn) {
+    if (which == 1) {
+        if (bn == 64) return num_b == 1 ? GemmCfg<2, 1, 64>::kSmem : GemmCfg<2, 2, 64>::kSmem;
+        return num_b == 1 ? GemmCfg<2, 1, 128>::kSmem : GemmCfg<2, 2, 128>::kSmem;
+    }
+    return bn == 64 ? GemmCfg<1, 2, 64>::kSmem : GemmCfg<1, 2, 128>::kSmem;
+}
+
+}  // namespace hf

@@ -1,6 +1,7 @@
 // hf_internal.cuh -- shared device helpers and host plumbing of libhf_moe.so.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (the encode entry point is fetched at run time)
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -55,7 +56,8 @@ struct PlanLayout {
     int offsets;      // [G+1] positions
     int u1;           // [G+1] GEMV1 unit prefix
     int u2;           // [G+1] GEMV2 unit prefix
-    int gemm_seg;     // [G+1] GEMM segment prefix (segments routed to the GEMM)
+    int g1;           // [G+1] GEMM1 (gate/up) tile prefix
+    int g2;           // [G+1] GEMM2 (down) tile prefix
     int stats;        // [4]: active experts, gemv segments, gemm segments, error word
     int words;        // total
     static PlanLayout make(int G) {
@@ -65,8 +67,9 @@ struct PlanLayout {
         p.offsets = p.counts + G;
         p.u1 = p.offsets + G + 1;
         p.u2 = p.u1 + G + 1;
-        p.gemm_seg = p.u2 + G + 1;
-        p.stats = p.gemm_seg + G + 1;
+        p.g1 = p.u2 + G + 1;
+        p.g2 = p.g1 + G + 1;
+        p.stats = p.g2 + G + 1;
         p.words = p.stats + 4;
         return p;
     }
@@ -95,6 +98,8 @@ struct RouteArgs {
     int32_t* blk_counts;      // [nb x E]
     int path;                 // hf_path
     int gemv_max;             // AUTO threshold
+    int gemm_ok;              // shapes allow the tcgen05 GEMM (64-aligned)
+    int gemm_bn;              // GEMM token tile (columns per tile)
 };
 
 // ------------------------------------------------------------------ device helpers
@@ -191,6 +196,39 @@ hf_status launch_gemv2(const GemvArgs& a, cudaStream_t st);
 int gemv_grid(int device, bool first, bool xf32, int H, int inter_max);
 size_t gemv1_smem(int H, bool xf32);
 size_t gemv2_smem(int inter_max);
+
+// tcgen05 grouped GEMM (hf_gemm.cu).
+struct GemmArgs {
+    const int32_t* plan;
+    PlanLayout pl;
+    int which;              // 1: gate/up + SwiGLU -> mid hi/lo; 2: down -> y
+    int H, I, Is, Imax, bn;
+    uint16_t* mid_hi;       // [slots x Imax] bf16
+    uint16_t* mid_lo;
+    float* y;               // [slots x H] fp32
+    int* err;               // error word (plan stats[3])
+    unsigned long long timeout_ns;
+    int test_stall;         // wait on a barrier nothing signals (test hook)
+};
+struct GemmMaps {
+    CUtensorMap A, A_sh;       // weights (routed view, shared expert view)
+    CUtensorMap B0, B1;        // activations (hi, lo planes), routed K extent
+    CUtensorMap B0_sh, B1_sh;  // the same with the shared expert's K extent
+};
+struct GatherArgs {
+    const int32_t* plan;
+    PlanLayout pl;
+    const int32_t* perm;
+    const void* x;
+    int T, k, H, device;
+    uint16_t* xp_hi;
+    uint16_t* xp_lo;
+};
+hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid, cudaStream_t st);
+hf_status launch_gather(const GatherArgs& a, int x_f32, cudaStream_t st);
+hf_status make_map_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows,
+                        uint64_t pitch, uint32_t box_rows);
+int gemm_smem_bytes(int which, int num_b, int bn);
 
 // Device generator (hf_synth.cu).
 hf_status synth_bf16(uint16_t* dst, uint64_t n, uint64_t key, float scale, cudaStream_t st);

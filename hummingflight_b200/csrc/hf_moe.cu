@@ -62,6 +62,10 @@ struct LayerBuf {
     uint16_t* shared = nullptr;  // [gate|up|down] of the shared expert
     GroupW* groups = nullptr;    // [G] device table
     bool loaded = false;
+    // TMA views of the weights for the tcgen05 GEMM (built with the buffers)
+    CUtensorMap gu{}, gu_sh{};   // gate/up rows: H-wide rows of [gate|up|down]
+    CUtensorMap dn{}, dn_sh{};   // down rows: I-wide rows of the same buffers
+    bool maps = false;
 };
 
 template <typename T>
@@ -96,6 +100,16 @@ struct hf_moe_ctx {
     float* y = nullptr;
     void* x_dev = nullptr;   // host-buffer API staging [T_max x H] fp32-sized
     float* out_dev = nullptr;
+    uint16_t* mid_hi = nullptr;  // GEMM path: SwiGLU output as bf16 hi + lo
+    uint16_t* mid_lo = nullptr;
+    uint16_t* xp_hi = nullptr;   // GEMM path: activations gathered by position
+    uint16_t* xp_lo = nullptr;
+    hf::GemmMaps maps1{}, maps2{};  // activation-side tensor maps (GEMM1, GEMM2)
+    bool gemm_ok = false;
+    unsigned long long timeout_ns = 2000ull * 1000 * 1000;
+    int stall = 0;               // test hook: GEMM kernels wait on a dead barrier
+    int nsm = 148;
+    int* err_host = nullptr;     // pinned copy of the device error word
     int grid1_bf16 = 0, grid1_f32 = 0, grid2 = 0;
     cudaStream_t last_stream = nullptr;
     // profiling: event pairs per phase, launch counters
@@ -183,9 +197,20 @@ static void free_ctx(hf_moe_ctx* c) {
     }
     for (auto e : c->ev_pool) cudaEventDestroy(e);
     void* bufs[] = {c->logits, c->ids, c->w, c->margins, c->plan, c->perm, c->slot_pos,
-                    c->masks, c->blk_counts, c->mid, c->y, c->x_dev, c->out_dev};
+                    c->masks, c->blk_counts, c->mid, c->y, c->x_dev, c->out_dev,
+                    c->mid_hi, c->mid_lo, c->xp_hi, c->xp_lo};
     for (void* p : bufs) cudaFree(p);
+    if (c->err_host) cudaFreeHost(c->err_host);
     delete c;
+}
+
+// Device error word (plan stats[3]) -> status; clears it.
+static hf_status take_error_word(hf_moe_ctx* c, int word) {
+    if (word == 0) return HF_OK;
+    HF_CUDA(cudaMemset(c->plan + c->pl.stats + 3, 0, sizeof(int)));
+    return fail(HF_ERR_TIMEOUT,
+                "a bounded device wait in the tcgen05 GEMM gave up; the kernel drained and "
+                "returned, outputs of that forward are invalid");
 }
 
 hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
@@ -260,11 +285,45 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     A(dalloc(&x->y, slots * x->H));
     A(dalloc(reinterpret_cast<float**>(&x->x_dev), T * x->H));
     A(dalloc(&x->out_dev, T * x->H));
+    x->gemm_ok = (x->H % 64 == 0) && (x->I % 64 == 0) && (x->Is % 64 == 0) &&
+                 x->cfg.path != HF_PATH_GEMV;
+    if (x->gemm_ok) {
+        A(dalloc(&x->mid_hi, slots * x->inter_max));
+        A(dalloc(&x->mid_lo, slots * x->inter_max));
+        A(dalloc(&x->xp_hi, slots * x->H));
+        A(dalloc(&x->xp_lo, slots * x->H));
+    }
     if (s != HF_OK) {
         std::string m = g_last_error;
         free_ctx(x);
         return fail(s, "hf_moe_create scratch: " + m);
     }
+    if (x->gemm_ok) {
+        // GEMM1 reads gathered activations (K = H); GEMM2 reads mid (K = I or Is).
+        auto M = [&](CUtensorMap* m, const void* b, int cols, int pitch) {
+            if (s == HF_OK) s = make_map_bf16(m, b, cols, slots, pitch, 16);
+        };
+        M(&x->maps1.B0, x->xp_hi, x->H, x->H);
+        M(&x->maps1.B1, x->xp_lo, x->H, x->H);
+        x->maps1.B0_sh = x->maps1.B0;
+        x->maps1.B1_sh = x->maps1.B1;
+        M(&x->maps2.B0, x->mid_hi, x->I, x->inter_max);
+        M(&x->maps2.B1, x->mid_lo, x->I, x->inter_max);
+        M(&x->maps2.B0_sh, x->mid_hi, x->Is > 0 ? x->Is : x->I, x->inter_max);
+        M(&x->maps2.B1_sh, x->mid_lo, x->Is > 0 ? x->Is : x->I, x->inter_max);
+        if (s != HF_OK) {
+            std::string m = g_last_error;
+            free_ctx(x);
+            return fail(s, "hf_moe_create tensor maps: " + m);
+        }
+    }
+    x->nsm = num_sms(c.device);
+    if (cudaMemset(x->plan, 0, sizeof(int32_t) * x->pl.words) != cudaSuccess ||
+        cudaMallocHost(reinterpret_cast<void**>(&x->err_host), 64) != cudaSuccess) {
+        free_ctx(x);
+        return fail(HF_ERR_CUDA, "hf_moe_create: plan/err buffer init failed");
+    }
+    *x->err_host = 0;
     x->grid1_bf16 = gemv_grid(c.device, true, false, x->H, x->inter_max);
     x->grid1_f32 = gemv_grid(c.device, true, true, x->H, x->inter_max);
     x->grid2 = gemv_grid(c.device, false, false, x->H, x->inter_max);
@@ -310,6 +369,20 @@ static hf_status layer_alloc(hf_moe_ctx* c, int layer) {
         w.pad = 0;
     }
     HF_CUDA(cudaMemcpy(L.groups, tab.data(), sizeof(GroupW) * c->G, cudaMemcpyHostToDevice));
+    if (c->gemm_ok) {
+        // one 2-D view per operand family covers every expert of the layer
+        const uint64_t el = uint64_t(c->E_local);
+        HF_TRY(make_map_bf16(&L.gu, L.experts, c->H, el * 3 * c->I, c->H, 128));
+        HF_TRY(make_map_bf16(&L.dn, L.experts, c->I, el * 3 * c->H, c->I, 128));
+        if (c->Is > 0) {
+            HF_TRY(make_map_bf16(&L.gu_sh, L.shared, c->H, 3ull * c->Is, c->H, 128));
+            HF_TRY(make_map_bf16(&L.dn_sh, L.shared, c->Is, 3ull * c->H, c->Is, 128));
+        } else {
+            L.gu_sh = L.gu;
+            L.dn_sh = L.dn;
+        }
+        L.maps = true;
+    }
     return HF_OK;
 }
 
@@ -441,8 +514,13 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
     ra.slot_pos = c->slot_pos;
     ra.masks = c->masks;
     ra.blk_counts = c->blk_counts;
-    ra.path = HF_PATH_GEMV;  // the tcgen05 grouped GEMM is not built yet
+    ra.path = c->cfg.path;
     ra.gemv_max = c->cfg.gemv_max_tokens;
+    ra.gemm_ok = c->gemm_ok && L.maps;
+    ra.gemm_bn = T <= 64 ? 64 : 128;
+    // segments can only exceed the GEMV threshold when T does
+    const bool maybe_gemm =
+        ra.gemm_ok && (c->cfg.path == HF_PATH_GEMM || T > c->cfg.gemv_max_tokens);
     {
         PhaseTimer p0(c, st, 0);
         HF_TRY(launch_router_logits(ra, st));
@@ -452,6 +530,21 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
         PhaseTimer p1(c, st, 1);
         int n = 0;
         HF_TRY(launch_route(ra, st, &n));
+        if (maybe_gemm && !route_only) {
+            GatherArgs gx{};
+            gx.plan = c->plan;
+            gx.pl = c->pl;
+            gx.perm = c->perm;
+            gx.x = x;
+            gx.T = T;
+            gx.k = k;
+            gx.H = c->H;
+            gx.device = c->cfg.device;
+            gx.xp_hi = c->xp_hi;
+            gx.xp_lo = c->xp_lo;
+            HF_TRY(launch_gather(gx, xd == HF_F32, st));
+            ++n;
+        }
         p1.done(n);
     }
     const size_t nslots = size_t(T) * k + (c->Is > 0 ? T : 0);
@@ -476,10 +569,42 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
             HF_TRY(launch_gemv1(ga, st));
             p2.done(1);
         }
+        GemmArgs gm{};
+        if (maybe_gemm) {
+            gm.plan = c->plan;
+            gm.pl = c->pl;
+            gm.which = 1;
+            gm.H = c->H;
+            gm.I = c->I;
+            gm.Is = c->Is;
+            gm.Imax = c->inter_max;
+            gm.bn = ra.gemm_bn;
+            gm.mid_hi = c->mid_hi;
+            gm.mid_lo = c->mid_lo;
+            gm.y = c->y;
+            gm.err = c->plan + c->pl.stats + 3;
+            gm.timeout_ns = c->timeout_ns;
+            gm.test_stall = c->stall;
+            GemmMaps m1 = c->maps1;
+            m1.A = L.gu;
+            m1.A_sh = L.gu_sh;
+            PhaseTimer p4(c, st, 4);
+            HF_TRY(launch_gemm(m1, gm, xd == HF_F32 ? 2 : 1, c->nsm, st));
+            p4.done(1);
+        }
         {
             PhaseTimer p3(c, st, 3);
             HF_TRY(launch_gemv2(ga, st));
             p3.done(1);
+        }
+        if (maybe_gemm) {
+            gm.which = 2;
+            GemmMaps m2 = c->maps2;
+            m2.A = L.dn;
+            m2.A_sh = L.dn_sh;
+            PhaseTimer p5(c, st, 5);
+            HF_TRY(launch_gemm(m2, gm, 2, c->nsm, st));
+            p5.done(1);
         }
         CombineArgs ca{};
         ca.y = c->y;
@@ -533,7 +658,30 @@ hf_status hf_moe_forward_host(hf_moe_ctx* ctx, int layer, const void* x_host, hf
     if (T > 0)
         HF_CUDA(cudaMemcpyAsync(out_host, ctx->out_dev, sizeof(float) * T * ctx->H,
                                 cudaMemcpyDeviceToHost, st));
+    HF_CUDA(cudaMemcpyAsync(ctx->err_host, ctx->plan + ctx->pl.stats + 3, sizeof(int),
+                            cudaMemcpyDeviceToHost, st));
     HF_CUDA(cudaStreamSynchronize(st));
+    return take_error_word(ctx, *ctx->err_host);
+}
+
+hf_status hf_moe_synchronize(hf_moe_ctx* ctx) {
+    if (!ctx) return fail(HF_ERR_ARG, "hf_moe_synchronize: null context");
+    DeviceGuard dg(ctx->cfg.device);
+    HF_CUDA(cudaStreamSynchronize(ctx->last_stream));
+    int word = 0;
+    HF_CUDA(cudaMemcpy(&word, ctx->plan + ctx->pl.stats + 3, sizeof(int), cudaMemcpyDeviceToHost));
+    return take_error_word(ctx, word);
+}
+
+hf_status hf_moe_set_wait_timeout(hf_moe_ctx* ctx, uint64_t ns) {
+    if (!ctx) return fail(HF_ERR_ARG, "hf_moe_set_wait_timeout: null context");
+    ctx->timeout_ns = ns ? ns : 2000ull * 1000 * 1000;
+    return HF_OK;
+}
+
+hf_status hf_moe_debug_stall(hf_moe_ctx* ctx, int enable) {
+    if (!ctx) return fail(HF_ERR_ARG, "hf_moe_debug_stall: null context");
+    ctx->stall = enable != 0;
     return HF_OK;
 }
 

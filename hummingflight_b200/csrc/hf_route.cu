@@ -277,6 +277,15 @@ __device__ int block_scan_excl(int* data, int n, int* warp_tot) {
     return total;
 }
 
+// Path of one expert segment: the grouped GEMV for short segments (AUTO) or
+// always (GEMV, or shapes the tcgen05 tiles do not cover); else the GEMM.
+__device__ __forceinline__ bool segment_uses_gemv(const RouteArgs& a, int c, int I) {
+    if (c <= 0 || I <= 0) return false;
+    if (!a.gemm_ok || a.path == HF_PATH_GEMV) return true;
+    if (a.path == HF_PATH_GEMM) return false;
+    return c <= a.gemv_max;
+}
+
 // From per-group counts (shared memory, s_cnt[G]) write counts, offsets, the
 // GEMV/GEMM work plan and the stats into the plan buffer. s_tmp: >= G+1 ints.
 __device__ void plan_from_counts(const RouteArgs& a, const int* s_cnt, int* s_tmp, int* warp_tot) {
@@ -293,23 +302,26 @@ __device__ void plan_from_counts(const RouteArgs& a, const int* s_cnt, int* s_tm
     for (int g = threadIdx.x; g < G; g += blockDim.x) plan[a.pl.offsets + g] = s_tmp[g];
     if (threadIdx.x == 0) plan[a.pl.offsets + G] = tot;
     __syncthreads();
-    // GEMV1 units
-    for (int pass = 0; pass < 3; ++pass) {
+    // work units: GEMV1, GEMV2 (per token chunk and row block), GEMM1, GEMM2
+    // (per 128-row tile and token tile)
+    for (int pass = 0; pass < 4; ++pass) {
         for (int g = threadIdx.x; g < G; g += blockDim.x) {
             const int c = s_cnt[g];
             const int I = (g == G - 1) ? a.shared_inter : a.inter;
-            const bool gemv = c > 0 && I > 0 &&
-                              (a.path == HF_PATH_GEMV || (a.path == HF_PATH_AUTO && c <= a.gemv_max));
+            const bool gemv = segment_uses_gemv(a, c, I);
+            const bool gemm = c > 0 && I > 0 && !gemv;
             const int nch = (c + kGemvTE - 1) / kGemvTE;
+            const int nt = gemm ? (c + a.gemm_bn - 1) / a.gemm_bn : 0;
             int v = 0;
             if (pass == 0) v = gemv ? nch * ((I + kGemv1Rows - 1) / kGemv1Rows) : 0;
             if (pass == 1) v = gemv ? nch * ((H + kGemv2Rows - 1) / kGemv2Rows) : 0;
-            if (pass == 2) v = (!gemv && c > 0 && I > 0) ? 1 : 0;
+            if (pass == 2) v = nt * ((I + 127) / 128);
+            if (pass == 3) v = nt * ((H + 127) / 128);
             s_tmp[g] = v;
         }
         __syncthreads();
         tot = block_scan_excl(s_tmp, G, warp_tot);
-        const int dst = pass == 0 ? a.pl.u1 : (pass == 1 ? a.pl.u2 : a.pl.gemm_seg);
+        const int dst = pass == 0 ? a.pl.u1 : pass == 1 ? a.pl.u2 : pass == 2 ? a.pl.g1 : a.pl.g2;
         for (int g = threadIdx.x; g < G; g += blockDim.x) plan[dst + g] = s_tmp[g];
         if (threadIdx.x == 0) plan[dst + G] = tot;
         __syncthreads();
@@ -321,8 +333,7 @@ __device__ void plan_from_counts(const RouteArgs& a, const int* s_cnt, int* s_tm
             const int c = s_cnt[g];
             const int I = (g == G - 1) ? a.shared_inter : a.inter;
             if (c > 0 && g < G - 1) ++act;
-            const bool gemv = c > 0 && I > 0 &&
-                              (a.path == HF_PATH_GEMV || (a.path == HF_PATH_AUTO && c <= a.gemv_max));
+            const bool gemv = segment_uses_gemv(a, c, I);
             if (gemv) ++gv;
             else if (c > 0 && I > 0) ++gm;
         }

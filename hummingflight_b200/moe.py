@@ -183,6 +183,18 @@ class MoELayer:
         call("hf_moe_layer", self._h, layer, inp.ctypes.data, output.ctypes.data)
         return output
 
+    def synchronize(self):
+        """Wait for the last forward; raises HfError(HF_ERR_TIMEOUT) when a
+        bounded device wait gave up in one of the forwards since the last check."""
+        call("hf_moe_synchronize", self._h)
+
+    def set_wait_timeout(self, ns: int):
+        call("hf_moe_set_wait_timeout", self._h, ns)
+
+    def debug_stall(self, enable: bool):
+        """Test hook: tensor-core kernels wait on a barrier nothing signals."""
+        call("hf_moe_debug_stall", self._h, int(enable))
+
     def last_stats(self):
         a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
         call("hf_moe_last_stats", self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))

@@ -149,6 +149,21 @@ HF_API hf_status hf_moe_layer(hf_moe_ctx* ctx, int layer, const float* input, fl
 HF_API hf_status hf_moe_route(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_dtype, int T,
                        const hf_moe_routing* routing, hf_stream stream);
 
+/* Waits for the context's last stream and reports device-side failures of
+ * the forwards since the previous check: HF_ERR_TIMEOUT when a bounded wait
+ * inside a kernel gave up (the kernel drained, freed its tensor memory and
+ * returned; the outputs of that forward are invalid, the context stays
+ * usable). hf_moe_forward_host and hf_moe_layer check this themselves. */
+HF_API hf_status hf_moe_synchronize(hf_moe_ctx* ctx);
+/* Limit of every bounded device wait, in nanoseconds (default 2 s, 0 restores
+ * it). Tests shorten it to make a wait run out on purpose. */
+HF_API hf_status hf_moe_set_wait_timeout(hf_moe_ctx* ctx, uint64_t ns);
+/* Test hook (failure detection without a GPU fault): while enabled, the
+ * tensor-core kernels first wait on a barrier that nothing signals, so their
+ * bounded wait runs out after the wait timeout and hf_moe_synchronize reports
+ * HF_ERR_TIMEOUT. No counterpart in the reference, which has no device waits. */
+HF_API hf_status hf_moe_debug_stall(hf_moe_ctx* ctx, int enable);
+
 /* Statistics of the most recent forward/route on this context (waits for it):
  * experts with at least one token, and segments on each expert path. */
 HF_API hf_status hf_moe_last_stats(hf_moe_ctx* ctx, int* active_experts, int* gemv_segments,
