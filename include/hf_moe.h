@@ -164,6 +164,26 @@ HF_API hf_status hf_moe_set_wait_timeout(hf_moe_ctx* ctx, uint64_t ns);
  * HF_ERR_TIMEOUT. No counterpart in the reference, which has no device waits. */
 HF_API hf_status hf_moe_debug_stall(hf_moe_ctx* ctx, int enable);
 
+/* Routing (router GEMV, sigmoid, bias, top-k, permutation) that allocates no
+ * device memory, for callers that cannot call cudaMalloc: an engine whose
+ * resident expert weights already hold the whole device, or a decode loop
+ * that must not take the device-wide synchronization an allocation can
+ * imply. No counterpart in the reference. Same kernels and outputs as
+ * hf_moe_route, with no context: router [E x H] BF16, bias [E] or NULL, x
+ * [T x H]; writes topk_ids/topk_weights [T*min(k,E)], counts [E+1], offsets
+ * [E+2], perm [T*min(k,E) + T] (shared slots included when has_shared).
+ * Scratch is a fixed array inside the library, one per device, kept until
+ * the process exits: T <= 128, E <= 256, k <= 8, else HF_ERR_ARG. The first
+ * call on a device looks the array up, so make it before any stream capture.
+ * Calls that can overlap on the GPU share the array and race; calls ordered
+ * on one stream do not. */
+HF_API hf_status hf_moe_route_noalloc(const uint16_t* router_bf16, const float* bias,
+                                      const void* x, hf_dtype x_dtype, int T, int H, int E,
+                                      int top_k, float routed_scaling_factor, int norm_topk_prob,
+                                      int has_shared, int32_t* topk_ids, float* topk_weights,
+                                      int32_t* counts, int32_t* offsets, int32_t* perm,
+                                      hf_stream stream);
+
 /* Statistics of the most recent forward/route on this context (waits for it):
  * experts with at least one token, and segments on each expert path. */
 HF_API hf_status hf_moe_last_stats(hf_moe_ctx* ctx, int* active_experts, int* gemv_segments,
