@@ -97,24 +97,37 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
-def phase_bytes(shape, counts, T, k):
-    """Algorithmic HBM bytes of each phase from the routing of one forward."""
+def phase_bytes(shape, counts, T, k, path, gemv_max):
+    """Algorithmic HBM bytes (and useful flops) of each phase from the routing
+    of one forward: every active expert's weights once, activations and
+    intermediates once, split by the path each expert segment takes."""
     H, I, Is, E = shape.hidden, shape.inter, shape.shared_inter, shape.num_experts
-    routed = counts[:E]
-    active = int((routed > 0).sum())
-    has_sh = Is > 0 and counts[E] > 0
-    n_slots = int(routed.sum()) + (int(counts[E]) if has_sh else 0)
-    w_gu = active * 2 * I * H * 2 + (2 * Is * H * 2 if has_sh else 0)
-    w_d = active * H * I * 2 + (H * Is * 2 if has_sh else 0)
-    mid = int(routed.sum()) * I * 4 + (int(counts[E]) * Is * 4 if has_sh else 0)
-    return {
-        "router": E * H * 2 + T * H * 2 + T * E * 4,
-        "gemv_gate_up": w_gu + T * H * 2 + mid,
-        "gemv_down": w_d + mid + n_slots * H * 4,
-        "combine": n_slots * H * 4 + T * H * 4 + T * k * 8,
-        "active": active,
-        "total_weights": E * H * 2 + w_gu + w_d,
-    }
+    inter = np.array([I] * E + [Is], np.int64)
+    c = counts.astype(np.int64).copy()
+    if Is == 0:
+        c[E] = 0
+    live = (c > 0) & (inter > 0)
+    if path == "gemv":
+        on_gemv = live
+    elif path == "gemm":
+        on_gemv = np.zeros_like(live)
+    else:
+        on_gemv = live & (c <= gemv_max)
+    out = {"active": int((c[:E] > 0).sum())}
+    for name, sel in (("gemv", on_gemv), ("gemm", live & ~on_gemv)):
+        w_gu = int((2 * inter[sel] * H * 2).sum())
+        w_d = int((H * inter[sel] * 2).sum())
+        slots = int(c[sel].sum())
+        mid_b = int((c[sel] * inter[sel]).sum()) * 4  # fp32 (GEMV) or BF16 hi + lo (GEMM)
+        out[f"{name}_gate_up"] = w_gu + slots * H * 2 + mid_b
+        out[f"{name}_down"] = w_d + mid_b + slots * H * 4
+        out[f"{name}_gate_up_flops"] = int((2 * 2 * c[sel] * inter[sel] * H).sum())
+        out[f"{name}_down_flops"] = int((2 * c[sel] * inter[sel] * H).sum())
+    n_slots = int(c.sum())
+    out["router"] = E * H * 2 + T * H * 2 + T * E * 4
+    out["combine"] = n_slots * H * 4 + T * H * 4 + T * k * 8
+    out["total_weights"] = E * H * 2 + int((3 * inter[live] * H * 2).sum())
+    return out
 
 
 # ---------------------------------------------------------------- reference arm (CPU)
@@ -196,16 +209,21 @@ def main():
     ap.add_argument("--experts", type=int, default=0,
                     help="profiling case: fewer routed experts (same per-expert shape)")
     ap.add_argument("--tokens", type=int, default=0, help="profiling case: override T")
+    ap.add_argument("--inter", type=int, default=0,
+                    help="profiling case: override the (routed and shared) intermediate size")
     ap.add_argument("--gemv-max", type=int, default=0,
                     help="AUTO path: segments up to this many tokens use the GEMV (0 = default)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     wl = WORKLOADS[args.config]
-    if args.experts or args.tokens:
+    if args.experts or args.tokens or args.inter:
         from dataclasses import replace
-        shape = replace(wl.shape, num_experts=args.experts or wl.shape.num_experts)
+        shape = replace(wl.shape, num_experts=args.experts or wl.shape.num_experts,
+                        inter=args.inter or wl.shape.inter,
+                        shared_inter=args.inter or wl.shape.shared_inter)
         wl = replace(wl, shape=shape, tokens=args.tokens or wl.tokens,
-                     name=f"{wl.name}_E{shape.num_experts}_T{args.tokens or wl.tokens}")
+                     name=f"{wl.name}_E{shape.num_experts}_T{args.tokens or wl.tokens}"
+                          f"_I{shape.inter}")
     if args.impl == "reference":
         run_reference(args, wl)
         return
@@ -296,14 +314,21 @@ def main():
         e2e_ms = float(t.item())
 
     if rank == 0:
-        hbm, _, peak_kind = peaks()
-        pb = phase_bytes(shape, counts, T, L.k)
+        hbm, tflops_peak, peak_kind = peaks()
+        gemv_max = args.gemv_max or 1
+        pb = phase_bytes(shape, counts, T, L.k, args.path, gemv_max)
         dom = max(("gemv_gate_up", "gemv_down", "router", "route", "combine",
                    "gemm_gate_up", "gemm_down"), key=lambda p: prof[p][0])
         dom_ms, dom_n = prof[dom]
         per_launch_ms = dom_ms / max(1, dom_n)
         alg = pb.get(dom)
-        achieved = alg / (per_launch_ms / 1e3) / 1e9 if alg else None
+        flops = pb.get(dom + "_flops")
+        # prefill-sized segments are tensor-bound; decode streams weights (HBM-bound)
+        tensor_bound = bool(flops) and flops / max(1, alg) > 0.5 * 1e3 * tflops_peak / hbm
+        if tensor_bound:
+            achieved = flops / (per_launch_ms / 1e3) / 1e12
+        else:
+            achieved = alg / (per_launch_ms / 1e3) / 1e9 if alg else None
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
@@ -329,10 +354,15 @@ def main():
             "layer_hbm_gbs": layer_bytes * wl.layers / (ms / 1e3) / 1e9,
             "layer_tflops": layer_flops(shape, T) * wl.layers / (ms / 1e3) / 1e12,
             "phases_ms_per_step": {p: v[0] / args.steps for p, v in prof.items() if v[1]},
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
-                         "unit": "GB/s", "frac": (achieved / hbm) if achieved else None,
+            "roofline": {"bound": "tensor" if tensor_bound else "hbm", "kernel": dom,
+                         "achieved": achieved,
+                         "peak": tflops_peak if tensor_bound else hbm,
+                         "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                         "frac": (achieved / (tflops_peak if tensor_bound else hbm))
+                         if achieved else None,
                          "peak_kind": peak_kind, "traffic": traffic,
                          "algorithmic_bytes_per_launch": alg,
+                         "algorithmic_flops_per_launch": flops,
                          "launch_ms": per_launch_ms},
             "clocks": clocks,
         }

@@ -40,7 +40,7 @@ template <int NUM_A, int NUM_B, int BN>
 struct GemmCfg {
     static constexpr int kStageBytes = NUM_A * kTileABytes + NUM_B * BN * 128;
     static constexpr int kStages0 = (220 * 1024) / kStageBytes;
-    static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
+    static constexpr int kStages = kStages0 > 12 ? 12 : kStages0;
     static constexpr int kAccCols = NUM_A * BN;
     static constexpr int kCols0 = 2 * kAccCols;
     static constexpr uint32_t kTmemCols = kCols0 <= 32 ? 32 : kCols0 <= 64 ? 64 : kCols0 <= 128 ? 128
@@ -57,17 +57,25 @@ struct TileInfo {
     bool shared;
 };
 
-__device__ __forceinline__ void decode_tile(const GemmArgs& a, int u, TileInfo& t) {
+// The three plan arrays a tile decode reads (tile prefix, counts, offsets),
+// staged in shared memory at kernel start when they fit, else read in place.
+struct PlanView {
+    const int32_t* pref;
+    const int32_t* cnt;
+    const int32_t* off;
+};
+
+__device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p, int u,
+                                            TileInfo& t) {
     const int G = a.pl.G;
-    const int32_t* pref = a.plan + (a.which == 1 ? a.pl.g1 : a.pl.g2);
-    const int g = find_group(pref, G, u);
-    const int c = a.plan[a.pl.counts + g];
+    const int g = find_group(p.pref, G, u);
+    const int c = p.cnt[g];
     const int nt = (c + a.bn - 1) / a.bn;
-    const int local = u - pref[g];
+    const int local = u - p.pref[g];
     const int mi = local / nt, ni = local % nt;
     t.shared = (g == G - 1);
     const int Ig = t.shared ? a.Is : a.I;
-    t.seg = a.plan[a.pl.offsets + g];
+    t.seg = p.off[g];
     t.n0 = ni * a.bn;
     t.n = min(a.bn, c - t.n0);
     t.m0 = mi * 128;
@@ -114,7 +122,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint64_t deadline = globaltimer() + a.timeout_ns;
-    const int total = a.plan[(a.which == 1 ? a.pl.g1 : a.pl.g2) + a.pl.G];
+    const int G = a.pl.G;
+    const int32_t* pref_g = a.plan + (a.which == 1 ? a.pl.g1 : a.pl.g2);
+    const int total = pref_g[G];
+    PlanView pv{pref_g, a.plan + a.pl.counts, a.plan + a.pl.offsets};
+    if (a.plan_smem) {
+        int32_t* sp = reinterpret_cast<int32_t*>(smem + C::kBarOff + 256);
+        for (int i = threadIdx.x; i <= G; i += blockDim.x) sp[i] = pref_g[i];
+        for (int i = threadIdx.x; i < G; i += blockDim.x) {
+            sp[G + 1 + i] = a.plan[a.pl.counts + i];
+            sp[2 * G + 1 + i] = a.plan[a.pl.offsets + i];
+        }
+        pv = PlanView{sp, sp + G + 1, sp + 2 * G + 1};
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -147,7 +167,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         bool ok = true;
         for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
             TileInfo t;
-            decode_tile(a, u, t);
+            decode_tile(a, pv, u, t);
             const int nb = (t.n + kBoxRowsB - 1) / kBoxRowsB;
             const uint32_t bytes = NUM_A * kTileABytes + NUM_B * nb * (kBoxRowsB * 128);
             const CUtensorMap* mA = t.shared ? &tmA_sh : &tmA;
@@ -184,7 +204,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (a.test_stall) ok = mbar_wait(stall_bar, 0, abort_flag, deadline);
         for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lt) {
             TileInfo t;
-            decode_tile(a, u, t);
+            decode_tile(a, pv, u, t);
             const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
             if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, deadline)) {
                 ok = false;
@@ -229,7 +249,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint32_t lt = 0;
         for (int u = blockIdx.x; u < total; u += gridDim.x, ++lt) {
             TileInfo t;
-            decode_tile(a, u, t);
+            decode_tile(a, pv, u, t);
             const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
             if (!mbar_wait(&tfull[acc], aph, abort_flag, deadline)) break;
             tc_fence_after();
@@ -321,19 +341,27 @@ template <int NUM_A, int NUM_B, int BN>
 static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cudaStream_t st) {
     using C = GemmCfg<NUM_A, NUM_B, BN>;
     auto kern = k_moe_gemm<NUM_A, NUM_B, BN>;
-    HF_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    kern<<<grid, kGemmThreads, C::kSmem, st>>>(m.A, m.A_sh, m.B0, m.B1, m.B0_sh, m.B1_sh, a);
+    GemmArgs args = a;
+    const int plan_bytes = ((3 * a.pl.G + 1) * 4 + 15) & ~15;
+    int smem = C::kSmem;
+    args.plan_smem = (C::kSmem + plan_bytes) <= 227 * 1024;
+    if (args.plan_smem) smem += plan_bytes;
+    HF_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, kGemmThreads, smem, st>>>(m.A, m.A_sh, m.B0, m.B1, m.B0_sh, m.B1_sh, args);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }
 
 hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid, cudaStream_t st) {
     if (a.which == 1) {
+        if (a.bn == 32) return num_b == 1 ? launch_one<2, 1, 32>(m, a, grid, st)
+                                          : launch_one<2, 2, 32>(m, a, grid, st);
         if (a.bn == 64) return num_b == 1 ? launch_one<2, 1, 64>(m, a, grid, st)
                                           : launch_one<2, 2, 64>(m, a, grid, st);
         if (a.bn == 128) return num_b == 1 ? launch_one<2, 1, 128>(m, a, grid, st)
                                            : launch_one<2, 2, 128>(m, a, grid, st);
     } else {
+        if (a.bn == 32) return launch_one<1, 2, 32>(m, a, grid, st);
         if (a.bn == 64) return launch_one<1, 2, 64>(m, a, grid, st);
         if (a.bn == 128) return launch_one<1, 2, 128>(m, a, grid, st);
     }
@@ -387,12 +415,5 @@ hf_status make_map_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_
     return HF_OK;
 }
 
-int gemm_smem_bytes(int which, int num_b, int bn) {
-    if (which == 1) {
-        if (bn == 64) return num_b == 1 ? GemmCfg<2, 1, 64>::kSmem : GemmCfg<2, 2, 64>::kSmem;
-        return num_b == 1 ? GemmCfg<2, 1, 128>::kSmem : GemmCfg<2, 2, 128>::kSmem;
-    }
-    return bn == 64 ? GemmCfg<1, 2, 64>::kSmem : GemmCfg<1, 2, 128>::kSmem;
-}
 
 }  // namespace hf

@@ -113,17 +113,22 @@ __global__ void __launch_bounds__(256) k_gemv1(GemvArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     void* xs = smem_raw;
     const int G = a.pl.G;
-    const int32_t* u1 = a.plan + a.pl.u1;
+    const int H = a.H;
+    int32_t* sp = reinterpret_cast<int32_t*>(smem_raw + size_t(kGemvTE) * H * (XF32 ? 4 : 2));
+    stage_plan(sp, a.plan + a.pl.u1, a.plan, a.pl);
+    __syncthreads();
+    const int32_t* u1 = sp;
+    const int32_t* cnts = sp + G + 1;
+    const int32_t* offs = sp + 2 * G + 1;
     const int total = u1[G];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int H = a.H;
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
         const int g = find_group(u1, G, u);
-        const int cnt = a.plan[a.pl.counts + g];
+        const int cnt = cnts[g];
         const int nch = (cnt + kGemvTE - 1) / kGemvTE;
         const int local = u - u1[g];
         const int rb = local / nch, ch = local % nch;
-        const int p0 = a.plan[a.pl.offsets + g] + ch * kGemvTE;
+        const int p0 = offs[g] + ch * kGemvTE;
         const int te = min(kGemvTE, cnt - ch * kGemvTE);
         __syncthreads();
         // stage the chunk's activation rows: te x H elements, 16 bytes per thread-step
@@ -218,17 +223,22 @@ __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float* ms = reinterpret_cast<float*>(smem_raw);
     const int G = a.pl.G;
-    const int32_t* u2 = a.plan + a.pl.u2;
+    int32_t* sp = reinterpret_cast<int32_t*>(smem_raw + size_t(kGemvTE) * a.inter_max * 4);
+    stage_plan(sp, a.plan + a.pl.u2, a.plan, a.pl);
+    __syncthreads();
+    const int32_t* u2 = sp;
+    const int32_t* cnts = sp + G + 1;
+    const int32_t* offs = sp + 2 * G + 1;
     const int total = u2[G];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = a.H;
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
         const int g = find_group(u2, G, u);
-        const int cnt = a.plan[a.pl.counts + g];
+        const int cnt = cnts[g];
         const int nch = (cnt + kGemvTE - 1) / kGemvTE;
         const int local = u - u2[g];
         const int rb = local / nch, ch = local % nch;
-        const int p0 = a.plan[a.pl.offsets + g] + ch * kGemvTE;
+        const int p0 = offs[g] + ch * kGemvTE;
         const int te = min(kGemvTE, cnt - ch * kGemvTE);
         const GroupW W = a.groups[g];
         const int I = W.inter;
@@ -250,11 +260,15 @@ __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
     }
 }
 
-size_t gemv1_smem(int H, bool xf32) { return size_t(kGemvTE) * H * (xf32 ? 4 : 2); }
-size_t gemv2_smem(int inter_max) { return size_t(kGemvTE) * inter_max * 4; }
+size_t gemv1_smem(int H, bool xf32, int G) {
+    return size_t(kGemvTE) * H * (xf32 ? 4 : 2) + plan_smem_bytes(G);
+}
+size_t gemv2_smem(int inter_max, int G) {
+    return size_t(kGemvTE) * inter_max * 4 + plan_smem_bytes(G);
+}
 
 hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st) {
-    const size_t s1 = gemv1_smem(a.H, a.x_f32 != 0);
+    const size_t s1 = gemv1_smem(a.H, a.x_f32 != 0, a.pl.G);
     if (a.x_f32) {
         HF_CUDA(cudaFuncSetAttribute(k_gemv1<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)s1));
@@ -269,22 +283,22 @@ hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st) {
 }
 
 hf_status launch_gemv2(const GemvArgs& a, cudaStream_t st) {
-    const size_t s2 = gemv2_smem(a.inter_max);
+    const size_t s2 = gemv2_smem(a.inter_max, a.pl.G);
     HF_CUDA(cudaFuncSetAttribute(k_gemv2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2));
     k_gemv2<<<a.grid2, 256, s2, st>>>(a);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }
 
-int gemv_grid(int device, bool first, bool xf32, int H, int inter_max) {
+int gemv_grid(int device, bool first, bool xf32, int H, int inter_max, int G) {
     int per_sm = 1;
     if (first) {
-        const size_t s = gemv1_smem(H, xf32);
+        const size_t s = gemv1_smem(H, xf32, G);
         auto kern = xf32 ? k_gemv1<true> : k_gemv1<false>;
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, s);
     } else {
-        const size_t s = gemv2_smem(inter_max);
+        const size_t s = gemv2_smem(inter_max, G);
         cudaFuncSetAttribute(k_gemv2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv2, 256, s);
     }

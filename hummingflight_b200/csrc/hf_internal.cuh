@@ -37,7 +37,7 @@ constexpr int kSmallRouteT = 128;  // single-CTA routing up to this many tokens
 constexpr int kGemvTE = 4;         // tokens per grouped-GEMV chunk
 constexpr int kGemv1Rows = 16;     // gate/up rows per GEMV1 unit (8 warps x 2)
 constexpr int kGemv2Rows = 32;     // down rows per GEMV2 unit (8 warps x 4)
-constexpr int kGemvDefaultMax = 16;// AUTO: segments <= this many tokens use the GEMV
+constexpr int kGemvDefaultMax = 1; // AUTO: segments <= this many tokens use the GEMV
 
 // Weights of one expert group (routed expert or the shared expert).
 struct GroupW {
@@ -157,6 +157,23 @@ __device__ __forceinline__ int token_of_slot(int slot, int T, int k) {
     return slot < T * k ? slot / k : slot - T * k;
 }
 
+// Copies a unit/tile prefix [G+1], counts [G] and offsets [G] of the plan into
+// shared memory (3G+1 words at sp), so per-unit lookups do not chain global
+// loads. The caller synchronizes the block before use.
+__device__ __forceinline__ void stage_plan(int32_t* sp, const int32_t* prefix, const int32_t* plan,
+                                           const PlanLayout& pl) {
+    const int G = pl.G;
+    for (int i = threadIdx.x; i <= G; i += blockDim.x) sp[i] = prefix[i];
+    for (int i = threadIdx.x; i < G; i += blockDim.x) {
+        sp[G + 1 + i] = plan[pl.counts + i];
+        sp[2 * G + 1 + i] = plan[pl.offsets + i];
+    }
+}
+
+__host__ __device__ __forceinline__ size_t plan_smem_bytes(int G) {
+    return (size_t(3 * G + 1) * 4 + 15) & ~size_t(15);
+}
+
 // Largest g with prefix[g] <= u (prefix non-decreasing, prefix[0] = 0).
 __device__ __forceinline__ int find_group(const int32_t* prefix, int G, int u) {
     int lo = 0, hi = G - 1;
@@ -193,9 +210,9 @@ struct GemvArgs {
 hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st);
 hf_status launch_gemv2(const GemvArgs& a, cudaStream_t st);
 // Persistent grid (SM count x resident blocks) of GEMV1 (first) or GEMV2.
-int gemv_grid(int device, bool first, bool xf32, int H, int inter_max);
-size_t gemv1_smem(int H, bool xf32);
-size_t gemv2_smem(int inter_max);
+int gemv_grid(int device, bool first, bool xf32, int H, int inter_max, int G);
+size_t gemv1_smem(int H, bool xf32, int G);
+size_t gemv2_smem(int inter_max, int G);
 
 // tcgen05 grouped GEMM (hf_gemm.cu).
 struct GemmArgs {
@@ -209,6 +226,7 @@ struct GemmArgs {
     int* err;               // error word (plan stats[3])
     unsigned long long timeout_ns;
     int test_stall;         // wait on a barrier nothing signals (test hook)
+    int plan_smem;          // set by the launcher: plan arrays staged in shared memory
 };
 struct GemmMaps {
     CUtensorMap A, A_sh;       // weights (routed view, shared expert view)
@@ -228,7 +246,6 @@ hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid,
 hf_status launch_gather(const GatherArgs& a, int x_f32, cudaStream_t st);
 hf_status make_map_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows,
                         uint64_t pitch, uint32_t box_rows);
-int gemm_smem_bytes(int which, int num_b, int bn);
 
 // Device generator (hf_synth.cu).
 hf_status synth_bf16(uint16_t* dst, uint64_t n, uint64_t key, float scale, cudaStream_t st);

@@ -8,6 +8,7 @@
 // caller's stream.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -108,6 +109,7 @@ struct hf_moe_ctx {
     bool gemm_ok = false;
     unsigned long long timeout_ns = 2000ull * 1000 * 1000;
     int stall = 0;               // test hook: GEMM kernels wait on a dead barrier
+    int gemm_bn = 0;             // GEMM token tile override (HF_GEMM_BN: 32, 64, 128)
     int nsm = 148;
     int* err_host = nullptr;     // pinned copy of the device error word
     int grid1_bf16 = 0, grid1_f32 = 0, grid2 = 0;
@@ -262,7 +264,11 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     x->pl = PlanLayout::make(x->G);
     x->T_max = c.max_tokens;
     if (x->cfg.gemv_max_tokens <= 0) x->cfg.gemv_max_tokens = kGemvDefaultMax;
-    if (gemv1_smem(x->H, true) > 227 * 1024 || gemv2_smem(x->inter_max) > 227 * 1024) {
+    if (const char* bn = std::getenv("HF_GEMM_BN")) {  // tuning knob
+        const int v = std::atoi(bn);
+        x->gemm_bn = (v == 32 || v == 64 || v == 128) ? v : 0;
+    }
+    if (gemv1_smem(x->H, true, x->G) > 227 * 1024 || gemv2_smem(x->inter_max, x->G) > 227 * 1024) {
         free_ctx(x);
         return fail(HF_ERR_ARG, "hidden/intermediate size too large for the GEMV staging");
     }
@@ -324,9 +330,9 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
         return fail(HF_ERR_CUDA, "hf_moe_create: plan/err buffer init failed");
     }
     *x->err_host = 0;
-    x->grid1_bf16 = gemv_grid(c.device, true, false, x->H, x->inter_max);
-    x->grid1_f32 = gemv_grid(c.device, true, true, x->H, x->inter_max);
-    x->grid2 = gemv_grid(c.device, false, false, x->H, x->inter_max);
+    x->grid1_bf16 = gemv_grid(c.device, true, false, x->H, x->inter_max, x->G);
+    x->grid1_f32 = gemv_grid(c.device, true, true, x->H, x->inter_max, x->G);
+    x->grid2 = gemv_grid(c.device, false, false, x->H, x->inter_max, x->G);
     *out = x;
     return HF_OK;
 }
@@ -517,7 +523,8 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
     ra.path = c->cfg.path;
     ra.gemv_max = c->cfg.gemv_max_tokens;
     ra.gemm_ok = c->gemm_ok && L.maps;
-    ra.gemm_bn = T <= 64 ? 64 : 128;
+    // decode: narrow token tiles leave room for a deeper weight ring
+    ra.gemm_bn = c->gemm_bn ? c->gemm_bn : (T <= 64 ? 32 : 128);
     // segments can only exceed the GEMV threshold when T does
     const bool maybe_gemm =
         ra.gemm_ok && (c->cfg.path == HF_PATH_GEMM || T > c->cfg.gemv_max_tokens);

@@ -17,13 +17,15 @@
 namespace hf {
 
 // ============================================================ router logits
-// Small T: block = 2 router rows x 4 K-slices (8 warps). Each lane keeps up to
-// 8 16-byte chunks of its row slice in registers and applies them to every
-// token, so the 3 MB router weight is read from HBM once.
-constexpr int kRouterRowsPerBlock = 2;
-constexpr int kRouterSlices = 4;
+// Small T: one block per router row, its 8 warps each own one K-slice. A lane
+// keeps up to 4 16-byte chunks of its slice in registers and applies them to
+// the tokens 8 at a time (24-32 activation loads in flight per lane), so the
+// 3 MB router weight is read from HBM once and token latency overlaps.
+constexpr int kRouterRowsPerBlock = 1;
+constexpr int kRouterSlices = 8;
 constexpr int kRouterMaxT = 64;
-constexpr int kRouterRegChunks = 8;
+constexpr int kRouterRegChunks = 4;
+constexpr int kRouterTokBatch = 8;
 
 template <bool XF32>
 __device__ __forceinline__ void load_x8(const void* x, size_t elem, float (&o)[8]) {
@@ -60,21 +62,37 @@ __global__ void __launch_bounds__(256) k_router_gemv(RouteArgs a) {
                 const int c = cb + lane + 32 * j;
                 wv[j] = (c < c1) ? ld_stream_u4(wrow + size_t(c) * 8) : make_uint4(0, 0, 0, 0);
             }
-            for (int t = 0; t < T; ++t) {
-                float acc = 0.0f;
+            // blocks start at different tokens so they do not all request the
+            // same activation lines from L2 at the same time
+            const int nbatch = (T + kRouterTokBatch - 1) / kRouterTokBatch;
+            const int rot = int(blockIdx.x % unsigned(nbatch));
+            for (int bi = 0; bi < nbatch; ++bi) {
+                const int t0 = ((bi + rot) % nbatch) * kRouterTokBatch;
+                float acc[kRouterTokBatch];
+#pragma unroll
+                for (int b = 0; b < kRouterTokBatch; ++b) acc[b] = 0.0f;
 #pragma unroll
                 for (int j = 0; j < kRouterRegChunks; ++j) {
                     const int c = cb + lane + 32 * j;
                     if (c < c1) {
-                        float xf[8], wf[8];
-                        load_x8<XF32>(a.x, size_t(t) * H + size_t(c) * 8, xf);
+                        float wf[8];
                         unpack8(wv[j], wf);
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) acc = fmaf(wf[q], xf[q], acc);
+                        for (int b = 0; b < kRouterTokBatch; ++b) {
+                            if (t0 + b < T) {
+                                float xf[8];
+                                load_x8<XF32>(a.x, size_t(t0 + b) * H + size_t(c) * 8, xf);
+#pragma unroll
+                                for (int q = 0; q < 8; ++q) acc[b] = fmaf(wf[q], xf[q], acc[b]);
+                            }
+                        }
                     }
                 }
-                acc = warp_sum(acc);
-                if (lane == 0) P[t] += acc;
+#pragma unroll
+                for (int b = 0; b < kRouterTokBatch; ++b) {
+                    const float s = warp_sum(acc[b]);
+                    if (lane == 0 && t0 + b < T) P[t0 + b] += s;
+                }
             }
         }
     }
