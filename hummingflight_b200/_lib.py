@@ -59,6 +59,8 @@ SIGNATURES = {
     "hf_moe_forward_host": (c_int, [c_vp, c_int, c_vp, c_int, c_int, c_vp, c_vp]),
     "hf_moe_layer": (c_int, [c_vp, c_int, c_vp, c_vp]),
     "hf_moe_route": (c_int, [c_vp, c_int, c_vp, c_int, c_int, ctypes.POINTER(HfMoeRouting), c_vp]),
+    "hf_ep_unique_id": (c_int, [c_vp]),
+    "hf_ep_plan": (c_int, [c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "hf_moe_route_noalloc": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float,
                                      c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "hf_moe_last_stats": (c_int, [c_vp, ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),

@@ -1,0 +1,179 @@
+// hf_ctx.cuh -- the MoE context shared by hf_moe.cu (single device) and
+// hf_ep.cu (expert parallelism over NCCL).
+#pragma once
+
+#include <string>
+#include <vector>
+
+#include "hf_internal.cuh"
+
+struct ncclComm;
+
+namespace hf {
+
+// Makes the context's device current for one API call and restores the
+// caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+struct LayerBuf {
+    uint16_t* router = nullptr;  // [E x H] (global router on every rank)
+    float* bias = nullptr;       // [E]
+    bool has_bias = false;
+    uint16_t* experts = nullptr; // [E_local][gate|up|down]
+    uint16_t* shared = nullptr;  // [gate|up|down] of the shared expert
+    GroupW* groups = nullptr;    // [G] device table: local experts, then shared
+    bool loaded = false;
+    // TMA views of the weights for the tcgen05 GEMM (built with the buffers)
+    CUtensorMap gu{}, gu_sh{};   // gate/up rows: H-wide rows of [gate|up|down]
+    CUtensorMap dn{}, dn_sh{};   // down rows: I-wide rows of the same buffers
+    bool maps = false;
+};
+
+template <typename T>
+inline hf_status dalloc(T** p, size_t count) {
+    *p = nullptr;
+    if (count == 0) return HF_OK;
+    HF_CUDA(cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T)));
+    return HF_OK;
+}
+
+// Expert-parallel state (hf_ep.cu). Absent when ep_world == 1.
+struct EpState;
+
+}  // namespace hf
+
+struct hf_moe_ctx {
+    hf_moe_config cfg{};
+    int H = 0, E = 0, K = 0, k = 0, I = 0, Is = 0;
+    int world = 1, rank = 0;
+    int E_local = 0, e_begin = 0;
+    int G = 0;        // expert groups run here: local experts + shared
+    int G_src = 0;    // routing groups: all experts + shared
+    int inter_max = 0;
+    size_t expert_elems = 0;
+    size_t slots_cap = 0;  // rows of the expert-side scratch
+    std::vector<hf::LayerBuf> layers;
+    hf::PlanLayout pl{};      // expert-side plan layout (G groups)
+    hf::PlanLayout pl_src{};  // routing plan layout (G_src groups)
+    int T_max = 0;
+    // routing scratch
+    float* logits = nullptr;
+    int32_t* ids = nullptr;
+    float* w = nullptr;
+    float* margins = nullptr;
+    int32_t* plan_src = nullptr;   // == plan on a single device
+    int32_t* perm_src = nullptr;   // == perm on a single device
+    int32_t* slot_pos = nullptr;
+    uint32_t* masks = nullptr;
+    int32_t* blk_counts = nullptr;
+    // expert-side scratch
+    int32_t* plan = nullptr;
+    int32_t* perm = nullptr;
+    float* mid = nullptr;
+    float* y = nullptr;
+    uint16_t* mid_hi = nullptr;  // GEMM path: SwiGLU output as bf16 hi + lo
+    uint16_t* mid_lo = nullptr;
+    uint16_t* xp_hi = nullptr;   // GEMM path: activations gathered by position
+    uint16_t* xp_lo = nullptr;
+    hf::GemmMaps maps1{}, maps2{};  // activation-side tensor maps (GEMM1, GEMM2)
+    // host-buffer API staging
+    void* x_dev = nullptr;
+    float* out_dev = nullptr;
+    bool gemm_ok = false;
+    unsigned long long timeout_ns = 2000ull * 1000 * 1000;
+    int stall = 0;               // test hook: GEMM kernels wait on a dead barrier
+    int gemm_bn = 0;             // GEMM token tile override (HF_GEMM_BN: 32, 64, 128)
+    int nsm = 148;
+    int* err_host = nullptr;     // pinned copy of the device error word
+    int grid1_bf16 = 0, grid1_f32 = 0, grid2 = 0;
+    cudaStream_t last_stream = nullptr;
+    hf::EpState* ep = nullptr;
+    // profiling: event pairs per phase, launch counters
+    bool profiling = false;
+    std::vector<cudaEvent_t> ev_pool;
+    struct Mark { int phase; cudaEvent_t a, b; };
+    std::vector<Mark> marks;
+    long long launches[HF_MOE_PHASES] = {0, 0, 0, 0, 0, 0, 0};
+};
+
+namespace hf {
+
+// Brackets one phase of a forward with events (when profiling) and counts its
+// kernel launches.
+struct PhaseTimer {
+    hf_moe_ctx* c;
+    cudaStream_t st;
+    int phase;
+    cudaEvent_t a = nullptr;
+    PhaseTimer(hf_moe_ctx* ctx, cudaStream_t s, int p) : c(ctx), st(s), phase(p) {
+        if (c->profiling) {
+            a = take();
+            if (a) cudaEventRecord(a, st);
+        }
+    }
+    cudaEvent_t take() {
+        cudaEvent_t e = nullptr;
+        if (!c->ev_pool.empty()) {
+            e = c->ev_pool.back();
+            c->ev_pool.pop_back();
+        } else if (cudaEventCreate(&e) != cudaSuccess) {
+            e = nullptr;
+        }
+        return e;
+    }
+    void done(int nlaunch) {
+        c->launches[phase] += nlaunch;
+        if (!a) return;
+        cudaEvent_t b = take();
+        if (!b) return;
+        cudaEventRecord(b, st);
+        c->marks.push_back({phase, a, b});
+        a = nullptr;
+    }
+    ~PhaseTimer() {
+        if (a) c->ev_pool.push_back(a);
+    }
+};
+
+// One expert pass: which plan, which activation rows, where outputs go. On a
+// single device the slots are the routed slots (t*k + i) and the shared ones;
+// on an expert-parallel receiver they are the received rows (k = 1) and the
+// shared slots of the local tokens.
+struct ExpertWork {
+    const int32_t* plan;
+    PlanLayout pl;
+    const int32_t* perm;
+    const void* x;     // activation rows addressed by token_of_slot(perm[p], T, k)
+    int x_f32;
+    int T, k;
+    float* y;          // [positions x H]
+    int bn;            // GEMM token tile the plan's tile prefixes were built with
+    bool maybe_gemm;
+};
+
+// Routing arguments of a forward on the given (source) plan.
+RouteArgs route_args(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T);
+hf_status run_route(hf_moe_ctx* c, const RouteArgs& ra, cudaStream_t st);
+hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st);
+hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, float* slot_out,
+                      cudaStream_t st);
+
+// hf_ep.cu
+hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id);
+void ep_destroy(hf_moe_ctx* c);
+hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T, float* out,
+                     const hf_moe_routing* r, cudaStream_t st);
+size_t ep_recv_cap(const hf_moe_ctx* c);
+
+}  // namespace hf

@@ -1,0 +1,332 @@
+// hf_ep.cu -- expert parallelism: experts sharded across GPUs, token rows
+// exchanged with NCCL over NVLink.
+//
+// The reference runs on one host with no collective backend (single-process
+// CPU engine); this exchange is new. Rank r owns experts
+// [r*E/W, (r+1)*E/W) and a replica of the shared expert. One forward:
+//
+//  1. route the rank's own tokens over ALL experts (the canonical
+//     permutation orders slots by expert, so the slots bound for rank d form
+//     one contiguous range) and gather their activation rows in that order;
+//  2. exchange per-expert counts (W x E/W int32), read them on the host and
+//     size the row exchange (the one host synchronization of a forward);
+//  3. send the rows (grouped ncclSend/ncclRecv), append the local tokens;
+//  4. run the same GEMV / tcgen05 GEMM kernels on the local experts (received
+//     rows, ordered expert-major then source rank) and on the shared expert
+//     (local tokens);
+//  5. send each expert output row (fp32) back to its source, where it lands
+//     at the slot's canonical position;
+//  6. combine at the source in the reference's top-k rank order.
+// Each slot's expert product and the combine order do not depend on W, so
+// the output equals the single-GPU output bit for bit.
+//
+// NCCL is loaded at run time (dlopen of libnccl.so.2, which returns the copy
+// the process already uses, e.g. PyTorch's), so the library does not pin an
+// NCCL build at link time.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+
+#include "hf_ctx.cuh"
+
+namespace hf {
+
+// ------------------------------------------------------------------ NCCL loader
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    std::string error;
+    bool ok = false;
+};
+
+static NcclApi load_nccl() {
+    NcclApi a;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+        a.error = std::string("cannot load libnccl.so.2: ") + dlerror();
+        return a;
+    }
+    auto sym = [&](const char* n) { return dlsym(h, n); };
+    a.GetUniqueId = reinterpret_cast<decltype(a.GetUniqueId)>(sym("ncclGetUniqueId"));
+    a.CommInitRank = reinterpret_cast<decltype(a.CommInitRank)>(sym("ncclCommInitRank"));
+    a.CommDestroy = reinterpret_cast<decltype(a.CommDestroy)>(sym("ncclCommDestroy"));
+    a.GroupStart = reinterpret_cast<decltype(a.GroupStart)>(sym("ncclGroupStart"));
+    a.GroupEnd = reinterpret_cast<decltype(a.GroupEnd)>(sym("ncclGroupEnd"));
+    a.Send = reinterpret_cast<decltype(a.Send)>(sym("ncclSend"));
+    a.Recv = reinterpret_cast<decltype(a.Recv)>(sym("ncclRecv"));
+    a.GetErrorString = reinterpret_cast<decltype(a.GetErrorString)>(sym("ncclGetErrorString"));
+    a.ok = a.GetUniqueId && a.CommInitRank && a.CommDestroy && a.GroupStart && a.GroupEnd &&
+           a.Send && a.Recv && a.GetErrorString;
+    if (!a.ok) a.error = "libnccl.so.2 lacks a required symbol";
+    return a;
+}
+
+static NcclApi& nccl() {
+    static std::once_flag once;
+    static NcclApi api;
+    std::call_once(once, [] { api = load_nccl(); });
+    return api;
+}
+
+static hf_status nccl_fail(ncclResult_t r, const char* what) {
+    const char* s = nccl().GetErrorString ? nccl().GetErrorString(r) : "unknown";
+    return fail(HF_ERR_NCCL, std::string(what) + ": " + s);
+}
+
+#define HF_NCCL(call)                                                  \
+    do {                                                               \
+        ncclResult_t _r = (call);                                      \
+        if (_r != ncclSuccess) return ::hf::nccl_fail(_r, #call);      \
+    } while (0)
+
+// ------------------------------------------------------------------ exchange plan (host)
+// Orders the received rows of one forward (see hf_ep_plan in include/hf_moe.h).
+struct ExchangePlan {
+    std::vector<int32_t> send_off, recv_off;  // [W+1] rows
+    std::vector<int32_t> local_counts;        // [El + 1]
+    int R = 0;
+};
+
+static void build_plan(int W, int El, int T, bool has_shared, const int32_t* send_counts,
+                       const int32_t* recv_counts, ExchangePlan& p, int32_t* local_rows,
+                       int32_t* row_pos) {
+    p.send_off.assign(W + 1, 0);
+    p.recv_off.assign(W + 1, 0);
+    p.local_counts.assign(El + 1, 0);
+    for (int d = 0; d < W; ++d) {
+        int s = 0, r = 0;
+        for (int j = 0; j < El; ++j) {
+            s += send_counts[d * El + j];
+            r += recv_counts[d * El + j];
+            p.local_counts[j] += recv_counts[d * El + j];
+        }
+        p.send_off[d + 1] = p.send_off[d] + s;
+        p.recv_off[d + 1] = p.recv_off[d] + r;
+    }
+    p.R = p.recv_off[W];
+    p.local_counts[El] = has_shared ? T : 0;
+    // local positions: expert-major, then source rank, then arrival order
+    std::vector<int32_t> base(El + 1, 0);
+    for (int j = 1; j <= El; ++j) base[j] = base[j - 1] + p.local_counts[j - 1];
+    std::vector<int32_t> cursor(base.begin(), base.begin() + El);
+    for (int s = 0; s < W; ++s) {
+        int row = p.recv_off[s];
+        for (int j = 0; j < El; ++j)
+            for (int i = 0; i < recv_counts[s * El + j]; ++i, ++row) {
+                const int pos = cursor[j]++;
+                if (local_rows) local_rows[pos] = row;
+                if (row_pos) row_pos[row] = pos;
+            }
+    }
+    if (local_rows && has_shared)
+        for (int t = 0; t < T; ++t) local_rows[base[El] + t] = p.R + t;
+}
+
+// ------------------------------------------------------------------ state
+struct EpState {
+    ncclComm_t comm = nullptr;
+    size_t R_cap = 0;
+    void* xsend = nullptr;     // [T_max*k x H] activation rows in canonical order
+    void* xall = nullptr;      // [(R_cap + T_max) x H] received rows, then local tokens
+    float* ysend = nullptr;    // [R_cap x H] expert outputs in arrival order
+    float* yrecv = nullptr;    // [(T_max*k + T_max) x H] outputs at canonical positions
+    int32_t* cnt_recv = nullptr;   // [W x El]
+    int32_t* loc_counts = nullptr; // [El + 1]
+    int32_t* row_pos = nullptr;    // [R_cap]
+    int32_t* h_src = nullptr;      // pinned [E + 1]
+    int32_t* h_recv = nullptr;     // pinned [W x El]
+    int32_t* h_perm = nullptr;     // pinned [R_cap + T_max]
+    int32_t* h_rowpos = nullptr;   // pinned [R_cap]
+    int32_t* h_loc = nullptr;      // pinned [El + 1]
+};
+
+size_t ep_recv_cap(const hf_moe_ctx* c) {
+    const size_t T = size_t(std::max(1, c->cfg.max_tokens));
+    return size_t(c->world) * T * size_t(std::min(c->k, c->E_local));
+}
+
+hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
+    NcclApi& n = nccl();
+    if (!n.ok) return fail(HF_ERR_NCCL, n.error);
+    auto* e = new EpState();
+    c->ep = e;
+    const size_t T = size_t(std::max(1, c->T_max));
+    e->R_cap = ep_recv_cap(c);
+    const int W = c->world, El = c->E_local;
+    HF_TRY(dalloc(reinterpret_cast<float**>(&e->xsend), T * c->k * c->H));
+    HF_TRY(dalloc(reinterpret_cast<float**>(&e->xall), (e->R_cap + T) * c->H));
+    HF_TRY(dalloc(&e->ysend, e->R_cap * c->H));
+    HF_TRY(dalloc(&e->yrecv, (T * c->k + T) * c->H));
+    HF_TRY(dalloc(&e->cnt_recv, size_t(W) * El));
+    HF_TRY(dalloc(&e->loc_counts, size_t(El) + 1));
+    HF_TRY(dalloc(&e->row_pos, e->R_cap));
+    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_src), sizeof(int32_t) * (c->E + 1)));
+    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_recv), sizeof(int32_t) * W * El));
+    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_perm), sizeof(int32_t) * (e->R_cap + T)));
+    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_rowpos), sizeof(int32_t) * e->R_cap));
+    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_loc), sizeof(int32_t) * (El + 1)));
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    HF_NCCL(n.CommInitRank(&e->comm, W, id, c->rank));
+    return HF_OK;
+}
+
+void ep_destroy(hf_moe_ctx* c) {
+    EpState* e = c->ep;
+    if (!e) return;
+    if (e->comm) nccl().CommDestroy(e->comm);
+    void* d[] = {e->xsend, e->xall, e->ysend, e->yrecv, e->cnt_recv, e->loc_counts, e->row_pos};
+    for (void* p : d) cudaFree(p);
+    void* h[] = {e->h_src, e->h_recv, e->h_perm, e->h_rowpos, e->h_loc};
+    for (void* p : h)
+        if (p) cudaFreeHost(p);
+    delete e;
+    c->ep = nullptr;
+}
+
+// ------------------------------------------------------------------ forward
+hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T, float* out,
+                     const hf_moe_routing* r, cudaStream_t st) {
+    EpState& e = *c->ep;
+    NcclApi& n = nccl();
+    const int W = c->world, El = c->E_local, k = c->k, H = c->H;
+    const size_t elt = xd == HF_F32 ? 4 : 2;
+    const size_t rowb = size_t(H) * elt;
+    const bool has_shared = c->Is > 0;
+
+    // 1. route the local tokens over all experts; gather their rows in slot order
+    const RouteArgs ra = route_args(c, L, x, xd, T);
+    if (T > 0) {
+        HF_TRY(run_route(c, ra, st));
+        PhaseTimer p1(c, st, 1);
+        HF_TRY(launch_gather_rows(e.xsend, x, rowb, T * k, c->perm_src, k, st));
+        p1.done(1);
+    } else {
+        HF_CUDA(cudaMemsetAsync(c->plan_src + c->pl_src.counts, 0, sizeof(int32_t) * c->G_src, st));
+    }
+    // 2. per-expert counts to every rank; read them back to size the exchange
+    const int32_t* cnt_src = c->plan_src + c->pl_src.counts;
+    HF_NCCL(n.GroupStart());
+    for (int d = 0; d < W; ++d) {
+        HF_NCCL(n.Send(cnt_src + d * El, El, ncclInt32, d, e.comm, st));
+        HF_NCCL(n.Recv(e.cnt_recv + d * El, El, ncclInt32, d, e.comm, st));
+    }
+    HF_NCCL(n.GroupEnd());
+    HF_CUDA(cudaMemcpyAsync(e.h_src, cnt_src, sizeof(int32_t) * c->E, cudaMemcpyDeviceToHost, st));
+    HF_CUDA(cudaMemcpyAsync(e.h_recv, e.cnt_recv, sizeof(int32_t) * W * El, cudaMemcpyDeviceToHost, st));
+    HF_CUDA(cudaStreamSynchronize(st));
+    ExchangePlan p;
+    build_plan(W, El, T, has_shared, e.h_src, e.h_recv, p, e.h_perm, e.h_rowpos);
+    const int R = p.R;
+    if (size_t(R) > e.R_cap) return fail(HF_ERR_STATE, "expert-parallel receive exceeds capacity");
+    // slot ids of the receiver plan: received row r -> r; shared token t -> (R+T) + (R+t)
+    for (int i = 0; i < R + (has_shared ? T : 0); ++i) {
+        const int row = e.h_perm[i];
+        e.h_perm[i] = row < R ? row : (R + T) + row;
+    }
+    int maxseg = 0;
+    for (int j = 0; j <= El; ++j) {
+        e.h_loc[j] = p.local_counts[j];
+        maxseg = std::max(maxseg, p.local_counts[j]);
+    }
+    const int npos = R + (has_shared ? T : 0);
+    if (npos > 0)
+        HF_CUDA(cudaMemcpyAsync(c->perm, e.h_perm, sizeof(int32_t) * npos, cudaMemcpyHostToDevice, st));
+    if (R > 0)
+        HF_CUDA(cudaMemcpyAsync(e.row_pos, e.h_rowpos, sizeof(int32_t) * R, cudaMemcpyHostToDevice, st));
+    HF_CUDA(cudaMemcpyAsync(e.loc_counts, e.h_loc, sizeof(int32_t) * (El + 1), cudaMemcpyHostToDevice, st));
+
+    // 3. dispatch: rows for rank d's experts to rank d; then append local tokens
+    char* xs = static_cast<char*>(e.xsend);
+    char* xa = static_cast<char*>(e.xall);
+    HF_NCCL(n.GroupStart());
+    for (int d = 0; d < W; ++d) {
+        const size_t ns = size_t(p.send_off[d + 1] - p.send_off[d]) * rowb;
+        const size_t nr = size_t(p.recv_off[d + 1] - p.recv_off[d]) * rowb;
+        if (ns) HF_NCCL(n.Send(xs + size_t(p.send_off[d]) * rowb, ns, ncclChar, d, e.comm, st));
+        if (nr) HF_NCCL(n.Recv(xa + size_t(p.recv_off[d]) * rowb, nr, ncclChar, d, e.comm, st));
+    }
+    HF_NCCL(n.GroupEnd());
+    if (T > 0) HF_CUDA(cudaMemcpyAsync(xa + size_t(R) * rowb, x, size_t(T) * rowb, cudaMemcpyDeviceToDevice, st));
+
+    // 4. local experts over received rows, shared expert over local tokens
+    RouteArgs rl = ra;
+    rl.plan = c->plan;
+    rl.pl = c->pl;
+    rl.T = R + T;
+    rl.gemm_bn = c->gemm_bn ? c->gemm_bn : (R + T <= 64 ? 32 : 128);
+    HF_TRY(launch_plan_from_counts(rl, e.loc_counts, st));
+    ExpertWork w{};
+    w.plan = c->plan;
+    w.pl = c->pl;
+    w.perm = c->perm;
+    w.x = e.xall;
+    w.x_f32 = xd == HF_F32;
+    w.T = R + T;
+    w.k = 1;
+    w.y = c->y;
+    w.bn = rl.gemm_bn;
+    w.maybe_gemm = rl.gemm_ok && (c->cfg.path == HF_PATH_GEMM || maxseg > c->cfg.gemv_max_tokens);
+    if (npos > 0) HF_TRY(run_experts(c, L, w, st));
+
+    // 5. outputs back to their sources, at canonical slot positions
+    if (R > 0) HF_TRY(launch_gather_rows(e.ysend, c->y, size_t(H) * 4, R, e.row_pos, 1, st));
+    const size_t yrow = size_t(H) * 4;
+    char* ys = reinterpret_cast<char*>(e.ysend);
+    char* yr = reinterpret_cast<char*>(e.yrecv);
+    HF_NCCL(n.GroupStart());
+    for (int d = 0; d < W; ++d) {
+        const size_t ns = size_t(p.recv_off[d + 1] - p.recv_off[d]) * yrow;
+        const size_t nr = size_t(p.send_off[d + 1] - p.send_off[d]) * yrow;
+        if (ns) HF_NCCL(n.Send(ys + size_t(p.recv_off[d]) * yrow, ns, ncclChar, d, e.comm, st));
+        if (nr) HF_NCCL(n.Recv(yr + size_t(p.send_off[d]) * yrow, nr, ncclChar, d, e.comm, st));
+    }
+    HF_NCCL(n.GroupEnd());
+    if (T > 0 && has_shared)
+        HF_CUDA(cudaMemcpyAsync(yr + size_t(T) * k * yrow, c->y + size_t(R) * H, size_t(T) * yrow,
+                                cudaMemcpyDeviceToDevice, st));
+    // 6. combine in the reference order at the source
+    if (T > 0) HF_TRY(run_combine(c, e.yrecv, T, out, r ? r->slot_out : nullptr, st));
+    return HF_OK;
+}
+
+}  // namespace hf
+
+using namespace hf;
+
+extern "C" hf_status hf_ep_unique_id(unsigned char* out) {
+    if (!out) return fail(HF_ERR_ARG, "hf_ep_unique_id: null output");
+    NcclApi& n = nccl();
+    if (!n.ok) return fail(HF_ERR_NCCL, n.error);
+    ncclUniqueId id;
+    HF_NCCL(n.GetUniqueId(&id));
+    static_assert(sizeof(id) == 128, "NCCL unique id is 128 bytes");
+    std::memcpy(out, &id, sizeof(id));
+    return HF_OK;
+}
+
+extern "C" hf_status hf_ep_plan(int world, int E_local, int T_local, int has_shared,
+                                const int32_t* send_counts, const int32_t* recv_counts,
+                                int32_t* send_off, int32_t* recv_off, int32_t* local_counts,
+                                int32_t* local_rows, int32_t* row_pos) {
+    if (world <= 0 || E_local <= 0 || T_local < 0 || !send_counts || !recv_counts)
+        return fail(HF_ERR_ARG, "hf_ep_plan: bad arguments");
+    ExchangePlan p;
+    build_plan(world, E_local, T_local, has_shared != 0, send_counts, recv_counts, p, local_rows,
+               row_pos);
+    if (send_off) std::copy(p.send_off.begin(), p.send_off.end(), send_off);
+    if (recv_off) std::copy(p.recv_off.begin(), p.recv_off.end(), recv_off);
+    if (local_counts) std::copy(p.local_counts.begin(), p.local_counts.end(), local_counts);
+    return HF_OK;
+}

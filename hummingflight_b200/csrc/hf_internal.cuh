@@ -188,6 +188,12 @@ __device__ __forceinline__ int find_group(const int32_t* prefix, int G, int u) {
 int num_sms(int device);
 
 hf_status launch_router_logits(const RouteArgs& a, cudaStream_t st);
+// Work plan (counts, offsets, unit and tile prefixes) from per-group counts
+// already in device memory (expert-parallel receivers, dense MLP).
+hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cudaStream_t st);
+// dst row i = src row (idx[i] / div), i < n; rows of row_bytes (multiple of 16).
+hf_status launch_gather_rows(void* dst, const void* src, size_t row_bytes, int n,
+                             const int32_t* idx, int div, cudaStream_t st);
 // Top-k + permutation + plan; *launches receives the number of kernels.
 hf_status launch_route(const RouteArgs& a, cudaStream_t st, int* launches);
 hf_status launch_topk(const float* scores, int T, int E, const float* bias, int k, float scale,

@@ -5,7 +5,8 @@
 // 196-492). Differences by design: all weights of a layer stay resident in HBM
 // (no per-token staging over PCIe), a forward covers T tokens at once, every
 // error is returned (no CPU fallback), and kernels run asynchronously on the
-// caller's stream.
+// caller's stream. A forward is three phases -- routing, experts, combine --
+// that the expert-parallel path (hf_ep.cu) reuses around its exchanges.
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
@@ -13,7 +14,7 @@
 #include <string>
 #include <vector>
 
-#include "hf_internal.cuh"
+#include "hf_ctx.cuh"
 #include "hf_synth.h"
 
 namespace hf {
@@ -40,128 +41,151 @@ int num_sms(int device) {
     return n;
 }
 
-// Makes the context's device current for one API call and restores the
-// caller's device afterwards.
-struct DeviceGuard {
-    int prev = -1;
-    bool ok = false;
-    explicit DeviceGuard(int dev) {
-        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-        ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
-    }
-    ~DeviceGuard() {
-        int cur = -1;
-        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-    }
-};
+// ------------------------------------------------------------------ phases
+RouteArgs route_args(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T) {
+    RouteArgs ra{};
+    ra.x = x;
+    ra.x_f32 = xd == HF_F32;
+    ra.T = T;
+    ra.H = c->H;
+    ra.E = c->E;
+    ra.k = c->k;
+    ra.router = L.router;
+    ra.bias = L.has_bias ? L.bias : nullptr;
+    ra.scale = c->cfg.routed_scaling_factor;
+    ra.norm = c->cfg.norm_topk_prob;
+    ra.logits = c->logits;
+    ra.ids = c->ids;
+    ra.w = c->w;
+    ra.margins = c->margins;
+    ra.plan = c->plan_src;
+    ra.pl = c->pl_src;
+    ra.has_shared = c->Is > 0;
+    ra.shared_inter = c->Is;
+    ra.inter = c->I;
+    ra.perm = c->perm_src;
+    ra.slot_pos = c->slot_pos;
+    ra.masks = c->masks;
+    ra.blk_counts = c->blk_counts;
+    ra.path = c->cfg.path;
+    ra.gemv_max = c->cfg.gemv_max_tokens;
+    ra.gemm_ok = c->gemm_ok && L.maps;
+    // decode: narrow token tiles leave room for a deeper weight ring
+    ra.gemm_bn = c->gemm_bn ? c->gemm_bn : (T <= 64 ? 32 : 128);
+    return ra;
+}
 
-struct LayerBuf {
-    uint16_t* router = nullptr;  // [E x H]
-    float* bias = nullptr;       // [E]
-    bool has_bias = false;
-    uint16_t* experts = nullptr; // [E_local][gate|up|down]
-    uint16_t* shared = nullptr;  // [gate|up|down] of the shared expert
-    GroupW* groups = nullptr;    // [G] device table
-    bool loaded = false;
-    // TMA views of the weights for the tcgen05 GEMM (built with the buffers)
-    CUtensorMap gu{}, gu_sh{};   // gate/up rows: H-wide rows of [gate|up|down]
-    CUtensorMap dn{}, dn_sh{};   // down rows: I-wide rows of the same buffers
-    bool maps = false;
-};
+hf_status run_route(hf_moe_ctx* c, const RouteArgs& ra, cudaStream_t st) {
+    {
+        PhaseTimer p0(c, st, 0);
+        HF_TRY(launch_router_logits(ra, st));
+        p0.done(1);
+    }
+    PhaseTimer p1(c, st, 1);
+    int n = 0;
+    HF_TRY(launch_route(ra, st, &n));
+    p1.done(n);
+    return HF_OK;
+}
 
-template <typename T>
-static hf_status dalloc(T** p, size_t count) {
-    *p = nullptr;
-    if (count == 0) return HF_OK;
-    HF_CUDA(cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T)));
+hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st) {
+    const int bn = w.bn;
+    if (w.maybe_gemm) {
+        GatherArgs gx{};
+        gx.plan = w.plan;
+        gx.pl = w.pl;
+        gx.perm = w.perm;
+        gx.x = w.x;
+        gx.T = w.T;
+        gx.k = w.k;
+        gx.H = c->H;
+        gx.device = c->cfg.device;
+        gx.xp_hi = c->xp_hi;
+        gx.xp_lo = c->xp_lo;
+        PhaseTimer p1(c, st, 1);
+        HF_TRY(launch_gather(gx, w.x_f32, st));
+        p1.done(1);
+    }
+    GemvArgs ga{};
+    ga.groups = L.groups;
+    ga.plan = w.plan;
+    ga.pl = w.pl;
+    ga.perm = w.perm;
+    ga.x = w.x;
+    ga.x_f32 = w.x_f32;
+    ga.T = w.T;
+    ga.H = c->H;
+    ga.k = w.k;
+    ga.inter_max = c->inter_max;
+    ga.mid = c->mid;
+    ga.y = w.y;
+    ga.grid1 = w.x_f32 ? c->grid1_f32 : c->grid1_bf16;
+    ga.grid2 = c->grid2;
+    const bool gemv_possible = !(w.maybe_gemm && c->cfg.path == HF_PATH_GEMM);
+    if (gemv_possible) {
+        PhaseTimer p2(c, st, 2);
+        HF_TRY(launch_gemv1(ga, st));
+        p2.done(1);
+    }
+    GemmArgs gm{};
+    if (w.maybe_gemm) {
+        gm.plan = w.plan;
+        gm.pl = w.pl;
+        gm.which = 1;
+        gm.H = c->H;
+        gm.I = c->I;
+        gm.Is = c->Is;
+        gm.Imax = c->inter_max;
+        gm.bn = bn;
+        gm.mid_hi = c->mid_hi;
+        gm.mid_lo = c->mid_lo;
+        gm.y = w.y;
+        gm.err = c->plan + c->pl.stats + 3;
+        gm.timeout_ns = c->timeout_ns;
+        gm.test_stall = c->stall;
+        GemmMaps m1 = c->maps1;
+        m1.A = L.gu;
+        m1.A_sh = L.gu_sh;
+        PhaseTimer p4(c, st, 4);
+        HF_TRY(launch_gemm(m1, gm, w.x_f32 ? 2 : 1, c->nsm, st));
+        p4.done(1);
+    }
+    if (gemv_possible) {
+        PhaseTimer p3(c, st, 3);
+        HF_TRY(launch_gemv2(ga, st));
+        p3.done(1);
+    }
+    if (w.maybe_gemm) {
+        gm.which = 2;
+        GemmMaps m2 = c->maps2;
+        m2.A = L.dn;
+        m2.A_sh = L.dn_sh;
+        PhaseTimer p5(c, st, 5);
+        HF_TRY(launch_gemm(m2, gm, 2, c->nsm, st));
+        p5.done(1);
+    }
+    return HF_OK;
+}
+
+hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, float* slot_out,
+                      cudaStream_t st) {
+    CombineArgs ca{};
+    ca.y = y;
+    ca.slot_pos = c->slot_pos;
+    ca.w = c->w;
+    ca.T = T;
+    ca.H = c->H;
+    ca.k = c->k;
+    ca.has_shared = c->Is > 0;
+    ca.out = out;
+    ca.slot_out = slot_out;
+    PhaseTimer p6(c, st, 6);
+    HF_TRY(launch_combine(ca, st));
+    p6.done(1);
     return HF_OK;
 }
 
 }  // namespace hf
-
-struct hf_moe_ctx {
-    hf_moe_config cfg{};
-    int H = 0, E = 0, K = 0, k = 0, I = 0, Is = 0;
-    int E_local = 0, e_begin = 0, G = 0, inter_max = 0;
-    size_t expert_elems = 0;
-    std::vector<hf::LayerBuf> layers;
-    hf::PlanLayout pl{};
-    int T_max = 0;
-    // scratch
-    float* logits = nullptr;
-    int32_t* ids = nullptr;
-    float* w = nullptr;
-    float* margins = nullptr;
-    int32_t* plan = nullptr;
-    int32_t* perm = nullptr;
-    int32_t* slot_pos = nullptr;
-    uint32_t* masks = nullptr;
-    int32_t* blk_counts = nullptr;
-    float* mid = nullptr;
-    float* y = nullptr;
-    void* x_dev = nullptr;   // host-buffer API staging [T_max x H] fp32-sized
-    float* out_dev = nullptr;
-    uint16_t* mid_hi = nullptr;  // GEMM path: SwiGLU output as bf16 hi + lo
-    uint16_t* mid_lo = nullptr;
-    uint16_t* xp_hi = nullptr;   // GEMM path: activations gathered by position
-    uint16_t* xp_lo = nullptr;
-    hf::GemmMaps maps1{}, maps2{};  // activation-side tensor maps (GEMM1, GEMM2)
-    bool gemm_ok = false;
-    unsigned long long timeout_ns = 2000ull * 1000 * 1000;
-    int stall = 0;               // test hook: GEMM kernels wait on a dead barrier
-    int gemm_bn = 0;             // GEMM token tile override (HF_GEMM_BN: 32, 64, 128)
-    int nsm = 148;
-    int* err_host = nullptr;     // pinned copy of the device error word
-    int grid1_bf16 = 0, grid1_f32 = 0, grid2 = 0;
-    cudaStream_t last_stream = nullptr;
-    // profiling: event pairs per phase, launch counters
-    bool profiling = false;
-    std::vector<cudaEvent_t> ev_pool;
-    struct Mark { int phase; cudaEvent_t a, b; };
-    std::vector<Mark> marks;
-    long long launches[HF_MOE_PHASES] = {0, 0, 0, 0, 0, 0, 0};
-};
-
-namespace {
-
-// Brackets one phase of a forward with events (when profiling) and counts its
-// kernel launches.
-struct PhaseTimer {
-    hf_moe_ctx* c;
-    cudaStream_t st;
-    int phase;
-    cudaEvent_t a = nullptr;
-    PhaseTimer(hf_moe_ctx* ctx, cudaStream_t s, int p) : c(ctx), st(s), phase(p) {
-        if (c->profiling) {
-            a = take();
-            if (a) cudaEventRecord(a, st);
-        }
-    }
-    cudaEvent_t take() {
-        cudaEvent_t e = nullptr;
-        if (!c->ev_pool.empty()) {
-            e = c->ev_pool.back();
-            c->ev_pool.pop_back();
-        } else if (cudaEventCreate(&e) != cudaSuccess) {
-            e = nullptr;
-        }
-        return e;
-    }
-    void done(int nlaunch) {
-        c->launches[phase] += nlaunch;
-        if (!a) return;
-        cudaEvent_t b = take();
-        if (!b) return;
-        cudaEventRecord(b, st);
-        c->marks.push_back({phase, a, b});
-        a = nullptr;
-    }
-    ~PhaseTimer() {
-        if (a) c->ev_pool.push_back(a);
-    }
-};
-
-}  // namespace
 
 using namespace hf;
 
@@ -186,6 +210,7 @@ const char* hf_status_string(hf_status s) {
 const char* hf_last_error(void) { return g_last_error.c_str(); }
 
 static void free_ctx(hf_moe_ctx* c) {
+    ep_destroy(c);
     for (auto& L : c->layers) {
         cudaFree(L.router);
         cudaFree(L.bias);
@@ -198,9 +223,11 @@ static void free_ctx(hf_moe_ctx* c) {
         cudaEventDestroy(m.b);
     }
     for (auto e : c->ev_pool) cudaEventDestroy(e);
-    void* bufs[] = {c->logits, c->ids, c->w, c->margins, c->plan, c->perm, c->slot_pos,
-                    c->masks, c->blk_counts, c->mid, c->y, c->x_dev, c->out_dev,
-                    c->mid_hi, c->mid_lo, c->xp_hi, c->xp_lo};
+    if (c->plan_src != c->plan) cudaFree(c->plan_src);
+    if (c->perm_src != c->perm) cudaFree(c->perm_src);
+    void* bufs[] = {c->logits, c->ids,    c->w,      c->margins, c->plan,  c->perm,
+                    c->slot_pos, c->masks, c->blk_counts, c->mid, c->y,     c->x_dev,
+                    c->out_dev, c->mid_hi, c->mid_lo, c->xp_hi,   c->xp_lo};
     for (void* p : bufs) cudaFree(p);
     if (c->err_host) cudaFreeHost(c->err_host);
     delete c;
@@ -233,8 +260,12 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     if (c.max_tokens < 0) return fail(HF_ERR_ARG, "max_tokens must be >= 0");
     if (c.path < HF_PATH_AUTO || c.path > HF_PATH_GEMM) return fail(HF_ERR_ARG, "bad path");
     const int world = c.ep_world <= 0 ? 1 : c.ep_world;
-    if (world != 1)
-        return fail(HF_ERR_UNSUPPORTED, "expert parallelism is not available in this build");
+    if (world > 1) {
+        if (c.num_experts % world)
+            return fail(HF_ERR_ARG, "expert parallelism needs num_experts divisible by ep_world");
+        if (c.ep_rank < 0 || c.ep_rank >= world) return fail(HF_ERR_ARG, "ep_rank out of range");
+        if (!c.ep_unique_id) return fail(HF_ERR_ARG, "ep_unique_id is required when ep_world > 1");
+    }
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
         return fail(HF_ERR_UNSUPPORTED, "no CUDA device");
@@ -250,6 +281,8 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     auto* x = new hf_moe_ctx();
     x->cfg = c;
     x->cfg.ep_world = world;
+    x->world = world;
+    x->rank = world > 1 ? c.ep_rank : 0;
     x->H = c.hidden_size;
     x->E = c.num_experts;
     x->K = c.num_experts_per_tok;
@@ -257,11 +290,13 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     x->I = c.moe_intermediate_size;
     x->Is = c.shared_intermediate_size;
     x->E_local = x->E / world;
-    x->e_begin = 0;
-    x->G = x->E + 1;
+    x->e_begin = x->rank * x->E_local;
+    x->G = x->E_local + 1;
+    x->G_src = x->E + 1;
     x->inter_max = std::max(x->I, x->Is);
     x->expert_elems = size_t(3) * x->I * x->H;
     x->pl = PlanLayout::make(x->G);
+    x->pl_src = PlanLayout::make(x->G_src);
     x->T_max = c.max_tokens;
     if (x->cfg.gemv_max_tokens <= 0) x->cfg.gemv_max_tokens = kGemvDefaultMax;
     if (const char* bn = std::getenv("HF_GEMM_BN")) {  // tuning knob
@@ -274,7 +309,9 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     }
     x->layers.resize(c.num_layers);
     const size_t T = size_t(std::max(1, c.max_tokens));
-    const size_t slots = T * x->k + T;
+    const size_t src_slots = T * x->k + T;
+    x->slots_cap = world > 1 ? ep_recv_cap(x) + T : src_slots;
+    const size_t slots = x->slots_cap;
     const size_t nb = (T + kSmallRouteT - 1) / kSmallRouteT;
     hf_status s = HF_OK;
     auto A = [&](hf_status r) { if (s == HF_OK) s = r; };
@@ -284,7 +321,14 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     A(dalloc(&x->margins, T));
     A(dalloc(&x->plan, size_t(x->pl.words)));
     A(dalloc(&x->perm, slots));
-    A(dalloc(&x->slot_pos, slots));
+    if (world > 1) {
+        A(dalloc(&x->plan_src, size_t(x->pl_src.words)));
+        A(dalloc(&x->perm_src, src_slots));
+    } else {
+        x->plan_src = x->plan;
+        x->perm_src = x->perm;
+    }
+    A(dalloc(&x->slot_pos, src_slots));
     A(dalloc(&x->masks, nb * 4 * x->E));
     A(dalloc(&x->blk_counts, nb * x->E));
     A(dalloc(&x->mid, slots * x->inter_max));
@@ -333,6 +377,14 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     x->grid1_bf16 = gemv_grid(c.device, true, false, x->H, x->inter_max, x->G);
     x->grid1_f32 = gemv_grid(c.device, true, true, x->H, x->inter_max, x->G);
     x->grid2 = gemv_grid(c.device, false, false, x->H, x->inter_max, x->G);
+    if (world > 1) {
+        s = ep_create(x, c.ep_unique_id);
+        if (s != HF_OK) {
+            std::string m = g_last_error;
+            free_ctx(x);
+            return fail(s, m);
+        }
+    }
     *out = x;
     return HF_OK;
 }
@@ -484,6 +536,23 @@ hf_status hf_moe_mark_loaded(hf_moe_ctx* ctx, int layer) {
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+static hf_status copy_routing(hf_moe_ctx* c, const hf_moe_routing* r, int T, cudaStream_t st) {
+    if (!r) return HF_OK;
+    const int k = c->k, G = c->G_src;
+    const size_t nslots = size_t(T) * k + (c->Is > 0 ? T : 0);
+    const cudaMemcpyKind d2d = cudaMemcpyDeviceToDevice;
+    if (r->topk_ids) HF_CUDA(cudaMemcpyAsync(r->topk_ids, c->ids, sizeof(int32_t) * T * k, d2d, st));
+    if (r->topk_weights) HF_CUDA(cudaMemcpyAsync(r->topk_weights, c->w, sizeof(float) * T * k, d2d, st));
+    if (r->margins) HF_CUDA(cudaMemcpyAsync(r->margins, c->margins, sizeof(float) * T, d2d, st));
+    if (r->counts)
+        HF_CUDA(cudaMemcpyAsync(r->counts, c->plan_src + c->pl_src.counts, sizeof(int32_t) * G, d2d, st));
+    if (r->offsets)
+        HF_CUDA(cudaMemcpyAsync(r->offsets, c->plan_src + c->pl_src.offsets, sizeof(int32_t) * (G + 1),
+                                d2d, st));
+    if (r->perm) HF_CUDA(cudaMemcpyAsync(r->perm, c->perm_src, sizeof(int32_t) * nslots, d2d, st));
+    return HF_OK;
+}
+
 static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype xd, int T,
                              float* out, const hf_moe_routing* r, cudaStream_t st, bool route_only) {
     LayerBuf& L = c->layers[layer];
@@ -494,148 +563,31 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
     if (!route_only && T > 0 && (!out || !aligned16(out)))
         return fail(HF_ERR_ARG, "out must be a 16-byte aligned device pointer");
     c->last_stream = st;
+    if (c->world > 1 && !route_only) {
+        // every rank takes part in the exchanges, even with no tokens of its own
+        HF_TRY(ep_forward(c, L, x, xd, T, out, r, st));
+        return copy_routing(c, r, T, st);
+    }
     if (T == 0) return HF_OK;
-    const int k = c->k;
-    RouteArgs ra{};
-    ra.x = x;
-    ra.x_f32 = xd == HF_F32;
-    ra.T = T;
-    ra.H = c->H;
-    ra.E = c->E;
-    ra.k = k;
-    ra.router = L.router;
-    ra.bias = L.has_bias ? L.bias : nullptr;
-    ra.scale = c->cfg.routed_scaling_factor;
-    ra.norm = c->cfg.norm_topk_prob;
-    ra.logits = c->logits;
-    ra.ids = c->ids;
-    ra.w = c->w;
-    ra.margins = c->margins;
-    ra.plan = c->plan;
-    ra.pl = c->pl;
-    ra.has_shared = c->Is > 0;
-    ra.shared_inter = c->Is;
-    ra.inter = c->I;
-    ra.perm = c->perm;
-    ra.slot_pos = c->slot_pos;
-    ra.masks = c->masks;
-    ra.blk_counts = c->blk_counts;
-    ra.path = c->cfg.path;
-    ra.gemv_max = c->cfg.gemv_max_tokens;
-    ra.gemm_ok = c->gemm_ok && L.maps;
-    // decode: narrow token tiles leave room for a deeper weight ring
-    ra.gemm_bn = c->gemm_bn ? c->gemm_bn : (T <= 64 ? 32 : 128);
-    // segments can only exceed the GEMV threshold when T does
-    const bool maybe_gemm =
-        ra.gemm_ok && (c->cfg.path == HF_PATH_GEMM || T > c->cfg.gemv_max_tokens);
-    {
-        PhaseTimer p0(c, st, 0);
-        HF_TRY(launch_router_logits(ra, st));
-        p0.done(1);
-    }
-    {
-        PhaseTimer p1(c, st, 1);
-        int n = 0;
-        HF_TRY(launch_route(ra, st, &n));
-        if (maybe_gemm && !route_only) {
-            GatherArgs gx{};
-            gx.plan = c->plan;
-            gx.pl = c->pl;
-            gx.perm = c->perm;
-            gx.x = x;
-            gx.T = T;
-            gx.k = k;
-            gx.H = c->H;
-            gx.device = c->cfg.device;
-            gx.xp_hi = c->xp_hi;
-            gx.xp_lo = c->xp_lo;
-            HF_TRY(launch_gather(gx, xd == HF_F32, st));
-            ++n;
-        }
-        p1.done(n);
-    }
-    const size_t nslots = size_t(T) * k + (c->Is > 0 ? T : 0);
+    const RouteArgs ra = route_args(c, L, x, xd, T);
+    HF_TRY(run_route(c, ra, st));
     if (!route_only) {
-        GemvArgs ga{};
-        ga.groups = L.groups;
-        ga.plan = c->plan;
-        ga.pl = c->pl;
-        ga.perm = c->perm;
-        ga.x = x;
-        ga.x_f32 = xd == HF_F32;
-        ga.T = T;
-        ga.H = c->H;
-        ga.k = k;
-        ga.inter_max = c->inter_max;
-        ga.mid = c->mid;
-        ga.y = c->y;
-        ga.grid1 = xd == HF_F32 ? c->grid1_f32 : c->grid1_bf16;
-        ga.grid2 = c->grid2;
-        {
-            PhaseTimer p2(c, st, 2);
-            HF_TRY(launch_gemv1(ga, st));
-            p2.done(1);
-        }
-        GemmArgs gm{};
-        if (maybe_gemm) {
-            gm.plan = c->plan;
-            gm.pl = c->pl;
-            gm.which = 1;
-            gm.H = c->H;
-            gm.I = c->I;
-            gm.Is = c->Is;
-            gm.Imax = c->inter_max;
-            gm.bn = ra.gemm_bn;
-            gm.mid_hi = c->mid_hi;
-            gm.mid_lo = c->mid_lo;
-            gm.y = c->y;
-            gm.err = c->plan + c->pl.stats + 3;
-            gm.timeout_ns = c->timeout_ns;
-            gm.test_stall = c->stall;
-            GemmMaps m1 = c->maps1;
-            m1.A = L.gu;
-            m1.A_sh = L.gu_sh;
-            PhaseTimer p4(c, st, 4);
-            HF_TRY(launch_gemm(m1, gm, xd == HF_F32 ? 2 : 1, c->nsm, st));
-            p4.done(1);
-        }
-        {
-            PhaseTimer p3(c, st, 3);
-            HF_TRY(launch_gemv2(ga, st));
-            p3.done(1);
-        }
-        if (maybe_gemm) {
-            gm.which = 2;
-            GemmMaps m2 = c->maps2;
-            m2.A = L.dn;
-            m2.A_sh = L.dn_sh;
-            PhaseTimer p5(c, st, 5);
-            HF_TRY(launch_gemm(m2, gm, 2, c->nsm, st));
-            p5.done(1);
-        }
-        CombineArgs ca{};
-        ca.y = c->y;
-        ca.slot_pos = c->slot_pos;
-        ca.w = c->w;
-        ca.T = T;
-        ca.H = c->H;
-        ca.k = k;
-        ca.has_shared = c->Is > 0;
-        ca.out = out;
-        ca.slot_out = r ? r->slot_out : nullptr;
-        PhaseTimer p6(c, st, 6);
-        HF_TRY(launch_combine(ca, st));
-        p6.done(1);
+        ExpertWork w{};
+        w.plan = c->plan;
+        w.pl = c->pl;
+        w.perm = c->perm;
+        w.x = x;
+        w.x_f32 = xd == HF_F32;
+        w.T = T;
+        w.k = c->k;
+        w.y = c->y;
+        w.bn = ra.gemm_bn;
+        // segments can only exceed the GEMV threshold when T does
+        w.maybe_gemm = ra.gemm_ok && (c->cfg.path == HF_PATH_GEMM || T > c->cfg.gemv_max_tokens);
+        HF_TRY(run_experts(c, L, w, st));
+        HF_TRY(run_combine(c, c->y, T, out, r ? r->slot_out : nullptr, st));
     }
-    if (r) {
-        if (r->topk_ids) HF_CUDA(cudaMemcpyAsync(r->topk_ids, c->ids, sizeof(int32_t) * T * k, cudaMemcpyDeviceToDevice, st));
-        if (r->topk_weights) HF_CUDA(cudaMemcpyAsync(r->topk_weights, c->w, sizeof(float) * T * k, cudaMemcpyDeviceToDevice, st));
-        if (r->margins) HF_CUDA(cudaMemcpyAsync(r->margins, c->margins, sizeof(float) * T, cudaMemcpyDeviceToDevice, st));
-        if (r->counts) HF_CUDA(cudaMemcpyAsync(r->counts, c->plan + c->pl.counts, sizeof(int32_t) * c->G, cudaMemcpyDeviceToDevice, st));
-        if (r->offsets) HF_CUDA(cudaMemcpyAsync(r->offsets, c->plan + c->pl.offsets, sizeof(int32_t) * (c->G + 1), cudaMemcpyDeviceToDevice, st));
-        if (r->perm) HF_CUDA(cudaMemcpyAsync(r->perm, c->perm, sizeof(int32_t) * nslots, cudaMemcpyDeviceToDevice, st));
-    }
-    return HF_OK;
+    return copy_routing(c, r, T, st);
 }
 
 hf_status hf_moe_forward(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_dtype, int T,

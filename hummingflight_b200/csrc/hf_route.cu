@@ -474,6 +474,48 @@ __global__ void __launch_bounds__(1024) k_perm_plan(RouteArgs a, int nb) {
     }
 }
 
+__global__ void __launch_bounds__(1024) k_plan_counts(RouteArgs a, const int32_t* counts) {
+    extern __shared__ __align__(16) uint32_t sm[];
+    const int G = a.pl.G;
+    int* s_cnt = reinterpret_cast<int*>(sm);
+    int* s_tmp = s_cnt + G;
+    int* warp_tot = s_tmp + G + 1;
+    for (int g = threadIdx.x; g < G; g += blockDim.x) s_cnt[g] = counts[g];
+    __syncthreads();
+    plan_from_counts(a, s_cnt, s_tmp, warp_tot);
+}
+
+hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cudaStream_t st) {
+    const int G = a.pl.G;
+    const size_t smem = sizeof(int) * (G + G + 1 + 33);
+    k_plan_counts<<<1, 1024, smem, st>>>(a, counts);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+__global__ void __launch_bounds__(256) k_gather_rows(uint4* dst, const uint4* src, int row_vec, int n,
+                                                     const int32_t* idx, int div) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int i = warp; i < n; i += nw) {
+        const int s = idx[i] / div;
+        const uint4* sr = src + size_t(s) * row_vec;
+        uint4* dr = dst + size_t(i) * row_vec;
+        for (int c = lane; c < row_vec; c += 32) dr[c] = ld_nc_u4(sr + c);
+    }
+}
+
+hf_status launch_gather_rows(void* dst, const void* src, size_t row_bytes, int n,
+                             const int32_t* idx, int div, cudaStream_t st) {
+    if (n <= 0) return HF_OK;
+    if (row_bytes % 16) return fail(HF_ERR_ARG, "row gather needs 16-byte rows");
+    const int blocks = std::min(num_sms(0) * 8, (n + 7) / 8);
+    k_gather_rows<<<blocks, 256, 0, st>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src),
+                                          int(row_bytes / 16), n, idx, div);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
 __global__ void __launch_bounds__(256) k_perm_scatter(RouteArgs a) {
     const int b = blockIdx.x, E = a.E, k = a.k, T = a.T;
     const int t0 = b * kSmallRouteT;

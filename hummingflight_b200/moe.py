@@ -75,15 +75,26 @@ class MoELayer:
     """Resident MoE layers on one device (a drop-in for the reference's moeLayer)."""
 
     def __init__(self, shape: LayerShape = GLM, num_layers: int = 1, max_tokens: int = 64,
-                 device: int = 0, path: str = "auto", gemv_max_tokens: int = 0):
+                 device: int = 0, path: str = "auto", gemv_max_tokens: int = 0,
+                 ep_rank: int = 0, ep_world: int = 1, ep_unique_id: Optional[bytes] = None):
+        """ep_world > 1: this rank holds experts [ep_rank*E/W, (ep_rank+1)*E/W)
+        and exchanges token rows with the other ranks (ep_unique_id from
+        hummingflight_b200.ep.unique_id() on rank 0, shared with all ranks)."""
         self.shape = shape
         self.num_layers = num_layers
         self.max_tokens = max_tokens
         self.device = device
         self.k = min(shape.top_k, shape.num_experts)
+        self.ep_rank, self.ep_world = ep_rank, ep_world
+        uid = None
+        if ep_world > 1:
+            if ep_unique_id is None or len(ep_unique_id) != 128:
+                raise ValueError("ep_unique_id (128 bytes) is required when ep_world > 1")
+            uid = ctypes.create_string_buffer(bytes(ep_unique_id), 128)
         cfg = HfMoeConfig(shape.hidden, shape.num_experts, shape.top_k, shape.inter,
                           shape.shared_inter, shape.scale, int(shape.norm_topk), num_layers,
-                          max_tokens, device, _PATHS[path], gemv_max_tokens, 0, 1, None)
+                          max_tokens, device, _PATHS[path], gemv_max_tokens, ep_rank, ep_world,
+                          ctypes.cast(uid, ctypes.c_void_p) if uid is not None else None)
         h = ctypes.c_void_p()
         call("hf_moe_create", ctypes.byref(h), ctypes.byref(cfg))
         self._h = h

@@ -164,6 +164,32 @@ HF_API hf_status hf_moe_set_wait_timeout(hf_moe_ctx* ctx, uint64_t ns);
  * HF_ERR_TIMEOUT. No counterpart in the reference, which has no device waits. */
 HF_API hf_status hf_moe_debug_stall(hf_moe_ctx* ctx, int enable);
 
+/* Expert parallelism (no reference counterpart: the reference is a single
+ * process on one host). With ep_world = W > 1 each rank's context holds the
+ * experts [rank*E/W, (rank+1)*E/W) plus the shared expert, and
+ * hf_moe_forward routes the rank's own T tokens, exchanges token rows and
+ * expert outputs with the other ranks over NCCL (one host synchronization per
+ * forward, after the per-expert counts arrive) and combines at the source in
+ * the reference's rank order, so outputs equal the single-GPU outputs. Every
+ * rank must call the same forwards in the same order (T may differ, even 0).
+ * NCCL is loaded at run time (libnccl.so.2). */
+/* A fresh NCCL unique id (128 bytes) for hf_moe_config.ep_unique_id; rank 0
+ * makes it and the caller broadcasts it to the other ranks. An id serves one
+ * set of contexts (one communicator): make a new one for every hf_moe_create
+ * round. */
+HF_API hf_status hf_ep_unique_id(unsigned char* out128);
+/* The host-side order of one exchange, as the forward builds it (for tests
+ * and external transports): send_counts / recv_counts [W x E_local] are the
+ * rows this rank sends to / receives from each rank per local expert;
+ * writes send_off, recv_off [W+1] (rows, source-major), local_counts
+ * [E_local+1] (last: T_local when has_shared), local_rows [R + T_local] (for
+ * each local position, expert-major then source rank, the row in [received
+ * rows | local tokens]) and row_pos [R] (received row -> local position). */
+HF_API hf_status hf_ep_plan(int world, int E_local, int T_local, int has_shared,
+                            const int32_t* send_counts, const int32_t* recv_counts,
+                            int32_t* send_off, int32_t* recv_off, int32_t* local_counts,
+                            int32_t* local_rows, int32_t* row_pos);
+
 /* Routing (router GEMV, sigmoid, bias, top-k, permutation) that allocates no
  * device memory, for callers that cannot call cudaMalloc: an engine whose
  * resident expert weights already hold the whole device, or a decode loop

@@ -1,0 +1,82 @@
+"""One rank of the expert-parallel GPU parity check (launched by
+tests/test_gpu_ep.py through torch.distributed.run, one process per GPU).
+
+Every rank builds an expert-parallel context (its E/W experts) and a
+single-GPU context holding all experts, runs the same global batch (each EP
+rank its own slice of tokens) and checks that its routing, per-slot expert
+outputs and shared-expert outputs equal the single-GPU ones bit for bit, and
+the combined output too whenever both runs use the same router kernel.
+"""
+import json
+import os
+import sys
+from datetime import timedelta
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+from oracle import oracle as O  # noqa: E402
+from hummingflight_b200.configs import GLM, LayerShape  # noqa: E402
+from hummingflight_b200.ep import broadcast_unique_id  # noqa: E402
+from hummingflight_b200.moe import MoELayer  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    cases = [("small_gemm", LayerShape(256, 16, 4, 128, 192, 2.5, True), 48, "gemm", 41),
+             ("small_auto", LayerShape(256, 16, 4, 128, 192, 2.5, True), 40, "auto", 42),
+             ("glm_auto", GLM, 16, "auto", 0)]
+    results = {}
+    for name, shape, t_local, path, wseed in cases:
+        T = t_local * world
+        xb = O.gen_x_bf16(wseed + 100, T, shape.hidden)
+        x_all = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
+        x_mine = x_all[rank * t_local:(rank + 1) * t_local].contiguous()
+        uid = broadcast_unique_id(dist, rank, dev)  # one id per communicator
+        ep = MoELayer(shape, 1, t_local, local, path, 0, rank, world, uid)
+        ep.synth_layer(0, wseed)
+        out_ep, r_ep = ep.forward(0, x_mine, routing=True, slot_out=True)
+        ep.synchronize()
+        one = MoELayer(shape, 1, T, local, path)
+        one.synth_layer(0, wseed)
+        out_one, r_one = one.forward(0, x_all, routing=True, slot_out=True)
+        one.synchronize()
+        sl = slice(rank * t_local, (rank + 1) * t_local)
+        k = min(shape.top_k, shape.num_experts)
+        # Expert products are bit-identical. The combined output is too when
+        # both runs use the same router kernel (T <= 64 on both sides); when
+        # the single-GPU batch is larger it takes the tiled router, whose
+        # different summation order can move a top-k weight by one ulp.
+        same_router = (T <= 64) == (t_local <= 64)
+        ref = out_one[sl]
+        tol = 0.0 if same_router else 1e-6 * float(ref.abs().max())
+        ok_out = float((out_ep - ref).abs().max()) <= tol
+        ok_w = float((r_ep["topk_weights"] - r_one["topk_weights"][sl]).abs().max()) <= (
+            0.0 if same_router else 1e-6)
+        ok_ids = torch.equal(r_ep["topk_ids"], r_one["topk_ids"][sl])
+        so_ep, so_one = r_ep["slot_out"], r_one["slot_out"]
+        ok_slots = torch.equal(so_ep[:t_local * k], so_one[rank * t_local * k:(rank + 1) * t_local * k])
+        ok_shared = torch.equal(so_ep[t_local * k:t_local * k + t_local],
+                                so_one[T * k + rank * t_local:T * k + (rank + 1) * t_local])
+        maxdiff = float((out_ep - out_one[sl]).abs().max())
+        results[name] = dict(out=ok_out and ok_w, ids=ok_ids, slots=ok_slots, shared=ok_shared,
+                             maxdiff=maxdiff, same_router=same_router)
+        ep.close()
+        one.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    print("EPRESULT", rank, json.dumps(results), flush=True)
+    bad = [n for n, r in results.items() if not (r["out"] and r["ids"] and r["slots"] and r["shared"])]
+    sys.exit(1 if bad else 0)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,37 @@
+"""Expert parallelism on 2 GPUs against the single-GPU layer
+(tests/ep_worker.py, one process per GPU over NCCL): routing, per-slot expert
+outputs and shared outputs bit-identical; combined outputs bit-identical
+when both runs use the same router kernel, else within 1e-6 relative.
+Skipped with fewer than two GPUs."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_expert_parallel_matches_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
+           f"--master-port={_port()}", os.path.join(HERE, "ep_worker.py")]
+    p = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    lines = [l for l in p.stdout.splitlines() if l.startswith("EPRESULT")]
+    errs = [l for l in (p.stdout + p.stderr).splitlines()
+            if "Error" in l or "error" in l or "EPRESULT" in l]
+    assert p.returncode == 0, "\n".join(errs[-60:])
+    assert len(lines) == 2, p.stdout[-2000:]
