@@ -158,12 +158,13 @@ struct ExpertWork {
     int x_f32;
     int T, k;
     float* y;          // [positions x H]
-    int bn;            // GEMM token tile the plan's tile prefixes were built with
+    int bn1, bn2, m2;  // GEMM tiles the plan's tile prefixes were built with
     bool maybe_gemm;
 };
 
 // Routing arguments of a forward on the given (source) plan.
 RouteArgs route_args(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T);
+void set_gemm_tiles(const hf_moe_ctx* c, int rows, bool x_f32, RouteArgs& ra);
 hf_status run_route(hf_moe_ctx* c, const RouteArgs& ra, cudaStream_t st);
 hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st);
 hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, float* slot_out,

@@ -265,7 +265,7 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     rl.plan = c->plan;
     rl.pl = c->pl;
     rl.T = R + T;
-    rl.gemm_bn = c->gemm_bn ? c->gemm_bn : (R + T <= 64 ? 32 : 128);
+    set_gemm_tiles(c, R + T, xd == HF_F32, rl);
     HF_TRY(launch_plan_from_counts(rl, e.loc_counts, st));
     ExpertWork w{};
     w.plan = c->plan;
@@ -276,7 +276,9 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     w.T = R + T;
     w.k = 1;
     w.y = c->y;
-    w.bn = rl.gemm_bn;
+    w.bn1 = rl.gemm_bn1;
+    w.bn2 = rl.gemm_bn2;
+    w.m2 = rl.gemm_m2;
     w.maybe_gemm = rl.gemm_ok && (c->cfg.path == HF_PATH_GEMM || maxseg > c->cfg.gemv_max_tokens);
     if (npos > 0) HF_TRY(run_experts(c, L, w, st));
 

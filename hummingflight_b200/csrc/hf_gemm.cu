@@ -42,12 +42,16 @@ struct GemmCfg {
     static constexpr int kStages0 = (220 * 1024) / kStageBytes;
     static constexpr int kStages = kStages0 > 12 ? 12 : kStages0;
     static constexpr int kAccCols = NUM_A * BN;
-    static constexpr int kCols0 = 2 * kAccCols;
+    // two accumulator buffers (epilogue of tile i overlaps MMAs of tile i+1)
+    // when they fit in the 512 TMEM columns, else one
+    static constexpr int kBufs = 2 * kAccCols <= 512 ? 2 : 1;
+    static constexpr int kCols0 = kBufs * kAccCols;
     static constexpr uint32_t kTmemCols = kCols0 <= 32 ? 32 : kCols0 <= 64 ? 64 : kCols0 <= 128 ? 128
                                           : kCols0 <= 256 ? 256 : 512;
     static constexpr int kBarOff = kStages * kStageBytes;
     static constexpr int kSmem = 1024 + kBarOff + 256;
     static_assert(kCols0 <= 512, "TMEM holds 512 columns");
+    static_assert(kStages >= 3, "pipeline needs at least 3 stages");
     static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
 };
 
@@ -78,16 +82,16 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p
     t.seg = p.off[g];
     t.n0 = ni * a.bn;
     t.n = min(a.bn, c - t.n0);
-    t.m0 = mi * 128;
+    t.m0 = mi * a.mrows;
     if (a.which == 1) {
         const int base = t.shared ? 0 : g * 3 * a.I;
         t.rowA0 = base + t.m0;
         t.rowA1 = base + Ig + t.m0;
         t.mvalid = Ig - t.m0;
         t.kblocks = (a.H + 63) / 64;
-    } else {
+    } else {  // down rows; a second accumulator takes the next 128 rows
         t.rowA0 = (t.shared ? 0 : g * 3 * a.H) + 2 * a.H + t.m0;
-        t.rowA1 = 0;
+        t.rowA1 = t.rowA0 + 128;
         t.mvalid = a.H - t.m0;
         t.kblocks = (Ig + 63) / 64;
     }
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lt) {
             TileInfo t;
             decode_tile(a, pv, u, t);
-            const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
+            const uint32_t acc = lt % C::kBufs, aph = (lt / C::kBufs) & 1;
             if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, deadline)) {
                 ok = false;
                 break;
@@ -250,31 +254,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int u = blockIdx.x; u < total; u += gridDim.x, ++lt) {
             TileInfo t;
             decode_tile(a, pv, u, t);
-            const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
+            const uint32_t acc = lt % C::kBufs, aph = (lt / C::kBufs) & 1;
             if (!mbar_wait(&tfull[acc], aph, abort_flag, deadline)) break;
             tc_fence_after();
             const uint32_t ta = tmem_base + (uint32_t(q * 32) << 16) + acc * C::kAccCols;
             const bool rv = r < t.mvalid;
+            const bool rv1 = r + 128 < t.mvalid;  // second down row block
             for (int c0 = 0; c0 < t.n; c0 += 32) {
                 uint32_t v0[32], v1[32];
                 tmem_ld32(ta + c0, v0);
                 if constexpr (NUM_A == 2) tmem_ld32(ta + BN + c0, v1);
                 tmem_ld_wait();
-                if (rv) {
+                if (NUM_A == 2 && a.which == 1) {  // gate/up pair -> SwiGLU -> hi/lo planes
+                    if (rv) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int col = c0 + j;
-                        if (col < t.n) {
-                            const size_t pos = size_t(t.seg + t.n0 + col);
-                            if constexpr (NUM_A == 2) {
+                        for (int j = 0; j < 32; ++j) {
+                            const int col = c0 + j;
+                            if (col < t.n) {
+                                const size_t pos = size_t(t.seg + t.n0 + col);
                                 const float m = swiglu(__uint_as_float(v0[j]), __uint_as_float(v1[j]));
                                 const uint16_t hi = f32_to_bf16_rne(m);
                                 const uint16_t lo = f32_to_bf16_rne(__fsub_rn(m, bf16_to_f32(hi)));
                                 a.mid_hi[pos * a.Imax + t.m0 + r] = hi;
                                 a.mid_lo[pos * a.Imax + t.m0 + r] = lo;
-                            } else {
-                                a.y[pos * a.H + t.m0 + r] = __uint_as_float(v0[j]);
                             }
+                        }
+                    }
+                } else {  // down rows m0 + r (and m0 + 128 + r) -> fp32 outputs
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int col = c0 + j;
+                        if (col < t.n) {
+                            const size_t pos = size_t(t.seg + t.n0 + col);
+                            if (rv) a.y[pos * a.H + t.m0 + r] = __uint_as_float(v0[j]);
+                            if (NUM_A == 2 && rv1) a.y[pos * a.H + t.m0 + 128 + r] = __uint_as_float(v1[j]);
                         }
                     }
                 }
@@ -346,7 +359,7 @@ static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cuda
     int smem = C::kSmem;
     args.plan_smem = (C::kSmem + plan_bytes) <= 227 * 1024;
     if (args.plan_smem) smem += plan_bytes;
-    HF_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    HF_CUDA(ensure_smem(reinterpret_cast<const void*>(kern), smem));
     kern<<<grid, kGemmThreads, smem, st>>>(m.A, m.A_sh, m.B0, m.B1, m.B0_sh, m.B1_sh, args);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
@@ -360,7 +373,10 @@ hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid,
                                           : launch_one<2, 2, 64>(m, a, grid, st);
         if (a.bn == 128) return num_b == 1 ? launch_one<2, 1, 128>(m, a, grid, st)
                                            : launch_one<2, 2, 128>(m, a, grid, st);
-    } else {
+        if (a.bn == 256 && num_b == 1) return launch_one<2, 1, 256>(m, a, grid, st);
+    } else if (a.mrows == 256) {
+        if (a.bn == 128) return launch_one<2, 2, 128>(m, a, grid, st);
+    } else if (a.mrows == 128) {
         if (a.bn == 32) return launch_one<1, 2, 32>(m, a, grid, st);
         if (a.bn == 64) return launch_one<1, 2, 64>(m, a, grid, st);
         if (a.bn == 128) return launch_one<1, 2, 128>(m, a, grid, st);

@@ -270,12 +270,10 @@ size_t gemv2_smem(int inter_max, int G) {
 hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st) {
     const size_t s1 = gemv1_smem(a.H, a.x_f32 != 0, a.pl.G);
     if (a.x_f32) {
-        HF_CUDA(cudaFuncSetAttribute(k_gemv1<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)s1));
+        HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_gemv1<true>), (int)s1));
         k_gemv1<true><<<a.grid1, 256, s1, st>>>(a);
     } else {
-        HF_CUDA(cudaFuncSetAttribute(k_gemv1<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)s1));
+        HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_gemv1<false>), (int)s1));
         k_gemv1<false><<<a.grid1, 256, s1, st>>>(a);
     }
     HF_CUDA(cudaGetLastError());
@@ -284,7 +282,7 @@ hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st) {
 
 hf_status launch_gemv2(const GemvArgs& a, cudaStream_t st) {
     const size_t s2 = gemv2_smem(a.inter_max, a.pl.G);
-    HF_CUDA(cudaFuncSetAttribute(k_gemv2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2));
+    HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_gemv2), (int)s2));
     k_gemv2<<<a.grid2, 256, s2, st>>>(a);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
@@ -314,17 +312,31 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
     const size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= size_t(a.T) * H4) return;
     const int t = int(idx / H4), h = int(idx % H4) * 4;
+    // all loads first (independent), then the accumulation in rank order
+    int pos[kMaxTopK];
+    float wt[kMaxTopK];
+    float4 yv[kMaxTopK];
+#pragma unroll
+    for (int i = 0; i < kMaxTopK; ++i)
+        if (i < a.k) {
+            pos[i] = a.slot_pos[t * a.k + i];
+            wt[i] = a.w[t * a.k + i];
+        }
+#pragma unroll
+    for (int i = 0; i < kMaxTopK; ++i)
+        if (i < a.k) yv[i] = *reinterpret_cast<const float4*>(a.y + size_t(pos[i]) * a.H + h);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = 0; i < a.k; ++i) {
-        const int slot = t * a.k + i;
-        const int pos = a.slot_pos[slot];
-        const float wi = a.w[slot];
-        const float4 y = *reinterpret_cast<const float4*>(a.y + size_t(pos) * a.H + h);
+#pragma unroll
+    for (int i = 0; i < kMaxTopK; ++i) {
+        if (i >= a.k) break;
+        const float wi = wt[i];
+        const float4 y = yv[i];
         acc.x = __fadd_rn(acc.x, __fmul_rn(wi, y.x));
         acc.y = __fadd_rn(acc.y, __fmul_rn(wi, y.y));
         acc.z = __fadd_rn(acc.z, __fmul_rn(wi, y.z));
         acc.w = __fadd_rn(acc.w, __fmul_rn(wi, y.w));
-        if (a.slot_out) *reinterpret_cast<float4*>(a.slot_out + size_t(slot) * a.H + h) = y;
+        if (a.slot_out)
+            *reinterpret_cast<float4*>(a.slot_out + size_t(t * a.k + i) * a.H + h) = y;
     }
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
     if (a.has_shared) {

@@ -99,7 +99,8 @@ struct RouteArgs {
     int path;                 // hf_path
     int gemv_max;             // AUTO threshold
     int gemm_ok;              // shapes allow the tcgen05 GEMM (64-aligned)
-    int gemm_bn;              // GEMM token tile (columns per tile)
+    int gemm_bn1, gemm_bn2;   // token tile (columns per tile) of GEMM1 / GEMM2
+    int gemm_m2;              // weight rows per GEMM2 tile (128 or 256)
 };
 
 // ------------------------------------------------------------------ device helpers
@@ -186,6 +187,8 @@ __device__ __forceinline__ int find_group(const int32_t* prefix, int G, int u) {
 
 // ------------------------------------------------------------------ launchers
 int num_sms(int device);
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device, size).
+cudaError_t ensure_smem(const void* kernel, int bytes);
 
 hf_status launch_router_logits(const RouteArgs& a, cudaStream_t st);
 // Work plan (counts, offsets, unit and tile prefixes) from per-group counts
@@ -226,6 +229,7 @@ struct GemmArgs {
     PlanLayout pl;
     int which;              // 1: gate/up + SwiGLU -> mid hi/lo; 2: down -> y
     int H, I, Is, Imax, bn;
+    int mrows;              // weight rows per tile: 128, or 256 for GEMM2 with two row blocks
     uint16_t* mid_hi;       // [slots x Imax] bf16
     uint16_t* mid_lo;
     float* y;               // [slots x H] fp32

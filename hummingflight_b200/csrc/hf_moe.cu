@@ -11,6 +11,8 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -39,6 +41,20 @@ int num_sms(int device) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
         n = 148;
     return n;
+}
+
+cudaError_t ensure_smem(const void* kernel, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> bytes set
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    int& have = done[{kernel, dev}];
+    if (have >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) have = bytes;
+    return e;
 }
 
 // ------------------------------------------------------------------ phases
@@ -70,9 +86,30 @@ RouteArgs route_args(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     ra.path = c->cfg.path;
     ra.gemv_max = c->cfg.gemv_max_tokens;
     ra.gemm_ok = c->gemm_ok && L.maps;
-    // decode: narrow token tiles leave room for a deeper weight ring
-    ra.gemm_bn = c->gemm_bn ? c->gemm_bn : (T <= 64 ? 32 : 128);
+    set_gemm_tiles(c, T, xd == HF_F32, ra);
     return ra;
+}
+
+// Token tiles of the two grouped GEMMs for a pass over `rows` activation rows.
+// Decode (<= 64 rows): narrow 32-column tiles leave room for a deeper weight
+// ring. Prefill (>= 1024 rows): gate/up tiles of 256 tokens and down tiles of
+// 256 weight rows x 128 tokens, which halve the shared-memory operand bytes
+// per MMA flop against 128 x 128 tiles.
+void set_gemm_tiles(const hf_moe_ctx* c, int rows, bool x_f32, RouteArgs& ra) {
+    if (c->gemm_bn) {
+        ra.gemm_bn1 = ra.gemm_bn2 = c->gemm_bn;
+        ra.gemm_m2 = 128;
+    } else if (rows <= 64) {
+        ra.gemm_bn1 = ra.gemm_bn2 = 32;
+        ra.gemm_m2 = 128;
+    } else if (rows < 1024) {
+        ra.gemm_bn1 = ra.gemm_bn2 = 128;
+        ra.gemm_m2 = 128;
+    } else {
+        ra.gemm_bn1 = x_f32 ? 128 : 256;
+        ra.gemm_bn2 = 128;
+        ra.gemm_m2 = 256;
+    }
 }
 
 hf_status run_route(hf_moe_ctx* c, const RouteArgs& ra, cudaStream_t st) {
@@ -89,7 +126,6 @@ hf_status run_route(hf_moe_ctx* c, const RouteArgs& ra, cudaStream_t st) {
 }
 
 hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st) {
-    const int bn = w.bn;
     if (w.maybe_gemm) {
         GatherArgs gx{};
         gx.plan = w.plan;
@@ -136,7 +172,8 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.I = c->I;
         gm.Is = c->Is;
         gm.Imax = c->inter_max;
-        gm.bn = bn;
+        gm.bn = w.bn1;
+        gm.mrows = 128;
         gm.mid_hi = c->mid_hi;
         gm.mid_lo = c->mid_lo;
         gm.y = w.y;
@@ -157,6 +194,8 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
     }
     if (w.maybe_gemm) {
         gm.which = 2;
+        gm.bn = w.bn2;
+        gm.mrows = w.m2;
         GemmMaps m2 = c->maps2;
         m2.A = L.dn;
         m2.A_sh = L.dn_sh;
@@ -581,7 +620,9 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
         w.T = T;
         w.k = c->k;
         w.y = c->y;
-        w.bn = ra.gemm_bn;
+        w.bn1 = ra.gemm_bn1;
+        w.bn2 = ra.gemm_bn2;
+        w.m2 = ra.gemm_m2;
         // segments can only exceed the GEMV threshold when T does
         w.maybe_gemm = ra.gemm_ok && (c->cfg.path == HF_PATH_GEMM || T > c->cfg.gemv_max_tokens);
         HF_TRY(run_experts(c, L, w, st));

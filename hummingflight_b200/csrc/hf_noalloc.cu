@@ -115,7 +115,8 @@ extern "C" hf_status hf_moe_route_noalloc(const uint16_t* router_bf16, const flo
     a.path = HF_PATH_GEMV;
     a.gemv_max = 1 << 30;
     a.gemm_ok = 0;
-    a.gemm_bn = 64;
+    a.gemm_bn1 = a.gemm_bn2 = 64;
+    a.gemm_m2 = 128;
     HF_TRY(launch_router_logits(a, st));
     int n = 0;
     HF_TRY(launch_route(a, st, &n));

@@ -258,43 +258,7 @@ __global__ void __launch_bounds__(256) k_topk(const float* scores, int T, int E,
                    nullptr);
 }
 
-// ============================================================ block helpers (1024 threads)
-// Exclusive scan of n <= 2048 ints in shared memory (in place), returns total.
-__device__ int block_scan_excl(int* data, int n, int* warp_tot) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int i0 = 2 * tid, i1 = 2 * tid + 1;
-    const int v0 = (i0 < n) ? data[i0] : 0;
-    const int v1 = (i1 < n) ? data[i1] : 0;
-    int s = v0 + v1;
-    int incl = s;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-        int wv = (lane < (int)(blockDim.x >> 5)) ? warp_tot[lane] : 0;
-        int wi = wv;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, wi, o);
-            if (lane >= o) wi += y;
-        }
-        warp_tot[lane] = wi - wv;  // exclusive prefix of warps
-        if (lane == 31) warp_tot[32] = wi;
-    }
-    __syncthreads();
-    const int base = warp_tot[warp] + incl - s;
-    if (i0 < n) data[i0] = base;
-    if (i1 < n) data[i1] = base + v0;
-    __syncthreads();
-    const int total = warp_tot[32];
-    __syncthreads();
-    return total;
-}
-
+// ============================================================ work plan (one block)
 // Path of one expert segment: the grouped GEMV for short segments (AUTO) or
 // always (GEMV, or shapes the tcgen05 tiles do not cover); else the GEMM.
 __device__ __forceinline__ bool segment_uses_gemv(const RouteArgs& a, int c, int I) {
@@ -304,68 +268,94 @@ __device__ __forceinline__ bool segment_uses_gemv(const RouteArgs& a, int c, int
     return c <= a.gemv_max;
 }
 
-// From per-group counts (shared memory, s_cnt[G]) write counts, offsets, the
-// GEMV/GEMM work plan and the stats into the plan buffer. s_tmp: >= G+1 ints.
-__device__ void plan_from_counts(const RouteArgs& a, const int* s_cnt, int* s_tmp, int* warp_tot) {
-    const int G = a.pl.G;
-    int32_t* plan = a.plan;
-    const int H = a.H;
-    // offsets
-    for (int g = threadIdx.x; g < G; g += blockDim.x) {
-        plan[a.pl.counts + g] = s_cnt[g];
-        s_tmp[g] = s_cnt[g];
+constexpr int kPlanVals = 8;  // per group: count, GEMV1/GEMV2 units, GEMM1/GEMM2 tiles, 3 stats
+constexpr int kPlanScratch = 33 * kPlanVals;  // ints of warp_tot
+
+// From per-group counts (shared memory s_cnt[G], G <= 2 * blockDim.x) write
+// counts, offsets, the GEMV unit and GEMM tile prefixes and the stats into the
+// plan buffer, and the offsets also into s_off[G+1]. One fused block scan of
+// eight values per group: two barriers.
+__device__ void plan_from_counts(const RouteArgs& a, const int* s_cnt, int* s_off, int* warp_tot) {
+    const int G = a.pl.G, H = a.H;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nwarps = int(blockDim.x >> 5);
+    int v[2][kPlanVals];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int g = 2 * tid + q;
+        const int c = g < G ? s_cnt[g] : 0;
+        const int I = (g == G - 1) ? a.shared_inter : a.inter;
+        const bool gemv = g < G && segment_uses_gemv(a, c, I);
+        const bool gemm = g < G && c > 0 && I > 0 && !gemv;
+        const int nch = (c + kGemvTE - 1) / kGemvTE;
+        const int nt1 = gemm ? (c + a.gemm_bn1 - 1) / a.gemm_bn1 : 0;
+        const int nt2 = gemm ? (c + a.gemm_bn2 - 1) / a.gemm_bn2 : 0;
+        v[q][0] = c;
+        v[q][1] = gemv ? nch * ((I + kGemv1Rows - 1) / kGemv1Rows) : 0;
+        v[q][2] = gemv ? nch * ((H + kGemv2Rows - 1) / kGemv2Rows) : 0;
+        v[q][3] = nt1 * ((I + 127) / 128);
+        v[q][4] = nt2 * ((H + a.gemm_m2 - 1) / a.gemm_m2);
+        v[q][5] = (g < G - 1 && c > 0) ? 1 : 0;
+        v[q][6] = gemv ? 1 : 0;
+        v[q][7] = gemm ? 1 : 0;
     }
-    __syncthreads();
-    int tot = block_scan_excl(s_tmp, G, warp_tot);
-    for (int g = threadIdx.x; g < G; g += blockDim.x) plan[a.pl.offsets + g] = s_tmp[g];
-    if (threadIdx.x == 0) plan[a.pl.offsets + G] = tot;
-    __syncthreads();
-    // work units: GEMV1, GEMV2 (per token chunk and row block), GEMM1, GEMM2
-    // (per 128-row tile and token tile)
-    for (int pass = 0; pass < 4; ++pass) {
-        for (int g = threadIdx.x; g < G; g += blockDim.x) {
-            const int c = s_cnt[g];
-            const int I = (g == G - 1) ? a.shared_inter : a.inter;
-            const bool gemv = segment_uses_gemv(a, c, I);
-            const bool gemm = c > 0 && I > 0 && !gemv;
-            const int nch = (c + kGemvTE - 1) / kGemvTE;
-            const int nt = gemm ? (c + a.gemm_bn - 1) / a.gemm_bn : 0;
-            int v = 0;
-            if (pass == 0) v = gemv ? nch * ((I + kGemv1Rows - 1) / kGemv1Rows) : 0;
-            if (pass == 1) v = gemv ? nch * ((H + kGemv2Rows - 1) / kGemv2Rows) : 0;
-            if (pass == 2) v = nt * ((I + 127) / 128);
-            if (pass == 3) v = nt * ((H + 127) / 128);
-            s_tmp[g] = v;
+    int sum[kPlanVals], incl[kPlanVals];
+#pragma unroll
+    for (int i = 0; i < kPlanVals; ++i) {
+        sum[i] = v[0][i] + v[1][i];
+        incl[i] = sum[i];
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < kPlanVals; ++i) {
+            const int y = __shfl_up_sync(0xffffffffu, incl[i], o);
+            if (lane >= o) incl[i] += y;
         }
-        __syncthreads();
-        tot = block_scan_excl(s_tmp, G, warp_tot);
-        const int dst = pass == 0 ? a.pl.u1 : pass == 1 ? a.pl.u2 : pass == 2 ? a.pl.g1 : a.pl.g2;
-        for (int g = threadIdx.x; g < G; g += blockDim.x) plan[dst + g] = s_tmp[g];
-        if (threadIdx.x == 0) plan[dst + G] = tot;
-        __syncthreads();
+    if (lane == 31)
+#pragma unroll
+        for (int i = 0; i < kPlanVals; ++i) warp_tot[warp * kPlanVals + i] = incl[i];
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int i = 0; i < kPlanVals; ++i) {
+            const int wv = lane < nwarps ? warp_tot[lane * kPlanVals + i] : 0;
+            int wi = wv;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += y;
+            }
+            warp_tot[lane * kPlanVals + i] = wi - wv;  // exclusive prefix of warps
+            if (lane == 31) warp_tot[32 * kPlanVals + i] = wi;
+        }
     }
-    // stats: active routed experts, gemv segments, gemm segments
-    if (threadIdx.x < 32) {
-        int act = 0, gv = 0, gm = 0;
-        for (int g = threadIdx.x; g < G; g += 32) {
-            const int c = s_cnt[g];
-            const int I = (g == G - 1) ? a.shared_inter : a.inter;
-            if (c > 0 && g < G - 1) ++act;
-            const bool gemv = segment_uses_gemv(a, c, I);
-            if (gemv) ++gv;
-            else if (c > 0 && I > 0) ++gm;
+    __syncthreads();
+    int32_t* plan = a.plan;
+    const int dst[5] = {a.pl.offsets, a.pl.u1, a.pl.u2, a.pl.g1, a.pl.g2};
+    int base[kPlanVals];
+#pragma unroll
+    for (int i = 0; i < kPlanVals; ++i) base[i] = warp_tot[warp * kPlanVals + i] + incl[i] - sum[i];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int g = 2 * tid + q;
+        if (g < G) {
+            plan[a.pl.counts + g] = v[q][0];
+            s_off[g] = base[0];
+#pragma unroll
+            for (int i = 0; i < 5; ++i) plan[dst[i] + g] = base[i];
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            act += __shfl_xor_sync(0xffffffffu, act, o);
-            gv += __shfl_xor_sync(0xffffffffu, gv, o);
-            gm += __shfl_xor_sync(0xffffffffu, gm, o);
-        }
-        if (threadIdx.x == 0) {
-            plan[a.pl.stats + 0] = act;
-            plan[a.pl.stats + 1] = gv;
-            plan[a.pl.stats + 2] = gm;
-        }
+        for (int i = 0; i < kPlanVals; ++i) base[i] += v[q][i];
+    }
+    if (tid == 0) {
+        const int* tot = warp_tot + 32 * kPlanVals;
+        s_off[G] = tot[0];
+#pragma unroll
+        for (int i = 0; i < 5; ++i) plan[dst[i] + G] = tot[i];
+        plan[a.pl.stats + 0] = tot[5];
+        plan[a.pl.stats + 1] = tot[6];
+        plan[a.pl.stats + 2] = tot[7];
     }
     __syncthreads();
 }
@@ -378,23 +368,34 @@ __device__ __forceinline__ int mask_rank(const uint32_t* m, int tl) {
     return r + __popc(m[w] & ((1u << (tl & 31)) - 1u));
 }
 
-// ============================================================ T <= 128: one block does it all
-template <int NPL>
-__global__ void __launch_bounds__(1024) k_route_small(RouteArgs a) {
+// ============================================================ T <= 128: one block
+// One block builds the masks, counts, plan and permutation of up to 128
+// tokens. With TOPK it first runs their top-k itself (one warp per token;
+// used for a handful of tokens, where a separate launch costs more than it
+// saves); otherwise the top-k already ran one warp per token on many SMs.
+constexpr int kFusedTopkMaxT = 16;
+
+template <int NPL, bool TOPK>
+__global__ void __launch_bounds__(1024) k_route_block(RouteArgs a) {
     extern __shared__ __align__(16) uint32_t sm[];
     const int E = a.E, T = a.T, k = a.k, G = a.pl.G;
     uint32_t* masks = sm;                                   // [E][4]
     int* s_cnt = reinterpret_cast<int*>(masks + 4 * E);     // [G]
     int* s_off = s_cnt + G;                                  // [G+1]
     int* s_ids = s_off + G + 1;                              // [128 * 8]
-    int* warp_tot = s_ids + kSmallRouteT * kMaxTopK;         // [33]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int* warp_tot = s_ids + kSmallRouteT * kMaxTopK;         // [kPlanScratch]
 
     for (int i = threadIdx.x; i < 4 * E; i += blockDim.x) masks[i] = 0u;
-    for (int t = warp; t < T; t += 32)
-        topk_warp<NPL>(a.logits + size_t(t) * E, 1, a.bias, E, k, a.scale, a.norm, lane,
-                       a.ids + size_t(t) * k, a.w + size_t(t) * k,
-                       a.margins ? a.margins + t : nullptr, s_ids + t * kMaxTopK);
+    if constexpr (TOPK) {
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int t = warp; t < T; t += 32)
+            topk_warp<NPL>(a.logits + size_t(t) * E, 1, a.bias, E, k, a.scale, a.norm, lane,
+                           a.ids + size_t(t) * k, a.w + size_t(t) * k,
+                           a.margins ? a.margins + t : nullptr, s_ids + t * kMaxTopK);
+    } else {
+        for (int i = threadIdx.x; i < T * k; i += blockDim.x)
+            s_ids[(i / k) * kMaxTopK + i % k] = a.ids[i];
+    }
     __syncthreads();
     for (int i = threadIdx.x; i < T * k; i += blockDim.x) {
         const int t = i / k, e = s_ids[t * kMaxTopK + i % k];
@@ -410,9 +411,6 @@ __global__ void __launch_bounds__(1024) k_route_small(RouteArgs a) {
     }
     __syncthreads();
     plan_from_counts(a, s_cnt, s_off, warp_tot);
-    // s_off now holds the last scan (gemm segments); reload offsets from plan
-    for (int g = threadIdx.x; g <= G; g += blockDim.x) s_off[g] = a.plan[a.pl.offsets + g];
-    __syncthreads();
     for (int i = threadIdx.x; i < T * k; i += blockDim.x) {
         const int t = i / k, e = s_ids[t * kMaxTopK + i % k];
         const int pos = s_off[e] + mask_rank(&masks[4 * e], t);
@@ -487,7 +485,7 @@ __global__ void __launch_bounds__(1024) k_plan_counts(RouteArgs a, const int32_t
 
 hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cudaStream_t st) {
     const int G = a.pl.G;
-    const size_t smem = sizeof(int) * (G + G + 1 + 33);
+    const size_t smem = sizeof(int) * (G + G + 1 + kPlanScratch);
     k_plan_counts<<<1, 1024, smem, st>>>(a, counts);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
@@ -572,18 +570,26 @@ hf_status launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
     *launches = 0;
     if (a.T == 0) return HF_OK;
     const int G = a.pl.G;
-    *launches = a.T <= kSmallRouteT ? 1 : 4;
     if (a.T <= kSmallRouteT) {
-        const size_t smem = sizeof(uint32_t) * (4 * a.E + G + G + 1 + kSmallRouteT * kMaxTopK + 33);
-        HF_NPL_SWITCH(a.E, {
-            auto kern = k_route_small<NPL>;
-            HF_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem));
-            kern<<<1, 1024, smem, st>>>(a);
-        });
+        const size_t smem =
+            sizeof(uint32_t) * (4 * a.E + G + G + 1 + kSmallRouteT * kMaxTopK + kPlanScratch);
+        if (a.T <= kFusedTopkMaxT) {
+            *launches = 1;
+            HF_NPL_SWITCH(a.E, { k_route_block<NPL, true><<<1, 1024, smem, st>>>(a); });
+        } else {
+            *launches = 2;
+            HF_NPL_SWITCH(a.E, {
+                k_topk<NPL><<<(a.T + 7) / 8, 256, 0, st>>>(a.logits, a.T, a.E, a.bias, a.k,
+                                                           a.scale, a.norm, 1, a.ids, a.w,
+                                                           a.margins);
+            });
+            HF_CUDA(cudaGetLastError());
+            k_route_block<1, false><<<1, 1024, smem, st>>>(a);
+        }
         HF_CUDA(cudaGetLastError());
         return HF_OK;
     }
+    *launches = 4;
     const int nb = (a.T + kSmallRouteT - 1) / kSmallRouteT;
     HF_NPL_SWITCH(a.E, {
         k_topk<NPL><<<(a.T + 7) / 8, 256, 0, st>>>(a.logits, a.T, a.E, a.bias, a.k, a.scale,
@@ -592,7 +598,7 @@ hf_status launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
     HF_CUDA(cudaGetLastError());
     k_perm_masks<<<nb, 256, 0, st>>>(a);
     HF_CUDA(cudaGetLastError());
-    const size_t smem = sizeof(int) * (G + G + 1 + 33);
+    const size_t smem = sizeof(int) * (G + G + 1 + kPlanScratch);
     k_perm_plan<<<1, 1024, smem, st>>>(a, nb);
     HF_CUDA(cudaGetLastError());
     k_perm_scatter<<<nb, 256, 0, st>>>(a);

@@ -59,6 +59,33 @@ def test_small_layer_gemm_matches_oracle(T, path, gemv_max, xdt):
     L.close()
 
 
+@pytest.mark.parametrize("T", [1024, 1500])
+@pytest.mark.parametrize("H", [192, 320])
+@pytest.mark.parametrize("xdt", ["bf16", "f32"])
+def test_prefill_tiles_match_oracle(T, H, xdt):
+    """From 1024 rows the gate/up GEMM takes 256-token tiles (bf16 input) and
+    the down GEMM 256 weight rows a tile; H = 192 and 320 leave the second
+    128-row block partly or wholly past the end, and per-expert segments of
+    ~T/4 rows leave ragged last token tiles."""
+    need_gpu()
+    E, K, I, Is = 16, 4, 128, 192
+    shape = LayerShape(H, E, K, I, Is, 2.5, True)
+    L = layer(shape, 45, T, "gemm")
+    x, xb = x_dev(46 + T, T, H, xdt)
+    out, r = L.forward(0, x, routing=True, slot_out=True)
+    L.synchronize()
+    assert L.last_stats()["gemm_segments"] == E + 1
+    orc = O.moe_layer_synth(O.Dims(H, E, K, I, Is), 45, 0, O.bf16_to_f32(xb).reshape(T, H),
+                            want_slots=True)
+    ids = check_routing(r, orc["ids"], orc["margins"], E)
+    assert np.array_equal(ids, orc["ids"])
+    close(out.cpu().numpy(), orc["out"], f"T={T} H={H}")
+    so = r["slot_out"].cpu().numpy()
+    close(so[:T * K], orc["slots"][:T * K], "routed slots")
+    close(so[T * K:T * K + T], orc["slots"][T * K:], "shared slots")
+    L.close()
+
+
 def test_gemm_and_gemv_paths_agree_on_glm_decode():
     need_gpu()
     wl = WORKLOADS[1]
