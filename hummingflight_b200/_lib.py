@@ -73,6 +73,7 @@ SIGNATURES = {
     "hf_topk_scores": (c_int, [c_vp, c_int, c_int, c_vp, c_int, c_float, c_int, c_vp, c_vp, c_vp]),
     "hf_dense_mlp_workspace_size": (c_size, [c_int, c_int, c_int]),
     "hf_dense_mlp_forward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_size, c_vp]),
+    "hf_dense_mlp_status": (c_int, [c_vp, c_vp]),
     "hf_synth_bf16_normal": (c_int, [c_vp, c_u64, c_u64, c_u32, c_u32, c_u32, ctypes.c_double, c_vp]),
     "hf_synth_f32_uniform": (c_int, [c_vp, c_u64, c_u64, c_u32, c_u32, c_u32, c_float, c_float, c_vp]),
     "hf_moe_synth_layer": (c_int, [c_vp, c_int, c_u64, c_u32, c_vp, c_vp]),

@@ -35,8 +35,8 @@ struct LayerBuf {
     GroupW* groups = nullptr;    // [G] device table: local experts, then shared
     bool loaded = false;
     // TMA views of the weights for the tcgen05 GEMM (built with the buffers)
-    CUtensorMap gu{}, gu_sh{};   // gate/up rows: H-wide rows of [gate|up|down]
-    CUtensorMap dn{}, dn_sh{};   // down rows: I-wide rows of the same buffers
+    CUtensorMap gu{}, dn{};      // routed: H-wide / I-wide rows of the [gate|up|down] blocks
+    CUtensorMap sh_gate{}, sh_up{}, sh_down{};  // shared expert: one view per matrix
     bool maps = false;
 };
 
@@ -164,7 +164,6 @@ struct ExpertWork {
 
 // Routing arguments of a forward on the given (source) plan.
 RouteArgs route_args(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T);
-void set_gemm_tiles(const hf_moe_ctx* c, int rows, bool x_f32, RouteArgs& ra);
 hf_status run_route(hf_moe_ctx* c, const RouteArgs& ra, cudaStream_t st);
 hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st);
 hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, float* slot_out,

@@ -265,7 +265,7 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     rl.plan = c->plan;
     rl.pl = c->pl;
     rl.T = R + T;
-    set_gemm_tiles(c, R + T, xd == HF_F32, rl);
+    set_gemm_tiles(c->gemm_bn, R + T, rl);
     HF_TRY(launch_plan_from_counts(rl, e.loc_counts, st));
     ExpertWork w{};
     w.plan = c->plan;

@@ -83,14 +83,16 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p
     t.n0 = ni * a.bn;
     t.n = min(a.bn, c - t.n0);
     t.m0 = mi * a.mrows;
+    // routed experts: one [gate|up|down] block per expert in one view; the
+    // shared expert: separate gate, up and down views
     if (a.which == 1) {
-        const int base = t.shared ? 0 : g * 3 * a.I;
-        t.rowA0 = base + t.m0;
-        t.rowA1 = base + Ig + t.m0;
+        const int base = g * 3 * a.I;
+        t.rowA0 = t.shared ? t.m0 : base + t.m0;
+        t.rowA1 = t.shared ? t.m0 : base + Ig + t.m0;
         t.mvalid = Ig - t.m0;
         t.kblocks = (a.H + 63) / 64;
     } else {  // down rows; a second accumulator takes the next 128 rows
-        t.rowA0 = (t.shared ? 0 : g * 3 * a.H) + 2 * a.H + t.m0;
+        t.rowA0 = t.shared ? t.m0 : g * 3 * a.H + 2 * a.H + t.m0;
         t.rowA1 = t.rowA0 + 128;
         t.mvalid = a.H - t.m0;
         t.kblocks = (Ig + 63) / 64;
@@ -107,6 +109,7 @@ __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
 template <int NUM_A, int NUM_B, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_moe_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_sh,
+               const __grid_constant__ CUtensorMap tmA_sh2,
                const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
                const __grid_constant__ CUtensorMap tmB0_sh,
                const __grid_constant__ CUtensorMap tmB1_sh, GemmArgs a) {
@@ -175,6 +178,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int nb = (t.n + kBoxRowsB - 1) / kBoxRowsB;
             const uint32_t bytes = NUM_A * kTileABytes + NUM_B * nb * (kBoxRowsB * 128);
             const CUtensorMap* mA = t.shared ? &tmA_sh : &tmA;
+            const CUtensorMap* mA1 = (t.shared && a.which == 1) ? &tmA_sh2 : mA;
             const CUtensorMap* mB0 = (a.which == 2 && t.shared) ? &tmB0_sh : &tmB0;
             const CUtensorMap* mB1 = (a.which == 2 && t.shared) ? &tmB1_sh : &tmB1;
             for (int kb = 0; kb < t.kblocks; ++kb, ++it) {
@@ -186,7 +190,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 uint8_t* st = smem + s * C::kStageBytes;
                 mbar_arrive_expect_tx(&full[s], bytes);
                 tma_load_2d(st, mA, &full[s], kb * 64, t.rowA0);
-                if (NUM_A == 2) tma_load_2d(st + kTileABytes, mA, &full[s], kb * 64, t.rowA1);
+                if (NUM_A == 2) tma_load_2d(st + kTileABytes, mA1, &full[s], kb * 64, t.rowA1);
                 uint8_t* sb = st + NUM_A * kTileABytes;
                 for (int j = 0; j < nb; ++j) {
                     const int row = t.seg + t.n0 + j * kBoxRowsB;
@@ -360,7 +364,7 @@ static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cuda
     args.plan_smem = (C::kSmem + plan_bytes) <= 227 * 1024;
     if (args.plan_smem) smem += plan_bytes;
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(kern), smem));
-    kern<<<grid, kGemmThreads, smem, st>>>(m.A, m.A_sh, m.B0, m.B1, m.B0_sh, m.B1_sh, args);
+    kern<<<grid, kGemmThreads, smem, st>>>(m.A, m.A_sh, m.A_sh2, m.B0, m.B1, m.B0_sh, m.B1_sh, args);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }
@@ -373,7 +377,6 @@ hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid,
                                           : launch_one<2, 2, 64>(m, a, grid, st);
         if (a.bn == 128) return num_b == 1 ? launch_one<2, 1, 128>(m, a, grid, st)
                                            : launch_one<2, 2, 128>(m, a, grid, st);
-        if (a.bn == 256 && num_b == 1) return launch_one<2, 1, 256>(m, a, grid, st);
     } else if (a.mrows == 256) {
         if (a.bn == 128) return launch_one<2, 2, 128>(m, a, grid, st);
     } else if (a.mrows == 128) {

@@ -191,9 +191,15 @@ int num_sms(int device);
 cudaError_t ensure_smem(const void* kernel, int bytes);
 
 hf_status launch_router_logits(const RouteArgs& a, cudaStream_t st);
+// GEMM tiles (gemm_bn1, gemm_bn2, gemm_m2) for a pass over `rows` activation
+// rows; bn_override (32, 64 or 128) forces both token tiles when non-zero.
+void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra);
 // Work plan (counts, offsets, unit and tile prefixes) from per-group counts
 // already in device memory (expert-parallel receivers, dense MLP).
 hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cudaStream_t st);
+// Dense MLP pass: one group of all T tokens in order; writes groups[0] = w.
+hf_status launch_dense_plan(const RouteArgs& a, const GroupW& w, GroupW* groups, int32_t* perm,
+                            cudaStream_t st);
 // dst row i = src row (idx[i] / div), i < n; rows of row_bytes (multiple of 16).
 hf_status launch_gather_rows(void* dst, const void* src, size_t row_bytes, int n,
                              const int32_t* idx, int div, cudaStream_t st);
@@ -239,7 +245,8 @@ struct GemmArgs {
     int plan_smem;          // set by the launcher: plan arrays staged in shared memory
 };
 struct GemmMaps {
-    CUtensorMap A, A_sh;       // weights (routed view, shared expert view)
+    CUtensorMap A, A_sh;       // weights: routed view; shared expert gate (GEMM1) or down rows
+    CUtensorMap A_sh2;         // shared expert up rows (GEMM1)
     CUtensorMap B0, B1;        // activations (hi, lo planes), routed K extent
     CUtensorMap B0_sh, B1_sh;  // the same with the shared expert's K extent
 };

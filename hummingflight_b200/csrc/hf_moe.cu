@@ -86,29 +86,27 @@ RouteArgs route_args(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     ra.path = c->cfg.path;
     ra.gemv_max = c->cfg.gemv_max_tokens;
     ra.gemm_ok = c->gemm_ok && L.maps;
-    set_gemm_tiles(c, T, xd == HF_F32, ra);
+    set_gemm_tiles(c->gemm_bn, T, ra);
     return ra;
 }
 
-// Token tiles of the two grouped GEMMs for a pass over `rows` activation rows.
-// Decode (<= 64 rows): narrow 32-column tiles leave room for a deeper weight
-// ring. Prefill (>= 1024 rows): gate/up tiles of 256 tokens and down tiles of
-// 256 weight rows x 128 tokens, which halve the shared-memory operand bytes
-// per MMA flop against 128 x 128 tiles.
-void set_gemm_tiles(const hf_moe_ctx* c, int rows, bool x_f32, RouteArgs& ra) {
-    if (c->gemm_bn) {
-        ra.gemm_bn1 = ra.gemm_bn2 = c->gemm_bn;
+// Tiles of the two grouped GEMMs for a pass over `rows` activation rows.
+// Decode (<= 64 rows): narrow 32-token tiles leave room for a deeper weight
+// ring. Prefill (>= 1024 rows): down tiles of 256 weight rows x 128 tokens
+// load each activation tile once per 256 output rows (a third fewer operand
+// bytes per MMA flop than 128 x 128). Gate/up keeps 128 x 128 tiles with two
+// accumulators: at 256 tokens the single TMEM buffer it would need measured
+// slower.
+void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
+    if (bn_override) {
+        ra.gemm_bn1 = ra.gemm_bn2 = bn_override;
         ra.gemm_m2 = 128;
     } else if (rows <= 64) {
         ra.gemm_bn1 = ra.gemm_bn2 = 32;
         ra.gemm_m2 = 128;
-    } else if (rows < 1024) {
-        ra.gemm_bn1 = ra.gemm_bn2 = 128;
-        ra.gemm_m2 = 128;
     } else {
-        ra.gemm_bn1 = x_f32 ? 128 : 256;
-        ra.gemm_bn2 = 128;
-        ra.gemm_m2 = 256;
+        ra.gemm_bn1 = ra.gemm_bn2 = 128;
+        ra.gemm_m2 = rows < 1024 ? 128 : 256;
     }
 }
 
@@ -182,7 +180,8 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.test_stall = c->stall;
         GemmMaps m1 = c->maps1;
         m1.A = L.gu;
-        m1.A_sh = L.gu_sh;
+        m1.A_sh = L.sh_gate;
+        m1.A_sh2 = L.sh_up;
         PhaseTimer p4(c, st, 4);
         HF_TRY(launch_gemm(m1, gm, w.x_f32 ? 2 : 1, c->nsm, st));
         p4.done(1);
@@ -198,7 +197,8 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.mrows = w.m2;
         GemmMaps m2 = c->maps2;
         m2.A = L.dn;
-        m2.A_sh = L.dn_sh;
+        m2.A_sh = L.sh_down;
+        m2.A_sh2 = L.sh_down;
         PhaseTimer p5(c, st, 5);
         HF_TRY(launch_gemm(m2, gm, 2, c->nsm, st));
         p5.done(1);
@@ -472,11 +472,13 @@ static hf_status layer_alloc(hf_moe_ctx* c, int layer) {
         HF_TRY(make_map_bf16(&L.gu, L.experts, c->H, el * 3 * c->I, c->H, 128));
         HF_TRY(make_map_bf16(&L.dn, L.experts, c->I, el * 3 * c->H, c->I, 128));
         if (c->Is > 0) {
-            HF_TRY(make_map_bf16(&L.gu_sh, L.shared, c->H, 3ull * c->Is, c->H, 128));
-            HF_TRY(make_map_bf16(&L.dn_sh, L.shared, c->Is, 3ull * c->H, c->Is, 128));
+            const size_t n = size_t(c->Is) * c->H;
+            HF_TRY(make_map_bf16(&L.sh_gate, L.shared, c->H, c->Is, c->H, 128));
+            HF_TRY(make_map_bf16(&L.sh_up, L.shared + n, c->H, c->Is, c->H, 128));
+            HF_TRY(make_map_bf16(&L.sh_down, L.shared + 2 * n, c->Is, c->H, c->Is, 128));
         } else {
-            L.gu_sh = L.gu;
-            L.dn_sh = L.dn;
+            L.sh_gate = L.sh_up = L.gu;
+            L.sh_down = L.dn;
         }
         L.maps = true;
     }
@@ -744,16 +746,6 @@ hf_status hf_topk_scores(const float* scores, int T, int E, const float* bias, i
     if (T > 0 && (!scores || !idx || !weights)) return fail(HF_ERR_ARG, "hf_topk_scores: null pointer");
     return launch_topk(scores, T, E, bias, std::min(k, E), scale, norm, idx, weights, 0, nullptr,
                        as_cuda(stream));
-}
-
-size_t hf_dense_mlp_workspace_size(int T, int H, int I) {
-    (void)T; (void)H; (void)I;
-    return 0;
-}
-
-hf_status hf_dense_mlp_forward(const uint16_t*, const uint16_t*, const uint16_t*, const void*,
-                               hf_dtype, int, int, int, float*, void*, size_t, hf_stream) {
-    return fail(HF_ERR_UNSUPPORTED, "hf_dense_mlp_forward is not available in this build");
 }
 
 hf_status hf_moe_synth_layer(hf_moe_ctx* ctx, int layer, uint64_t seed, uint32_t gen_layer,

@@ -491,6 +491,34 @@ hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cud
     return HF_OK;
 }
 
+// Plan of a dense MLP pass: a single group (the shared-expert slot, G = 1)
+// holding all T tokens in order (perm = identity, slot id = token with k = 0).
+// Block 0 also writes the group's weight pointers and clears the error word.
+__global__ void __launch_bounds__(1024) k_dense_plan(RouteArgs a, GroupW w, GroupW* groups,
+                                                     int32_t* perm) {
+    __shared__ int s_cnt[1], s_off[2];
+    __shared__ int warp_tot[kPlanScratch];
+    if (blockIdx.x == 0) {
+        if (threadIdx.x == 0) {
+            groups[0] = w;
+            s_cnt[0] = a.T;
+            a.plan[a.pl.stats + 3] = 0;
+        }
+        __syncthreads();
+        plan_from_counts(a, s_cnt, s_off, warp_tot);
+    }
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < a.T; p += gridDim.x * blockDim.x)
+        perm[p] = p;
+}
+
+hf_status launch_dense_plan(const RouteArgs& a, const GroupW& w, GroupW* groups, int32_t* perm,
+                            cudaStream_t st) {
+    const int blocks = std::max(1, std::min(64, (a.T + 1023) / 1024));
+    k_dense_plan<<<blocks, 1024, 0, st>>>(a, w, groups, perm);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
 __global__ void __launch_bounds__(256) k_gather_rows(uint4* dst, const uint4* src, int row_vec, int n,
                                                      const int32_t* idx, int div) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;

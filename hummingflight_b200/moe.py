@@ -255,6 +255,35 @@ def top_k_scores(scores, bias, top_k: int, routed_scaling_factor: float, norm_to
     return idx, w
 
 
+def dense_mlp_workspace_size(T: int, H: int, I: int) -> int:
+    return int(_lib.lib().hf_dense_mlp_workspace_size(T, H, I))
+
+
+def dense_mlp_forward(gate, up, down, x, out=None, workspace=None, stream=None):
+    """denseMlp (glm_forward.cpp:411-432) over the rows of x [T x H] (device
+    bf16 or fp32): out = Wd (silu(Wg x) * (Wu x)), fp32 [T x H]. gate/up are
+    BF16 bits [I x H], down [H x I], each its own device tensor."""
+    torch = _torch()
+    T, H = x.shape
+    I = gate.shape[0]
+    if tuple(gate.shape) != (I, H) or tuple(up.shape) != (I, H) or tuple(down.shape) != (H, I):
+        raise ValueError("dense_mlp_forward: gate/up must be [I x H] and down [H x I]")
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float32, device=x.device)
+    need = dense_mlp_workspace_size(T, H, I)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    call("hf_dense_mlp_forward", _ptr(gate), _ptr(up), _ptr(down), _ptr(x), _dtype_code(x), T, H,
+         I, _ptr(out), _ptr(workspace), workspace.numel(), _stream(stream))
+    return out, workspace
+
+
+def dense_mlp_status(workspace, stream=None):
+    """Waits for the stream; raises HfError (HF_ERR_TIMEOUT) if the last dense
+    forward on this workspace hit a bounded-wait timeout."""
+    call("hf_dense_mlp_status", _ptr(workspace), _stream(stream))
+
+
 def synth_bf16_normal(dst, seed: int, layer: int, kind: int, expert: int, sigma: float,
                       stream=None):
     call("hf_synth_bf16_normal", _ptr(dst), dst.numel(), seed, layer, kind, expert, sigma,
@@ -269,5 +298,6 @@ def synth_f32_uniform(dst, seed: int, layer: int, kind: int, expert: int, lo: fl
     return dst
 
 
-__all__ = ["MoELayer", "gemv_bf16_f32", "top_k_scores", "synth_bf16_normal",
+__all__ = ["MoELayer", "gemv_bf16_f32", "top_k_scores", "dense_mlp_forward",
+           "dense_mlp_workspace_size", "dense_mlp_status", "synth_bf16_normal",
            "synth_f32_uniform", "HfError", "HF_BF16", "HF_F32"]

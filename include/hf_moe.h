@@ -239,13 +239,24 @@ HF_API hf_status hf_gemv_bf16_f32(const uint16_t* A, const float* x, float* y, i
 HF_API hf_status hf_topk_scores(const float* scores, int T, int E, const float* bias, int k, float scale,
                          int norm, int32_t* idx, float* weights, hf_stream stream);
 
-/* Dense SwiGLU MLP (GLMForward::denseMlp, glm_forward.cpp:411-432) over T
- * tokens with device weights gate/up [I x H], down [H x I]. workspace: device
- * scratch of at least hf_dense_mlp_workspace_size(T, H, I) bytes. */
+/* Dense SwiGLU MLP (GLMForward::denseMlp, glm_forward.cpp:411-432; the
+ * reference's per-token gemv_bf16_f32 x3 + fp32 SwiGLU) over T tokens.
+ * gate, up: device BF16 [I x H]; down: device BF16 [H x I], three separate
+ * pointers (16-byte aligned); x: device [T x H] bf16 or f32; out: device fp32
+ * [T x H]. H and I multiples of 8 (of 64 for the tensor-core path, taken
+ * from T = 2 tokens). workspace: device scratch, 256-byte aligned, of at least
+ * hf_dense_mlp_workspace_size(T, H, I) bytes; not touched by the host, so one
+ * workspace serves any number of layers called in stream order. Asynchronous
+ * on `stream`; the reference's denseMlp is void, here argument errors return
+ * HF_ERR_ARG before anything is enqueued. */
 HF_API size_t hf_dense_mlp_workspace_size(int T, int H, int I);
 HF_API hf_status hf_dense_mlp_forward(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
                                const void* x, hf_dtype x_dtype, int T, int H, int I, float* out,
                                void* workspace, size_t workspace_bytes, hf_stream stream);
+/* Waits for `stream` and reports whether the last hf_dense_mlp_forward on this
+ * workspace hit a bounded-wait timeout (HF_ERR_TIMEOUT) -- no counterpart in
+ * the reference, whose CPU GEMVs cannot time out. */
+HF_API hf_status hf_dense_mlp_status(const void* workspace, hf_stream stream);
 
 #ifdef __cplusplus
 }

@@ -65,3 +65,32 @@ def test_null_arguments_are_rejected():
     assert L.hf_gemv_bf16_f32(None, None, None, 4, 4, 1.0, 0.0, None) == _lib.HF_ERR_ARG
     assert L.hf_topk_scores(None, 1, 8, None, 9, 1.0, 1, None, None, None) == _lib.HF_ERR_ARG
     assert L.hf_moe_forward(None, 0, None, 0, 1, None, None, None) == _lib.HF_ERR_ARG
+
+
+def test_dense_mlp_arguments_checked_before_any_device_call():
+    """hf_dense_mlp_forward validates shape, pointers, alignment and workspace
+    size on the host; these cases return HF_ERR_ARG without touching CUDA (the
+    pointers below are never dereferenced)."""
+    L = _lib.lib()
+    T, H, I = 4, 256, 384
+    need = L.hf_dense_mlp_workspace_size(T, H, I)
+    assert need > 0 and L.hf_dense_mlp_workspace_size(0, H, I) == 0
+    assert L.hf_dense_mlp_workspace_size(2 * T, H, I) > need
+    p, ws = 0x10000, 0x100000   # fake, aligned
+    ok = [p, p, p, p, _lib.HF_BF16, T, H, I, p, ws, need, None]
+
+    def call(**kw):
+        a = list(ok)
+        for k, v in kw.items():
+            a[["gate", "up", "down", "x", "dt", "T", "H", "I", "out", "ws", "nb", "st"].index(k)] = v
+        return L.hf_dense_mlp_forward(*a)
+
+    assert call(T=-1) == _lib.HF_ERR_ARG
+    assert call(up=None) == _lib.HF_ERR_ARG
+    assert call(dt=7) == _lib.HF_ERR_ARG
+    assert call(H=250) == _lib.HF_ERR_ARG          # not a multiple of 8
+    assert call(x=p + 2) == _lib.HF_ERR_ARG        # not 16-byte aligned
+    assert call(ws=ws + 16) == _lib.HF_ERR_ARG     # workspace not 256-byte aligned
+    assert call(nb=need - 1) == _lib.HF_ERR_ARG    # workspace too small
+    assert call(T=0) == _lib.HF_OK                 # nothing to do
+    assert L.hf_dense_mlp_status(None, None) == _lib.HF_ERR_ARG
