@@ -37,6 +37,7 @@ struct LayerBuf {
     // TMA views of the weights for the tcgen05 GEMM (built with the buffers)
     CUtensorMap gu{}, dn{};      // routed: H-wide / I-wide rows of the [gate|up|down] blocks
     CUtensorMap sh_gate{}, sh_up{}, sh_down{};  // shared expert: one view per matrix
+    CUtensorMap rt{};            // router rows (the router GEMM's weight operand)
     bool maps = false;
 };
 
@@ -94,6 +95,7 @@ struct hf_moe_ctx {
     unsigned long long timeout_ns = 2000ull * 1000 * 1000;
     int stall = 0;               // test hook: GEMM kernels wait on a dead barrier
     int gemm_bn = 0;             // GEMM token tile override (HF_GEMM_BN: 32, 64, 128)
+    int router_mode = 0;         // 0: by batch size, 1: SIMT kernels, 2: tcgen05 (HF_ROUTER)
     int nsm = 148;
     int* err_host = nullptr;     // pinned copy of the device error word
     int grid1_bf16 = 0, grid1_f32 = 0, grid2 = 0;
@@ -159,12 +161,24 @@ struct ExpertWork {
     int T, k;
     float* y;          // [positions x H]
     int bn1, bn2, m2;  // GEMM tiles the plan's tile prefixes were built with
-    bool maybe_gemm;
+    bool maybe_gemm;   // some segment may take the GEMM / the GEMV (else skip the launches)
+    bool maybe_gemv;
 };
 
 // Routing arguments of a forward on the given (source) plan.
 RouteArgs route_args(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T);
-hf_status run_route(hf_moe_ctx* c, const RouteArgs& ra, cudaStream_t st);
+hf_status run_route(hf_moe_ctx* c, LayerBuf& L, const RouteArgs& ra, cudaStream_t st);
+// AUTO GEMV threshold (segments of up to this many tokens) of a pass over `rows` rows.
+int gemv_threshold(const hf_moe_ctx* c, int rows);
+
+// Router logits on the tensor cores: [E x H] router rows against the token
+// rows, split over K into `nsplit` runs of `kbper` 64-wide blocks whose
+// partial planes [T x E] the top-k sums in order.
+struct RouterTiles {
+    int bn, mrows, kbper, nsplit;
+};
+RouterTiles router_tiles(int T, int E, int H, int nsm);
+bool use_tc_router(const hf_moe_ctx* c, const LayerBuf& L, const void* x, hf_dtype xd, int T);
 hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st);
 hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, float* slot_out,
                       cudaStream_t st);

@@ -208,7 +208,7 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     // 1. route the local tokens over all experts; gather their rows in slot order
     const RouteArgs ra = route_args(c, L, x, xd, T);
     if (T > 0) {
-        HF_TRY(run_route(c, ra, st));
+        HF_TRY(run_route(c, L, ra, st));
         PhaseTimer p1(c, st, 1);
         HF_TRY(launch_gather_rows(e.xsend, x, rowb, T * k, c->perm_src, k, st));
         p1.done(1);
@@ -266,6 +266,7 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     rl.pl = c->pl;
     rl.T = R + T;
     set_gemm_tiles(c->gemm_bn, R + T, rl);
+    rl.gemv_max = gemv_threshold(c, R + T);
     HF_TRY(launch_plan_from_counts(rl, e.loc_counts, st));
     ExpertWork w{};
     w.plan = c->plan;
@@ -279,7 +280,9 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     w.bn1 = rl.gemm_bn1;
     w.bn2 = rl.gemm_bn2;
     w.m2 = rl.gemm_m2;
-    w.maybe_gemm = rl.gemm_ok && (c->cfg.path == HF_PATH_GEMM || maxseg > c->cfg.gemv_max_tokens);
+    w.maybe_gemm = rl.gemm_ok && (c->cfg.path == HF_PATH_GEMM || maxseg > rl.gemv_max);
+    w.maybe_gemv = !rl.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
+                   (c->cfg.path == HF_PATH_AUTO && rl.gemv_max > 0);
     if (npos > 0) HF_TRY(run_experts(c, L, w, st));
 
     // 5. outputs back to their sources, at canonical slot positions

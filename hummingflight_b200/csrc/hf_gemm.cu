@@ -56,8 +56,10 @@ struct GemmCfg {
 };
 
 struct TileInfo {
-    int seg, n0, n, m0, mvalid, kblocks;
+    int seg, n0, n, m0, mvalid;
+    int kb0, kb1;      // K blocks [kb0, kb1) of this tile (split-K runs)
     int rowA0, rowA1;
+    long long yoff;    // split-K partial plane of the output
     bool shared;
 };
 
@@ -71,6 +73,11 @@ struct PlanView {
 
 __device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p, int u,
                                             TileInfo& t) {
+    int ks = 0;
+    if (a.nsplit > 1) {  // K-split runs of one output tile are adjacent tile ids
+        ks = u % a.nsplit;
+        u /= a.nsplit;
+    }
     const int G = a.pl.G;
     const int g = find_group(p.pref, G, u);
     const int c = p.cnt[g];
@@ -90,12 +97,19 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p
         t.rowA0 = t.shared ? t.m0 : base + t.m0;
         t.rowA1 = t.shared ? t.m0 : base + Ig + t.m0;
         t.mvalid = Ig - t.m0;
-        t.kblocks = (a.H + 63) / 64;
+        t.kb1 = (a.H + 63) / 64;
     } else {  // down rows; a second accumulator takes the next 128 rows
         t.rowA0 = t.shared ? t.m0 : g * 3 * a.H + 2 * a.H + t.m0;
         t.rowA1 = t.rowA0 + 128;
         t.mvalid = a.H - t.m0;
-        t.kblocks = (Ig + 63) / 64;
+        t.kb1 = (Ig + 63) / 64;
+    }
+    t.kb0 = 0;
+    t.yoff = 0;
+    if (a.nsplit > 1) {  // the launcher sizes nsplit so that no run is empty
+        t.kb0 = ks * a.kbper;
+        t.kb1 = min(t.kb1, t.kb0 + a.kbper);
+        t.yoff = ks * a.split_stride;
     }
 }
 
@@ -130,18 +144,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint64_t deadline = globaltimer() + a.timeout_ns;
     const int G = a.pl.G;
-    const int32_t* pref_g = a.plan + (a.which == 1 ? a.pl.g1 : a.pl.g2);
-    const int total = pref_g[G];
-    PlanView pv{pref_g, a.plan + a.pl.counts, a.plan + a.pl.offsets};
-    if (a.plan_smem) {
+    int total;
+    PlanView pv;
+    if (!a.plan) {  // one group of dense_T rows: tile prefix, count and offset in shared memory
         int32_t* sp = reinterpret_cast<int32_t*>(smem + C::kBarOff + 256);
-        for (int i = threadIdx.x; i <= G; i += blockDim.x) sp[i] = pref_g[i];
-        for (int i = threadIdx.x; i < G; i += blockDim.x) {
-            sp[G + 1 + i] = a.plan[a.pl.counts + i];
-            sp[2 * G + 1 + i] = a.plan[a.pl.offsets + i];
+        const int rows_out = a.which == 1 ? a.Is : a.H;
+        total = ((a.dense_T + a.bn - 1) / a.bn) * ((rows_out + a.mrows - 1) / a.mrows);
+        if (threadIdx.x == 0) {
+            sp[0] = 0;
+            sp[1] = total;
+            sp[2] = a.dense_T;
+            sp[3] = 0;
         }
-        pv = PlanView{sp, sp + G + 1, sp + 2 * G + 1};
+        pv = PlanView{sp, sp + 2, sp + 3};
+    } else {
+        const int32_t* pref_g = a.plan + (a.which == 1 ? a.pl.g1 : a.pl.g2);
+        total = pref_g[G];
+        pv = PlanView{pref_g, a.plan + a.pl.counts, a.plan + a.pl.offsets};
+        if (a.plan_smem) {
+            int32_t* sp = reinterpret_cast<int32_t*>(smem + C::kBarOff + 256);
+            for (int i = threadIdx.x; i <= G; i += blockDim.x) sp[i] = pref_g[i];
+            for (int i = threadIdx.x; i < G; i += blockDim.x) {
+                sp[G + 1 + i] = a.plan[a.pl.counts + i];
+                sp[2 * G + 1 + i] = a.plan[a.pl.offsets + i];
+            }
+            pv = PlanView{sp, sp + G + 1, sp + 2 * G + 1};
+        }
     }
+    if (a.nsplit > 1) total *= a.nsplit;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -181,7 +211,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const CUtensorMap* mA1 = (t.shared && a.which == 1) ? &tmA_sh2 : mA;
             const CUtensorMap* mB0 = (a.which == 2 && t.shared) ? &tmB0_sh : &tmB0;
             const CUtensorMap* mB1 = (a.which == 2 && t.shared) ? &tmB1_sh : &tmB1;
-            for (int kb = 0; kb < t.kblocks; ++kb, ++it) {
+            for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
                 const uint32_t s = it % S, ph = (it / S) & 1;
                 if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, deadline)) {
                     ok = false;
@@ -222,7 +252,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t nmma = uint32_t((t.n + 15) & ~15);
             const uint32_t idesc = idesc_bf16_m128(nmma);
             const uint32_t d0 = tmem_base + acc * C::kAccCols;
-            for (int kb = 0; kb < t.kblocks; ++kb, ++it) {
+            for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
                 const uint32_t s = it % S, ph = (it / S) & 1;
                 if (!mbar_wait(&full[s], ph, abort_flag, deadline)) {
                     ok = false;
@@ -239,7 +269,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         for (int bi = 0; bi < NUM_B; ++bi) {
                             const uint64_t bd =
                                 desc_k_sw128(st + NUM_A * kTileABytes + bi * BN * 128) + 2 * kk;
-                            mma_bf16(d0 + ai * BN, ad, bd, idesc, (kb | kk | bi) != 0);
+                            mma_bf16(d0 + ai * BN, ad, bd, idesc, (kb != t.kb0 || kk || bi));
                         }
                     }
                 }
@@ -264,15 +294,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t ta = tmem_base + (uint32_t(q * 32) << 16) + acc * C::kAccCols;
             const bool rv = r < t.mvalid;
             const bool rv1 = r + 128 < t.mvalid;  // second down row block
-            for (int c0 = 0; c0 < t.n; c0 += 32) {
-                uint32_t v0[32], v1[32];
-                tmem_ld32(ta + c0, v0);
-                if constexpr (NUM_A == 2) tmem_ld32(ta + BN + c0, v1);
+            // columns per TMEM load: 32, or 16 for 16-token tiles (an x32 load
+            // would reach past the allocated columns)
+            constexpr int CW = BN < 32 ? BN : 32;
+            for (int c0 = 0; c0 < t.n; c0 += CW) {
+                uint32_t v0[CW], v1[CW];
+                if constexpr (CW == 16) {
+                    tmem_ld16(ta + c0, v0);
+                    if constexpr (NUM_A == 2) tmem_ld16(ta + BN + c0, v1);
+                } else {
+                    tmem_ld32(ta + c0, v0);
+                    if constexpr (NUM_A == 2) tmem_ld32(ta + BN + c0, v1);
+                }
                 tmem_ld_wait();
                 if (NUM_A == 2 && a.which == 1) {  // gate/up pair -> SwiGLU -> hi/lo planes
                     if (rv) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
+                        for (int j = 0; j < CW; ++j) {
                             const int col = c0 + j;
                             if (col < t.n) {
                                 const size_t pos = size_t(t.seg + t.n0 + col);
@@ -286,12 +324,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                 } else {  // down rows m0 + r (and m0 + 128 + r) -> fp32 outputs
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < CW; ++j) {
                         const int col = c0 + j;
                         if (col < t.n) {
                             const size_t pos = size_t(t.seg + t.n0 + col);
-                            if (rv) a.y[pos * a.H + t.m0 + r] = __uint_as_float(v0[j]);
-                            if (NUM_A == 2 && rv1) a.y[pos * a.H + t.m0 + 128 + r] = __uint_as_float(v1[j]);
+                            float* yr = a.y + t.yoff + pos * a.H + t.m0 + r;
+                            if (rv) yr[0] = __uint_as_float(v0[j]);
+                            if (NUM_A == 2 && rv1) yr[128] = __uint_as_float(v1[j]);
                         }
                     }
                 }
@@ -363,6 +402,7 @@ static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cuda
     int smem = C::kSmem;
     args.plan_smem = (C::kSmem + plan_bytes) <= 227 * 1024;
     if (args.plan_smem) smem += plan_bytes;
+    else if (!a.plan) return fail(HF_ERR_ARG, "plan-free GEMM needs its shared-memory plan slot");
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(kern), smem));
     kern<<<grid, kGemmThreads, smem, st>>>(m.A, m.A_sh, m.A_sh2, m.B0, m.B1, m.B0_sh, m.B1_sh, args);
     HF_CUDA(cudaGetLastError());
@@ -377,7 +417,18 @@ hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid,
                                           : launch_one<2, 2, 64>(m, a, grid, st);
         if (a.bn == 128) return num_b == 1 ? launch_one<2, 1, 128>(m, a, grid, st)
                                            : launch_one<2, 2, 128>(m, a, grid, st);
+    } else if (num_b == 1) {  // single-plane B (router logits): bf16 activations
+        if (a.mrows == 256) {
+            if (a.bn == 32) return launch_one<2, 1, 32>(m, a, grid, st);
+            if (a.bn == 64) return launch_one<2, 1, 64>(m, a, grid, st);
+            if (a.bn == 128) return launch_one<2, 1, 128>(m, a, grid, st);
+        } else if (a.mrows == 128) {
+            if (a.bn == 32) return launch_one<1, 1, 32>(m, a, grid, st);
+            if (a.bn == 64) return launch_one<1, 1, 64>(m, a, grid, st);
+            if (a.bn == 128) return launch_one<1, 1, 128>(m, a, grid, st);
+        }
     } else if (a.mrows == 256) {
+        if (a.bn == 16) return launch_one<2, 2, 16>(m, a, grid, st);
         if (a.bn == 128) return launch_one<2, 2, 128>(m, a, grid, st);
     } else if (a.mrows == 128) {
         if (a.bn == 32) return launch_one<1, 2, 32>(m, a, grid, st);

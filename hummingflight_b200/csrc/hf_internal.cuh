@@ -37,7 +37,12 @@ constexpr int kSmallRouteT = 128;  // single-CTA routing up to this many tokens
 constexpr int kGemvTE = 4;         // tokens per grouped-GEMV chunk
 constexpr int kGemv1Rows = 16;     // gate/up rows per GEMV1 unit (8 warps x 2)
 constexpr int kGemv2Rows = 32;     // down rows per GEMV2 unit (8 warps x 4)
-constexpr int kGemvDefaultMax = 1; // AUTO: segments <= this many tokens use the GEMV
+// AUTO with gemv_max_tokens = 0: in passes of up to kGemvAutoBatch rows,
+// single-token segments take the GEMV; larger passes run every segment on the
+// tcgen05 GEMM (measured faster from 64 rows: its weight stream runs at the
+// copy rate, the GEMV pair at 75-88% of it).
+constexpr int kGemvAutoBatch = 16;
+constexpr int kGemvAutoMax = 1;
 
 // Weights of one expert group (routed expert or the shared expert).
 struct GroupW {
@@ -101,6 +106,7 @@ struct RouteArgs {
     int gemm_ok;              // shapes allow the tcgen05 GEMM (64-aligned)
     int gemm_bn1, gemm_bn2;   // token tile (columns per tile) of GEMM1 / GEMM2
     int gemm_m2;              // weight rows per GEMM2 tile (128 or 256)
+    int lsplit;               // logits are the sum of lsplit planes of [T x E] (split-K router)
 };
 
 // ------------------------------------------------------------------ device helpers
@@ -243,6 +249,12 @@ struct GemmArgs {
     unsigned long long timeout_ns;
     int test_stall;         // wait on a barrier nothing signals (test hook)
     int plan_smem;          // set by the launcher: plan arrays staged in shared memory
+    // plan == nullptr: one group of dense_T rows in order (no device plan)
+    int dense_T;
+    // GEMM2 split-K: nsplit > 1 cuts the K blocks into runs of kbper; run s
+    // writes its partial sums to y + s * split_stride (summed by the reader)
+    int nsplit, kbper;
+    long long split_stride;
 };
 struct GemmMaps {
     CUtensorMap A, A_sh;       // weights: routed view; shared expert gate (GEMM1) or down rows

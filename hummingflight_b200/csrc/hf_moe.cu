@@ -84,15 +84,80 @@ RouteArgs route_args(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     ra.masks = c->masks;
     ra.blk_counts = c->blk_counts;
     ra.path = c->cfg.path;
-    ra.gemv_max = c->cfg.gemv_max_tokens;
+    ra.gemv_max = gemv_threshold(c, T);
     ra.gemm_ok = c->gemm_ok && L.maps;
     set_gemm_tiles(c->gemm_bn, T, ra);
+    ra.lsplit = use_tc_router(c, L, x, xd, T) ? router_tiles(T, c->E, c->H, c->nsm).nsplit : 1;
     return ra;
 }
 
+// Token tile 32/64/128 by batch; 128 router rows a tile for small batches
+// (more CTAs), 256 (two accumulators) from 512 tokens when E > 128. K is
+// split into at most kMaxRouterSplit runs so the grid covers more SMs while
+// the top-k's in-order sum of the partial planes stays short (T = 64,
+// E = 256, H = 6144: 2 x 12 CTAs of 8 K blocks).
+constexpr int kMaxRouterSplit = 12;
+
+RouterTiles router_tiles(int T, int E, int H, int nsm) {
+    RouterTiles r{};
+    r.bn = T <= 32 ? 32 : T <= 64 ? 64 : 128;
+    r.mrows = (E > 128 && T >= 512) ? 256 : 128;
+    const int kb = (H + 63) / 64;
+    const int tiles = ((T + r.bn - 1) / r.bn) * ((E + r.mrows - 1) / r.mrows);
+    const int ns = std::max(1, std::min(kMaxRouterSplit, (nsm + tiles - 1) / tiles));
+    r.kbper = (kb + ns - 1) / ns;
+    r.nsplit = (kb + r.kbper - 1) / r.kbper;  // no empty run
+    return r;
+}
+
+// The SIMT kernels read fp32 activations exactly and serve single tokens;
+// bf16 batches from kTcRouterMinT tokens take the tensor cores.
+constexpr int kTcRouterMinT = 16;
+
+bool use_tc_router(const hf_moe_ctx* c, const LayerBuf& L, const void* x, hf_dtype xd, int T) {
+    if (!L.maps || xd != HF_BF16 || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
+    if (c->router_mode == 1) return false;
+    if (c->router_mode == 2) return T > 0;
+    return T >= kTcRouterMinT;
+}
+
+static hf_status launch_tc_router(hf_moe_ctx* c, LayerBuf& L, const RouteArgs& ra,
+                                  cudaStream_t st) {
+    const RouterTiles rt = router_tiles(ra.T, c->E, c->H, c->nsm);
+    GemmMaps m{};
+    m.A = m.A_sh = m.A_sh2 = L.rt;
+    HF_TRY(make_map_bf16(&m.B0, ra.x, c->H, ra.T, c->H, 16));
+    m.B1 = m.B0_sh = m.B1_sh = m.B0;
+    GemmArgs g{};
+    g.plan = nullptr;  // one group of T rows
+    g.pl = PlanLayout::make(1);
+    g.dense_T = ra.T;
+    g.which = 2;       // y[t][e] = sum_k router[e][k] x[t][k]
+    g.H = c->E;        // output rows
+    g.I = g.Is = c->H; // K
+    g.Imax = c->H;
+    g.bn = rt.bn;
+    g.mrows = rt.mrows;
+    g.y = ra.logits;
+    g.err = c->plan + c->pl.stats + 3;
+    g.timeout_ns = c->timeout_ns;
+    g.nsplit = rt.nsplit;
+    g.kbper = rt.kbper;
+    g.split_stride = (long long)ra.T * c->E;
+    return launch_gemm(m, g, 1, c->nsm, st);
+}
+
+int gemv_threshold(const hf_moe_ctx* c, int rows) {
+    if (c->cfg.gemv_max_tokens > 0) return c->cfg.gemv_max_tokens;
+    return rows <= kGemvAutoBatch ? kGemvAutoMax : 0;
+}
+
 // Tiles of the two grouped GEMMs for a pass over `rows` activation rows.
-// Decode (<= 64 rows): narrow 32-token tiles leave room for a deeper weight
-// ring. Prefill (>= 1024 rows): down tiles of 256 weight rows x 128 tokens
+// Decode (<= 64 rows, a few tokens per expert): narrow token tiles leave the
+// shared memory to the weight ring -- gate/up 32-token tiles (two 16 KB
+// weight boxes + 4 KB of tokens a stage, 6 stages), down 256 weight rows x
+// 16 tokens (32 KB + 4 KB, 6 stages: as many weight bytes in flight as
+// gate/up, against 9 x 16 KB for 128 x 32 tiles). Prefill (>= 1024 rows): down tiles of 256 weight rows x 128 tokens
 // load each activation tile once per 256 output rows (a third fewer operand
 // bytes per MMA flop than 128 x 128). Gate/up keeps 128 x 128 tiles with two
 // accumulators: at 256 tokens the single TMEM buffer it would need measured
@@ -102,18 +167,22 @@ void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
         ra.gemm_bn1 = ra.gemm_bn2 = bn_override;
         ra.gemm_m2 = 128;
     } else if (rows <= 64) {
-        ra.gemm_bn1 = ra.gemm_bn2 = 32;
-        ra.gemm_m2 = 128;
+        ra.gemm_bn1 = 32;
+        ra.gemm_bn2 = 16;
+        ra.gemm_m2 = 256;
     } else {
         ra.gemm_bn1 = ra.gemm_bn2 = 128;
         ra.gemm_m2 = rows < 1024 ? 128 : 256;
     }
 }
 
-hf_status run_route(hf_moe_ctx* c, const RouteArgs& ra, cudaStream_t st) {
+hf_status run_route(hf_moe_ctx* c, LayerBuf& L, const RouteArgs& ra, cudaStream_t st) {
     {
         PhaseTimer p0(c, st, 0);
-        HF_TRY(launch_router_logits(ra, st));
+        if (ra.lsplit > 1 || use_tc_router(c, L, ra.x, ra.x_f32 ? HF_F32 : HF_BF16, ra.T))
+            HF_TRY(launch_tc_router(c, L, ra, st));
+        else
+            HF_TRY(launch_router_logits(ra, st));
         p0.done(1);
     }
     PhaseTimer p1(c, st, 1);
@@ -155,7 +224,7 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
     ga.y = w.y;
     ga.grid1 = w.x_f32 ? c->grid1_f32 : c->grid1_bf16;
     ga.grid2 = c->grid2;
-    const bool gemv_possible = !(w.maybe_gemm && c->cfg.path == HF_PATH_GEMM);
+    const bool gemv_possible = w.maybe_gemv;
     if (gemv_possible) {
         PhaseTimer p2(c, st, 2);
         HF_TRY(launch_gemv1(ga, st));
@@ -337,11 +406,14 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     x->pl = PlanLayout::make(x->G);
     x->pl_src = PlanLayout::make(x->G_src);
     x->T_max = c.max_tokens;
-    if (x->cfg.gemv_max_tokens <= 0) x->cfg.gemv_max_tokens = kGemvDefaultMax;
+    if (x->cfg.gemv_max_tokens < 0) x->cfg.gemv_max_tokens = 0;
     if (const char* bn = std::getenv("HF_GEMM_BN")) {  // tuning knob
         const int v = std::atoi(bn);
         x->gemm_bn = (v == 32 || v == 64 || v == 128) ? v : 0;
     }
+    if (const char* rm = std::getenv("HF_ROUTER"))  // "simt" / "tc": force one router kernel
+        x->router_mode = std::string(rm) == "simt" ? 1 : std::string(rm) == "tc" ? 2 : 0;
+    x->nsm = num_sms(c.device);
     if (gemv1_smem(x->H, true, x->G) > 227 * 1024 || gemv2_smem(x->inter_max, x->G) > 227 * 1024) {
         free_ctx(x);
         return fail(HF_ERR_ARG, "hidden/intermediate size too large for the GEMV staging");
@@ -354,7 +426,10 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
     const size_t nb = (T + kSmallRouteT - 1) / kSmallRouteT;
     hf_status s = HF_OK;
     auto A = [&](hf_status r) { if (s == HF_OK) s = r; };
-    A(dalloc(&x->logits, T * x->E));
+    size_t lrows = T;  // logits: nsplit partial planes when the router GEMM splits K
+    for (size_t t = 1; t <= T; ++t)
+        lrows = std::max(lrows, t * size_t(router_tiles(int(t), x->E, x->H, x->nsm).nsplit));
+    A(dalloc(&x->logits, lrows * x->E));
     A(dalloc(&x->ids, T * x->k));
     A(dalloc(&x->w, T * x->k));
     A(dalloc(&x->margins, T));
@@ -406,7 +481,6 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
             return fail(s, "hf_moe_create tensor maps: " + m);
         }
     }
-    x->nsm = num_sms(c.device);
     if (cudaMemset(x->plan, 0, sizeof(int32_t) * x->pl.words) != cudaSuccess ||
         cudaMallocHost(reinterpret_cast<void**>(&x->err_host), 64) != cudaSuccess) {
         free_ctx(x);
@@ -480,6 +554,7 @@ static hf_status layer_alloc(hf_moe_ctx* c, int layer) {
             L.sh_gate = L.sh_up = L.gu;
             L.sh_down = L.dn;
         }
+        HF_TRY(make_map_bf16(&L.rt, L.router, c->H, c->E, c->H, 128));
         L.maps = true;
     }
     return HF_OK;
@@ -611,7 +686,7 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
     }
     if (T == 0) return HF_OK;
     const RouteArgs ra = route_args(c, L, x, xd, T);
-    HF_TRY(run_route(c, ra, st));
+    HF_TRY(run_route(c, L, ra, st));
     if (!route_only) {
         ExpertWork w{};
         w.plan = c->plan;
@@ -626,7 +701,9 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
         w.bn2 = ra.gemm_bn2;
         w.m2 = ra.gemm_m2;
         // segments can only exceed the GEMV threshold when T does
-        w.maybe_gemm = ra.gemm_ok && (c->cfg.path == HF_PATH_GEMM || T > c->cfg.gemv_max_tokens);
+        w.maybe_gemm = ra.gemm_ok && (c->cfg.path == HF_PATH_GEMM || T > ra.gemv_max);
+        w.maybe_gemv = !ra.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
+                       (c->cfg.path == HF_PATH_AUTO && ra.gemv_max > 0);
         HF_TRY(run_experts(c, L, w, st));
         HF_TRY(run_combine(c, c->y, T, out, r ? r->slot_out : nullptr, st));
     }

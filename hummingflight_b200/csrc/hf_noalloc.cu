@@ -116,6 +116,7 @@ extern "C" hf_status hf_moe_route_noalloc(const uint16_t* router_bf16, const flo
     a.gemv_max = 1 << 30;
     a.gemm_ok = 0;
     a.gemm_bn1 = a.gemm_bn2 = 64;
+    a.lsplit = 1;
     a.gemm_m2 = 128;
     HF_TRY(launch_router_logits(a, st));
     int n = 0;

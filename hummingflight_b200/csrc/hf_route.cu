@@ -171,16 +171,35 @@ __global__ void __launch_bounds__(256) k_router_tile(RouteArgs a) {
 // and that sum > 0, then multiplied by routedScalingFactor. Sigmoid as
 // glm_forward.cpp:522-524. Ties go to the lower expert id.
 template <int NPL>
-__device__ __forceinline__ void topk_warp(const float* row, int apply_sigmoid, const float* bias,
+__device__ __forceinline__ void topk_warp(const float* row, int planes, size_t pstride,
+                                          int apply_sigmoid, const float* bias,
                                           int E, int k, float scale, int norm, int lane,
                                           int32_t* ids_out, float* w_out, float* margin_out,
                                           int32_t* ids_smem) {
-    float v[NPL], s[NPL];
+    float v[NPL], s[NPL], lg[NPL];
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) lg[j] = (j * 32 + lane < E) ? row[j * 32 + lane] : 0.0f;
+    // split-K partial planes, summed in plane order (deterministic); four
+    // planes x NPL experts of loads are issued before each group of adds
+    for (int p = 1; p < planes; p += 4) {
+        float b[4][NPL];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < NPL; ++j)
+                b[i][j] = (p + i < planes && j * 32 + lane < E)
+                              ? row[size_t(p + i) * pstride + j * 32 + lane] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (p + i < planes)
+#pragma unroll
+                for (int j = 0; j < NPL; ++j) lg[j] = __fadd_rn(lg[j], b[i][j]);
+    }
 #pragma unroll
     for (int j = 0; j < NPL; ++j) {
         const int e = j * 32 + lane;
         if (e < E) {
-            const float l = row[e];
+            const float l = lg[j];
             const float sc = apply_sigmoid ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-l))) : l;
             s[j] = sc;
             v[j] = __fadd_rn(sc, bias ? bias[e] : 0.0f);
@@ -247,13 +266,15 @@ __device__ __forceinline__ void topk_warp(const float* row, int apply_sigmoid, c
 }
 
 template <int NPL>
-__global__ void __launch_bounds__(256) k_topk(const float* scores, int T, int E, const float* bias,
-                                              int k, float scale, int norm, int apply_sigmoid,
-                                              int32_t* ids, float* w, float* margins) {
+__global__ void __launch_bounds__(256) k_topk(const float* scores, int planes, int T, int E,
+                                              const float* bias, int k, float scale, int norm,
+                                              int apply_sigmoid, int32_t* ids, float* w,
+                                              float* margins) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + warp;
     if (t >= T) return;
-    topk_warp<NPL>(scores + size_t(t) * E, apply_sigmoid, bias, E, k, scale, norm, lane,
+    topk_warp<NPL>(scores + size_t(t) * E, planes, size_t(T) * E, apply_sigmoid, bias, E, k,
+                   scale, norm, lane,
                    ids + size_t(t) * k, w + size_t(t) * k, margins ? margins + t : nullptr,
                    nullptr);
 }
@@ -389,7 +410,8 @@ __global__ void __launch_bounds__(1024) k_route_block(RouteArgs a) {
     if constexpr (TOPK) {
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         for (int t = warp; t < T; t += 32)
-            topk_warp<NPL>(a.logits + size_t(t) * E, 1, a.bias, E, k, a.scale, a.norm, lane,
+            topk_warp<NPL>(a.logits + size_t(t) * E, a.lsplit, size_t(T) * E, 1, a.bias, E, k,
+                           a.scale, a.norm, lane,
                            a.ids + size_t(t) * k, a.w + size_t(t) * k,
                            a.margins ? a.margins + t : nullptr, s_ids + t * kMaxTopK);
     } else {
@@ -607,9 +629,9 @@ hf_status launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
         } else {
             *launches = 2;
             HF_NPL_SWITCH(a.E, {
-                k_topk<NPL><<<(a.T + 7) / 8, 256, 0, st>>>(a.logits, a.T, a.E, a.bias, a.k,
-                                                           a.scale, a.norm, 1, a.ids, a.w,
-                                                           a.margins);
+                k_topk<NPL><<<(a.T + 7) / 8, 256, 0, st>>>(a.logits, a.lsplit, a.T, a.E,
+                                                           a.bias, a.k, a.scale, a.norm, 1,
+                                                           a.ids, a.w, a.margins);
             });
             HF_CUDA(cudaGetLastError());
             k_route_block<1, false><<<1, 1024, smem, st>>>(a);
@@ -620,8 +642,8 @@ hf_status launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
     *launches = 4;
     const int nb = (a.T + kSmallRouteT - 1) / kSmallRouteT;
     HF_NPL_SWITCH(a.E, {
-        k_topk<NPL><<<(a.T + 7) / 8, 256, 0, st>>>(a.logits, a.T, a.E, a.bias, a.k, a.scale,
-                                                   a.norm, 1, a.ids, a.w, a.margins);
+        k_topk<NPL><<<(a.T + 7) / 8, 256, 0, st>>>(a.logits, a.lsplit, a.T, a.E, a.bias, a.k,
+                                                   a.scale, a.norm, 1, a.ids, a.w, a.margins);
     });
     HF_CUDA(cudaGetLastError());
     k_perm_masks<<<nb, 256, 0, st>>>(a);
@@ -639,7 +661,7 @@ hf_status launch_topk(const float* scores, int T, int E, const float* bias, int 
                       cudaStream_t st) {
     if (T == 0) return HF_OK;
     HF_NPL_SWITCH(E, {
-        k_topk<NPL><<<(T + 7) / 8, 256, 0, st>>>(scores, T, E, bias, k, scale, norm,
+        k_topk<NPL><<<(T + 7) / 8, 256, 0, st>>>(scores, 1, T, E, bias, k, scale, norm,
                                                  apply_sigmoid, idx, w, margins);
     });
     HF_CUDA(cudaGetLastError());
