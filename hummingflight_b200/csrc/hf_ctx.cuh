@@ -98,6 +98,7 @@ struct hf_moe_ctx {
     int router_mode = 0;         // 0: by batch size, 1: SIMT kernels, 2: tcgen05 (HF_ROUTER)
     int nsm = 148;
     int* err_host = nullptr;     // pinned copy of the device error word
+    int* sched = nullptr;        // GEMM tile-scheduler counters (zero between launches)
     int grid1_bf16 = 0, grid1_f32 = 0, grid2 = 0;
     cudaStream_t last_stream = nullptr;
     hf::EpState* ep = nullptr;

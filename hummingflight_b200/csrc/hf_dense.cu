@@ -27,7 +27,7 @@ constexpr int kDenseGemvMax = 1;  // tokens up to which the GEMV pair runs
 size_t up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct DenseWs {
-    size_t plan, groups, perm, scratch, total;
+    size_t plan, groups, sched, perm, scratch, total;
     // scratch: GEMV path mid fp32 [T x I]; GEMM path xp_hi, xp_lo [T x H] and
     // mid_hi, mid_lo [T x I] (bf16)
     size_t xp_lo, mid_hi, mid_lo;
@@ -41,6 +41,8 @@ DenseWs layout(int T, int H, int I) {
     o += up(sizeof(int32_t) * pl.words);
     w.groups = o;
     o += up(sizeof(GroupW));
+    w.sched = o;
+    o += up(sizeof(int) * 2);
     w.perm = o;
     o += up(sizeof(int32_t) * size_t(T));
     w.scratch = o;
@@ -99,6 +101,7 @@ hf_status hf_dense_mlp_forward(const uint16_t* gate, const uint16_t* upw, const 
     int32_t* plan = reinterpret_cast<int32_t*>(ws + L.plan);
     GroupW* groups = reinterpret_cast<GroupW*>(ws + L.groups);
     int32_t* perm = reinterpret_cast<int32_t*>(ws + L.perm);
+    int* sched = reinterpret_cast<int*>(ws + L.sched);
     const PlanLayout pl = PlanLayout::make(1);
 
     RouteArgs ra{};
@@ -116,7 +119,7 @@ hf_status hf_dense_mlp_forward(const uint16_t* gate, const uint16_t* upw, const 
     ra.gemm_ok = gemm;
     set_gemm_tiles(0, T, ra);
     GroupW w{gate, upw, down, I, 0};
-    HF_TRY(launch_dense_plan(ra, w, groups, perm, st));
+    HF_TRY(launch_dense_plan(ra, w, groups, perm, sched, st));
 
     if (!gemm) {
         GemvArgs ga{};
@@ -190,6 +193,7 @@ hf_status hf_dense_mlp_forward(const uint16_t* gate, const uint16_t* upw, const 
     gm.err = plan + pl.stats + 3;
     gm.timeout_ns = 2000ull * 1000 * 1000;
     gm.test_stall = 0;
+    gm.sched = sched;
     const int nsm = num_sms(dev);
     HF_TRY(launch_gemm(m1, gm, xf32 ? 2 : 1, nsm, st));
     gm.which = 2;

@@ -35,6 +35,8 @@ constexpr int kGemmThreads = 192;
 constexpr int kBoxRowsB = 16;
 constexpr uint32_t kTileABytes = 128 * 64 * 2;  // 128 rows x 64 bf16
 constexpr uint64_t kDrainNs = 500ull * 1000 * 1000;
+constexpr int kTileQ = 8;        // tile ids in flight from the producer to the MMA / epilogue
+constexpr int kBarBytes = 512;   // barriers, tile queue, TMEM slot, abort flag
 
 template <int NUM_A, int NUM_B, int BN>
 struct GemmCfg {
@@ -49,9 +51,11 @@ struct GemmCfg {
     static constexpr uint32_t kTmemCols = kCols0 <= 32 ? 32 : kCols0 <= 64 ? 64 : kCols0 <= 128 ? 128
                                           : kCols0 <= 256 ? 256 : 512;
     static constexpr int kBarOff = kStages * kStageBytes;
-    static constexpr int kSmem = 1024 + kBarOff + 256;
+    static constexpr int kSmem = 1024 + kBarOff + kBarBytes;
     static_assert(kCols0 <= 512, "TMEM holds 512 columns");
     static_assert(kStages >= 3, "pipeline needs at least 3 stages");
+    static_assert((2 * kStages + 6 + 2 * kTileQ) * 8 + kTileQ * 4 + 8 <= kBarBytes,
+                  "barrier area overflow");
     static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
 };
 
@@ -87,8 +91,12 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p
     t.shared = (g == G - 1);
     const int Ig = t.shared ? a.Is : a.I;
     t.seg = p.off[g];
-    t.n0 = ni * a.bn;
-    t.n = min(a.bn, c - t.n0);
+    // the segment's nt token tiles get equal widths (ceil(c / nt) <= bn), so
+    // the CTAs that stream the same weight rows for them progress at the same
+    // rate and the later reads of those rows hit L2
+    const int nw = (c + nt - 1) / nt;
+    t.n0 = ni * nw;
+    t.n = min(nw, c - t.n0);
     t.m0 = mi * a.mrows;
     // routed experts: one [gate|up|down] block per expert in one view; the
     // shared expert: separate gate, up and down views
@@ -138,7 +146,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* tempty = tfull + 2;
     uint64_t* final_bar = tempty + 2;
     uint64_t* stall_bar = final_bar + 1;  // never signalled (test hook)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stall_bar + 1);
+    uint64_t* tq_full = stall_bar + 1;    // tile queue: producer -> MMA + epilogue
+    uint64_t* tq_empty = tq_full + kTileQ;
+    int* tile_q = reinterpret_cast<int*>(tq_empty + kTileQ);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_q + kTileQ);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -147,7 +158,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int total;
     PlanView pv;
     if (!a.plan) {  // one group of dense_T rows: tile prefix, count and offset in shared memory
-        int32_t* sp = reinterpret_cast<int32_t*>(smem + C::kBarOff + 256);
+        int32_t* sp = reinterpret_cast<int32_t*>(smem + C::kBarOff + kBarBytes);
         const int rows_out = a.which == 1 ? a.Is : a.H;
         total = ((a.dense_T + a.bn - 1) / a.bn) * ((rows_out + a.mrows - 1) / a.mrows);
         if (threadIdx.x == 0) {
@@ -162,7 +173,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         total = pref_g[G];
         pv = PlanView{pref_g, a.plan + a.pl.counts, a.plan + a.pl.offsets};
         if (a.plan_smem) {
-            int32_t* sp = reinterpret_cast<int32_t*>(smem + C::kBarOff + 256);
+            int32_t* sp = reinterpret_cast<int32_t*>(smem + C::kBarOff + kBarBytes);
             for (int i = threadIdx.x; i <= G; i += blockDim.x) sp[i] = pref_g[i];
             for (int i = threadIdx.x; i < G; i += blockDim.x) {
                 sp[G + 1 + i] = a.plan[a.pl.counts + i];
@@ -184,6 +195,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         mbar_init(final_bar, 1);
         mbar_init(stall_bar, 1);
+        for (int q = 0; q < kTileQ; ++q) {
+            mbar_init(&tq_full[q], 1);
+            mbar_init(&tq_empty[q], 5);  // the MMA thread and the 4 epilogue warps
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -200,11 +215,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // ---------------------------------------------------------- TMA producer
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB0);
-        uint32_t it = 0;
+        // Tiles are taken from a global counter in launch order, so tiles that
+        // share weight rows (a segment's token tiles, adjacent ids) start
+        // together on different SMs; each id goes to the MMA thread and the
+        // epilogue through the shared-memory tile queue.
+        uint32_t it = 0, qi = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        int u = atomicAdd(a.sched, 1);
+        while (true) {
+            const uint32_t q = qi % kTileQ;
+            if (!mbar_wait(&tq_empty[q], ((qi / kTileQ) & 1) ^ 1, abort_flag, deadline)) {
+                ok = false;
+                break;
+            }
+            tile_q[q] = u;
+            mbar_arrive(&tq_full[q]);
+            ++qi;
+            if (u >= total) break;
+            const int u_next = atomicAdd(a.sched, 1);
             TileInfo t;
             decode_tile(a, pv, u, t);
+            u = u_next;
             const int nb = (t.n + kBoxRowsB - 1) / kBoxRowsB;
             const uint32_t bytes = NUM_A * kTileABytes + NUM_B * nb * (kBoxRowsB * 128);
             const CUtensorMap* mA = t.shared ? &tmA_sh : &tmA;
@@ -230,6 +261,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                     row);
                 }
             }
+            if (!ok) break;
         }
         if (!ok) {  // drain: let every issued load land before the CTA exits
             const uint32_t first = it > uint32_t(S) ? it - S : 0;
@@ -237,10 +269,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp == 1 && lane == 0) {
         // ---------------------------------------------------------- MMA issuer
-        uint32_t it = 0, lt = 0;
+        uint32_t it = 0, lt = 0, qi = 0;
         bool ok = true;
         if (a.test_stall) ok = mbar_wait(stall_bar, 0, abort_flag, deadline);
-        for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lt) {
+        for (; ok; ++lt) {
+            const uint32_t q = qi % kTileQ;
+            if (!mbar_wait(&tq_full[q], (qi / kTileQ) & 1, abort_flag, deadline)) {
+                ok = false;
+                break;
+            }
+            const int u = tile_q[q];
+            mbar_arrive(&tq_empty[q]);
+            ++qi;
+            if (u >= total) break;
             TileInfo t;
             decode_tile(a, pv, u, t);
             const uint32_t acc = lt % C::kBufs, aph = (lt / C::kBufs) & 1;
@@ -284,8 +325,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // ---------------------------------------------------------- epilogue
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const int r = q * 32 + lane;
-        uint32_t lt = 0;
-        for (int u = blockIdx.x; u < total; u += gridDim.x, ++lt) {
+        uint32_t lt = 0, qi = 0;
+        for (;; ++lt) {
+            const uint32_t qs = qi % kTileQ;
+            if (!mbar_wait(&tq_full[qs], (qi / kTileQ) & 1, abort_flag, deadline)) break;
+            const int u = tile_q[qs];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tq_empty[qs]);
+            ++qi;
+            if (u >= total) break;
             TileInfo t;
             decode_tile(a, pv, u, t);
             const uint32_t acc = lt % C::kBufs, aph = (lt / C::kBufs) & 1;
@@ -347,7 +395,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem_base, C::kTmemCols);
     }
-    if (threadIdx.x == 0 && *abort_flag) atomicOr(a.err, 1);
+    if (threadIdx.x == 0) {
+        if (*abort_flag) atomicOr(a.err, 1);
+        // the last CTA out resets the tile counter for the next launch (every
+        // producer has taken its final id before its CTA gets here)
+        __threadfence();
+        if (atomicAdd(a.sched + 1, 1) == int(gridDim.x) - 1) {
+            a.sched[0] = 0;
+            a.sched[1] = 0;
+            __threadfence();
+        }
+    }
 }
 
 // ============================================================ activation gather
@@ -403,6 +461,7 @@ static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cuda
     args.plan_smem = (C::kSmem + plan_bytes) <= 227 * 1024;
     if (args.plan_smem) smem += plan_bytes;
     else if (!a.plan) return fail(HF_ERR_ARG, "plan-free GEMM needs its shared-memory plan slot");
+    if (!a.sched) return fail(HF_ERR_ARG, "GEMM launch without a tile-scheduler counter");
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(kern), smem));
     kern<<<grid, kGemmThreads, smem, st>>>(m.A, m.A_sh, m.A_sh2, m.B0, m.B1, m.B0_sh, m.B1_sh, args);
     HF_CUDA(cudaGetLastError());

@@ -205,7 +205,7 @@ void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra);
 hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cudaStream_t st);
 // Dense MLP pass: one group of all T tokens in order; writes groups[0] = w.
 hf_status launch_dense_plan(const RouteArgs& a, const GroupW& w, GroupW* groups, int32_t* perm,
-                            cudaStream_t st);
+                            int* sched, cudaStream_t st);
 // dst row i = src row (idx[i] / div), i < n; rows of row_bytes (multiple of 16).
 hf_status launch_gather_rows(void* dst, const void* src, size_t row_bytes, int n,
                              const int32_t* idx, int div, cudaStream_t st);
@@ -255,6 +255,9 @@ struct GemmArgs {
     // writes its partial sums to y + s * split_stride (summed by the reader)
     int nsplit, kbper;
     long long split_stride;
+    // tile scheduler: [0] next tile id, [1] CTAs done; zero before a launch,
+    // left zero by it (device memory owned by the caller, one pair per stream)
+    int* sched;
 };
 struct GemmMaps {
     CUtensorMap A, A_sh;       // weights: routed view; shared expert gate (GEMM1) or down rows

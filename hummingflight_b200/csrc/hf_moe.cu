@@ -141,6 +141,7 @@ static hf_status launch_tc_router(hf_moe_ctx* c, LayerBuf& L, const RouteArgs& r
     g.y = ra.logits;
     g.err = c->plan + c->pl.stats + 3;
     g.timeout_ns = c->timeout_ns;
+    g.sched = c->sched;
     g.nsplit = rt.nsplit;
     g.kbper = rt.kbper;
     g.split_stride = (long long)ra.T * c->E;
@@ -247,6 +248,7 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.err = c->plan + c->pl.stats + 3;
         gm.timeout_ns = c->timeout_ns;
         gm.test_stall = c->stall;
+        gm.sched = c->sched;
         GemmMaps m1 = c->maps1;
         m1.A = L.gu;
         m1.A_sh = L.sh_gate;
@@ -335,7 +337,7 @@ static void free_ctx(hf_moe_ctx* c) {
     if (c->perm_src != c->perm) cudaFree(c->perm_src);
     void* bufs[] = {c->logits, c->ids,    c->w,      c->margins, c->plan,  c->perm,
                     c->slot_pos, c->masks, c->blk_counts, c->mid, c->y,     c->x_dev,
-                    c->out_dev, c->mid_hi, c->mid_lo, c->xp_hi,   c->xp_lo};
+                    c->out_dev, c->mid_hi, c->mid_lo, c->xp_hi,   c->xp_lo, c->sched};
     for (void* p : bufs) cudaFree(p);
     if (c->err_host) cudaFreeHost(c->err_host);
     delete c;
@@ -443,6 +445,7 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
         x->perm_src = x->perm;
     }
     A(dalloc(&x->slot_pos, src_slots));
+    A(dalloc(&x->sched, 8));
     A(dalloc(&x->masks, nb * 4 * x->E));
     A(dalloc(&x->blk_counts, nb * x->E));
     A(dalloc(&x->mid, slots * x->inter_max));
@@ -482,6 +485,7 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
         }
     }
     if (cudaMemset(x->plan, 0, sizeof(int32_t) * x->pl.words) != cudaSuccess ||
+        cudaMemset(x->sched, 0, sizeof(int) * 8) != cudaSuccess ||
         cudaMallocHost(reinterpret_cast<void**>(&x->err_host), 64) != cudaSuccess) {
         free_ctx(x);
         return fail(HF_ERR_CUDA, "hf_moe_create: plan/err buffer init failed");

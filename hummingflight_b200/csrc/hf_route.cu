@@ -517,7 +517,7 @@ hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cud
 // holding all T tokens in order (perm = identity, slot id = token with k = 0).
 // Block 0 also writes the group's weight pointers and clears the error word.
 __global__ void __launch_bounds__(1024) k_dense_plan(RouteArgs a, GroupW w, GroupW* groups,
-                                                     int32_t* perm) {
+                                                     int32_t* perm, int* sched) {
     __shared__ int s_cnt[1], s_off[2];
     __shared__ int warp_tot[kPlanScratch];
     if (blockIdx.x == 0) {
@@ -525,6 +525,7 @@ __global__ void __launch_bounds__(1024) k_dense_plan(RouteArgs a, GroupW w, Grou
             groups[0] = w;
             s_cnt[0] = a.T;
             a.plan[a.pl.stats + 3] = 0;
+            sched[0] = sched[1] = 0;  // the workspace may be fresh memory
         }
         __syncthreads();
         plan_from_counts(a, s_cnt, s_off, warp_tot);
@@ -534,9 +535,9 @@ __global__ void __launch_bounds__(1024) k_dense_plan(RouteArgs a, GroupW w, Grou
 }
 
 hf_status launch_dense_plan(const RouteArgs& a, const GroupW& w, GroupW* groups, int32_t* perm,
-                            cudaStream_t st) {
+                            int* sched, cudaStream_t st) {
     const int blocks = std::max(1, std::min(64, (a.T + 1023) / 1024));
-    k_dense_plan<<<blocks, 1024, 0, st>>>(a, w, groups, perm);
+    k_dense_plan<<<blocks, 1024, 0, st>>>(a, w, groups, perm, sched);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }
