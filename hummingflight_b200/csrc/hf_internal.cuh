@@ -107,6 +107,7 @@ struct RouteArgs {
     int gemm_bn1, gemm_bn2;   // token tile (columns per tile) of GEMM1 / GEMM2
     int gemm_m2;              // weight rows per GEMM2 tile (128 or 256)
     int lsplit;               // logits are the sum of lsplit planes of [T x E] (split-K router)
+    int* route_counter;       // zeroed device int: router + routing in one launch (null: two)
 };
 
 // ------------------------------------------------------------------ device helpers
@@ -196,7 +197,9 @@ int num_sms(int device);
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device, size).
 cudaError_t ensure_smem(const void* kernel, int bytes);
 
-hf_status launch_router_logits(const RouteArgs& a, cudaStream_t st);
+// Router logits; with `routed` non-null, small batches also run the whole
+// routing in the same launch (then *routed = true and launch_route is skipped).
+hf_status launch_router_logits(const RouteArgs& a, cudaStream_t st, bool* routed = nullptr);
 // GEMM tiles (gemm_bn1, gemm_bn2, gemm_m2) for a pass over `rows` activation
 // rows; bn_override (32, 64 or 128) forces both token tiles when non-zero.
 void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra);

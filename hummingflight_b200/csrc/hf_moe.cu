@@ -88,6 +88,7 @@ RouteArgs route_args(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     ra.gemm_ok = c->gemm_ok && L.maps;
     set_gemm_tiles(c->gemm_bn, T, ra);
     ra.lsplit = use_tc_router(c, L, x, xd, T) ? router_tiles(T, c->E, c->H, c->nsm).nsplit : 1;
+    ra.route_counter = c->sched + 4;
     return ra;
 }
 
@@ -110,9 +111,10 @@ RouterTiles router_tiles(int T, int E, int H, int nsm) {
     return r;
 }
 
-// The SIMT kernels read fp32 activations exactly and serve single tokens;
-// bf16 batches from kTcRouterMinT tokens take the tensor cores.
-constexpr int kTcRouterMinT = 16;
+// The SIMT kernels read fp32 activations exactly and serve decode batches
+// (up to 16 tokens they also run the routing in the same launch); bf16
+// batches from kTcRouterMinT tokens take the tensor cores.
+constexpr int kTcRouterMinT = 17;
 
 bool use_tc_router(const hf_moe_ctx* c, const LayerBuf& L, const void* x, hf_dtype xd, int T) {
     if (!L.maps || xd != HF_BF16 || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
@@ -178,14 +180,16 @@ void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
 }
 
 hf_status run_route(hf_moe_ctx* c, LayerBuf& L, const RouteArgs& ra, cudaStream_t st) {
+    bool routed = false;
     {
         PhaseTimer p0(c, st, 0);
         if (ra.lsplit > 1 || use_tc_router(c, L, ra.x, ra.x_f32 ? HF_F32 : HF_BF16, ra.T))
             HF_TRY(launch_tc_router(c, L, ra, st));
         else
-            HF_TRY(launch_router_logits(ra, st));
+            HF_TRY(launch_router_logits(ra, st, &routed));
         p0.done(1);
     }
+    if (routed) return HF_OK;
     PhaseTimer p1(c, st, 1);
     int n = 0;
     HF_TRY(launch_route(ra, st, &n));

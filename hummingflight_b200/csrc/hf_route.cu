@@ -41,7 +41,7 @@ __device__ __forceinline__ void load_x8(const void* x, size_t elem, float (&o)[8
 }
 
 template <bool XF32>
-__global__ void __launch_bounds__(256) k_router_gemv(RouteArgs a) {
+__device__ __forceinline__ void router_rows(const RouteArgs& a) {
     __shared__ float part[kRouterSlices][kRouterRowsPerBlock][kRouterMaxT];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rloc = warp / kRouterSlices, slice = warp % kRouterSlices;
@@ -107,6 +107,11 @@ __global__ void __launch_bounds__(256) k_router_gemv(RouteArgs a) {
             a.logits[size_t(t) * a.E + r] = s;
         }
     }
+}
+
+template <bool XF32>
+__global__ void __launch_bounds__(256) k_router_gemv(RouteArgs a) {
+    router_rows<XF32>(a);
 }
 
 // Large T: 64 tokens x 64 experts per block, K in steps of 32, 4x4 per thread.
@@ -397,8 +402,7 @@ __device__ __forceinline__ int mask_rank(const uint32_t* m, int tl) {
 constexpr int kFusedTopkMaxT = 16;
 
 template <int NPL, bool TOPK>
-__global__ void __launch_bounds__(1024) k_route_block(RouteArgs a) {
-    extern __shared__ __align__(16) uint32_t sm[];
+__device__ void route_block_body(const RouteArgs& a, uint32_t* sm) {
     const int E = a.E, T = a.T, k = a.k, G = a.pl.G;
     uint32_t* masks = sm;                                   // [E][4]
     int* s_cnt = reinterpret_cast<int*>(masks + 4 * E);     // [G]
@@ -409,7 +413,7 @@ __global__ void __launch_bounds__(1024) k_route_block(RouteArgs a) {
     for (int i = threadIdx.x; i < 4 * E; i += blockDim.x) masks[i] = 0u;
     if constexpr (TOPK) {
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        for (int t = warp; t < T; t += 32)
+        for (int t = warp; t < T; t += int(blockDim.x >> 5))
             topk_warp<NPL>(a.logits + size_t(t) * E, a.lsplit, size_t(T) * E, 1, a.bias, E, k,
                            a.scale, a.norm, lane,
                            a.ids + size_t(t) * k, a.w + size_t(t) * k,
@@ -446,6 +450,33 @@ __global__ void __launch_bounds__(1024) k_route_block(RouteArgs a) {
             a.slot_pos[slot] = pos;
         }
 }
+
+template <int NPL, bool TOPK>
+__global__ void __launch_bounds__(1024) k_route_block(RouteArgs a) {
+    extern __shared__ __align__(16) uint32_t sm[];
+    route_block_body<NPL, TOPK>(a, sm);
+}
+
+// Decode (T <= kFusedTopkMaxT): router rows, then the last block to finish
+// (a device counter, reset by that block) runs top-k, counts, plan and
+// permutation over all logits -- one launch instead of two. Every block
+// fences its logits before it counts itself in, the last one after it has
+// seen the full count.
+template <bool XF32, int NPL>
+__global__ void __launch_bounds__(256) k_router_route(RouteArgs a) {
+    extern __shared__ __align__(16) uint32_t sm[];
+    __shared__ int s_last;
+    router_rows<XF32>(a);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(a.route_counter, 1) == int(gridDim.x) - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    route_block_body<NPL, true>(a, sm);
+    if (threadIdx.x == 0) *a.route_counter = 0;
+}
+
 
 // ============================================================ T > 128: four launches
 // (1) k_topk, (2) masks + per-block counts, (3) scan + plan + per-block bases,
@@ -602,10 +633,26 @@ __global__ void __launch_bounds__(256) k_perm_scatter(RouteArgs a) {
         else { constexpr int NPL = 32; __VA_ARGS__; }              \
     } while (0)
 
-hf_status launch_router_logits(const RouteArgs& a, cudaStream_t st) {
+size_t route_block_smem(const RouteArgs& a) {
+    const int G = a.pl.G;
+    return sizeof(uint32_t) * (4 * a.E + G + G + 1 + kSmallRouteT * kMaxTopK + kPlanScratch);
+}
+
+hf_status launch_router_logits(const RouteArgs& a, cudaStream_t st, bool* routed) {
+    if (routed) *routed = false;
     if (a.T == 0) return HF_OK;
+    const int grid = (a.E + kRouterRowsPerBlock - 1) / kRouterRowsPerBlock;
+    if (routed && a.route_counter && a.T <= kFusedTopkMaxT && a.lsplit == 1 && a.pl.G <= 2 * 256) {
+        const size_t smem = route_block_smem(a);
+        HF_NPL_SWITCH(a.E, {
+            if (a.x_f32) k_router_route<true, NPL><<<grid, 256, smem, st>>>(a);
+            else k_router_route<false, NPL><<<grid, 256, smem, st>>>(a);
+        });
+        HF_CUDA(cudaGetLastError());
+        *routed = true;
+        return HF_OK;
+    }
     if (a.T <= kRouterMaxT) {
-        const int grid = (a.E + kRouterRowsPerBlock - 1) / kRouterRowsPerBlock;
         if (a.x_f32) k_router_gemv<true><<<grid, 256, 0, st>>>(a);
         else k_router_gemv<false><<<grid, 256, 0, st>>>(a);
     } else {
@@ -622,8 +669,7 @@ hf_status launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
     if (a.T == 0) return HF_OK;
     const int G = a.pl.G;
     if (a.T <= kSmallRouteT) {
-        const size_t smem =
-            sizeof(uint32_t) * (4 * a.E + G + G + 1 + kSmallRouteT * kMaxTopK + kPlanScratch);
+        const size_t smem = route_block_smem(a);
         if (a.T <= kFusedTopkMaxT) {
             *launches = 1;
             HF_NPL_SWITCH(a.E, { k_route_block<NPL, true><<<1, 1024, smem, st>>>(a); });
