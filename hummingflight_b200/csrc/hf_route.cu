@@ -213,14 +213,17 @@ __device__ __forceinline__ void topk_warp(const float* row, int planes, size_t p
             v[j] = -INFINITY;
         }
     }
+    // k (+1 for the margin) rounds of a warp argmax; lane r keeps the r-th
+    // pick. The round loop stays rolled: this code runs once per token, so
+    // its instruction footprint (cold at every launch) costs more than the
+    // loop overhead.
     uint32_t taken = 0;
-    int sel_i[kMaxTopK];
-    float sel_s[kMaxTopK];
+    int my_i = 0;
+    float my_s = 0.0f;
     float kth = 0.0f, next = -INFINITY;
     const int rounds = (k < E) ? k + 1 : k;
-#pragma unroll
-    for (int r = 0; r < kMaxTopK + 1; ++r) {
-        if (r >= rounds) break;
+#pragma unroll 1
+    for (int r = 0; r < rounds; ++r) {
         float bv = -INFINITY, bs = 0.0f;
         int bi = 0x7fffffff;
 #pragma unroll
@@ -244,28 +247,26 @@ __device__ __forceinline__ void topk_warp(const float* row, int planes, size_t p
             }
         }
         if (r < k) {
-            sel_i[r] = bi;
-            sel_s[r] = bs;
+            if (lane == r) {
+                my_i = bi;
+                my_s = bs;
+            }
             kth = bv;
             if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
         } else {
             next = bv;
         }
     }
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kMaxTopK; ++i)
-        if (i < k) sum = __fadd_rn(sum, sel_s[i]);
-#pragma unroll
-    for (int i = 0; i < kMaxTopK; ++i) {
-        if (i < k && lane == i) {
-            float wi = sel_s[i];
-            if (norm && sum > 0.0f) wi = __fdiv_rn(wi, sum);
-            wi = __fmul_rn(wi, scale);
-            ids_out[i] = sel_i[i];
-            w_out[i] = wi;
-            if (ids_smem) ids_smem[i] = sel_i[i];
-        }
+    float sum = 0.0f;  // rank order, as the reference sums
+#pragma unroll 1
+    for (int i = 0; i < k; ++i) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, my_s, i));
+    if (lane < k) {
+        float wi = my_s;
+        if (norm && sum > 0.0f) wi = __fdiv_rn(wi, sum);
+        wi = __fmul_rn(wi, scale);
+        ids_out[lane] = my_i;
+        w_out[lane] = wi;
+        if (ids_smem) ids_smem[lane] = my_i;
     }
     if (lane == 0 && margin_out) *margin_out = (k < E) ? __fsub_rn(kth, next) : INFINITY;
 }
