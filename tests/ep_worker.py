@@ -52,10 +52,11 @@ def main():
         sl = slice(rank * t_local, (rank + 1) * t_local)
         k = min(shape.top_k, shape.num_experts)
         # Expert products are bit-identical. The combined output is too when
-        # both runs use the same router kernel (T <= 64 on both sides); when
-        # the single-GPU batch is larger it takes the tiled router, whose
-        # different summation order can move a top-k weight by one ulp.
-        same_router = (T <= 64) == (t_local <= 64)
+        # both runs compute the router logits the same way: up to 16 bf16
+        # tokens both take the SIMT router; larger batches take the tensor-core
+        # router, whose K split (and so its summation order) depends on the
+        # batch size and can move a top-k weight by one ulp.
+        same_router = T <= 16
         ref = out_one[sl]
         tol = 0.0 if same_router else 1e-6 * float(ref.abs().max())
         ok_out = float((out_ep - ref).abs().max()) <= tol
