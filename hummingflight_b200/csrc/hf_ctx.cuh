@@ -161,7 +161,8 @@ struct ExpertWork {
     int x_f32;
     int T, k;
     float* y;          // [positions x H]
-    int bn1, bn2, m2;  // GEMM tiles the plan's tile prefixes were built with
+    int bn1, bn2, m1, m2;  // GEMM tiles the plan's tile prefixes were built with
+    int pair;              // the GEMM tiles run on CTA pairs
     bool maybe_gemm;   // some segment may take the GEMM / the GEMV (else skip the launches)
     bool maybe_gemv;
 };

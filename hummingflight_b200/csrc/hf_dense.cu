@@ -186,7 +186,8 @@ hf_status hf_dense_mlp_forward(const uint16_t* gate, const uint16_t* upw, const 
     gm.Is = I;
     gm.Imax = I;
     gm.bn = ra.gemm_bn1;
-    gm.mrows = 128;
+    gm.mrows = ra.gemm_m1;
+    gm.pair = ra.gemm_pair;
     gm.mid_hi = mid_hi;
     gm.mid_lo = mid_lo;
     gm.y = out;

@@ -279,7 +279,9 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     w.y = c->y;
     w.bn1 = rl.gemm_bn1;
     w.bn2 = rl.gemm_bn2;
+    w.m1 = rl.gemm_m1;
     w.m2 = rl.gemm_m2;
+    w.pair = rl.gemm_pair;
     w.maybe_gemm = rl.gemm_ok && (c->cfg.path == HF_PATH_GEMM || maxseg > rl.gemv_max);
     w.maybe_gemv = !rl.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
                    (c->cfg.path == HF_PATH_AUTO && rl.gemv_max > 0);

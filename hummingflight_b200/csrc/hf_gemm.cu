@@ -24,6 +24,10 @@
 // buffered TMEM accumulators. Every wait is bounded (see hf_sm100.cuh): on
 // timeout the CTA drains its TMA loads and MMAs, frees TMEM and reports
 // HF_ERR_TIMEOUT through the error word instead of hanging.
+#include <algorithm>
+#include <map>
+#include <mutex>
+
 #include "hf_internal.cuh"
 #include "hf_sm100.cuh"
 
@@ -38,9 +42,13 @@ constexpr uint64_t kDrainNs = 500ull * 1000 * 1000;
 constexpr int kTileQ = 8;        // tile ids in flight from the producer to the MMA / epilogue
 constexpr int kBarBytes = 512;   // barriers, tile queue, TMEM slot, abort flag
 
-template <int NUM_A, int NUM_B, int BN>
+// PAIR: a cluster of two CTAs computes a 256-row tile with cta_group::2 MMAs;
+// each CTA then holds its own 128 weight rows per A tile and half of the BN
+// token rows, so it loads half the activation bytes of a one-CTA tile.
+template <int NUM_A, int NUM_B, int BN, bool PAIR = false>
 struct GemmCfg {
-    static constexpr int kStageBytes = NUM_A * kTileABytes + NUM_B * BN * 128;
+    static constexpr int kBRows = PAIR ? BN / 2 : BN;  // token rows of B per CTA
+    static constexpr int kStageBytes = NUM_A * kTileABytes + NUM_B * kBRows * 128;
     static constexpr int kStages0 = (220 * 1024) / kStageBytes;
     static constexpr int kStages = kStages0 > 12 ? 12 : kStages0;
     static constexpr int kAccCols = NUM_A * BN;
@@ -57,6 +65,7 @@ struct GemmCfg {
     static_assert((2 * kStages + 6 + 2 * kTileQ) * 8 + kTileQ * 4 + 8 <= kBarBytes,
                   "barrier area overflow");
     static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
+    static_assert(!PAIR || (BN % 32 == 0 && kBufs == 2), "pair tiles: BN/2 in 16-row boxes, 2 buffers");
 };
 
 struct TileInfo {
@@ -128,14 +137,15 @@ __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
     return true;
 }
 
-template <int NUM_A, int NUM_B, int BN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    k_moe_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_sh,
-               const __grid_constant__ CUtensorMap tmA_sh2,
-               const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
-               const __grid_constant__ CUtensorMap tmB0_sh,
-               const __grid_constant__ CUtensorMap tmB1_sh, GemmArgs a) {
-    using C = GemmCfg<NUM_A, NUM_B, BN>;
+// Kernel body. One CTA (PAIR = false) or one CTA of a pair (PAIR = true; rank
+// 0 is the leader: it takes tile ids, arms the stage barriers and issues the
+// MMAs for both; both CTAs load their halves and run their own epilogue).
+template <int NUM_A, int NUM_B, int BN, bool PAIR>
+__device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmA_sh,
+                                          const CUtensorMap& tmA_sh2, const CUtensorMap& tmB0,
+                                          const CUtensorMap& tmB1, const CUtensorMap& tmB0_sh,
+                                          const CUtensorMap& tmB1_sh, const GemmArgs& a) {
+    using C = GemmCfg<NUM_A, NUM_B, BN, PAIR>;
     constexpr int S = C::kStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -153,6 +163,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;
+    const bool leader = rank == 0;
+    const int row_off = int(rank) * 128;  // this CTA's weight rows inside a pair tile
     const uint64_t deadline = globaltimer() + a.timeout_ns;
     const int G = a.pl.G;
     int total;
@@ -191,83 +204,130 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 4);
+            mbar_init(&tempty[b], PAIR ? 8 : 4);  // epilogue warps of this CTA (and the peer)
         }
         mbar_init(final_bar, 1);
         mbar_init(stall_bar, 1);
         for (int q = 0; q < kTileQ; ++q) {
             mbar_init(&tq_full[q], 1);
-            mbar_init(&tq_empty[q], 5);  // the MMA thread and the 4 epilogue warps
+            // MMA thread + 4 epilogue warps (+ the peer's producer and 4 epilogue warps)
+            mbar_init(&tq_empty[q], PAIR ? 10 : 5);
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, C::kTmemCols);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, C::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, C::kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
+    // waits: barriers that the peer CTA (or its TMA / MMA completions) arrive
+    // on are waited on with cluster-scope acquire
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return PAIR ? mbar_wait_cl(bar, parity, abort_flag, deadline)
+                    : mbar_wait(bar, parity, abort_flag, deadline);
+    };
+
     if (warp == 0 && lane == 0) {
         // ---------------------------------------------------------- TMA producer
-        tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB0);
         // Tiles are taken from a global counter in launch order, so tiles that
         // share weight rows (a segment's token tiles, adjacent ids) start
         // together on different SMs; each id goes to the MMA thread and the
-        // epilogue through the shared-memory tile queue.
+        // epilogue (and the peer CTA) through the shared-memory tile queue.
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB0);
         uint32_t it = 0, qi = 0;
         bool ok = true;
-        int u = atomicAdd(a.sched, 1);
+        int u = leader ? atomicAdd(a.sched, 1) : 0;
         while (true) {
             const uint32_t q = qi % kTileQ;
-            if (!mbar_wait(&tq_empty[q], ((qi / kTileQ) & 1) ^ 1, abort_flag, deadline)) {
-                ok = false;
-                break;
+            if (leader) {
+                if (!wait(&tq_empty[q], ((qi / kTileQ) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                tile_q[q] = u;
+                mbar_arrive(&tq_full[q]);
+                if constexpr (PAIR) {
+                    st_cluster_u32(cluster_addr(&tile_q[q], 1), uint32_t(u));
+                    mbar_arrive_remote(cluster_addr(&tq_full[q], 1));
+                }
+            } else {
+                if (!wait(&tq_full[q], (qi / kTileQ) & 1)) {
+                    ok = false;
+                    break;
+                }
+                u = tile_q[q];
+                mbar_arrive_remote(cluster_addr(&tq_empty[q], 0));
             }
-            tile_q[q] = u;
-            mbar_arrive(&tq_full[q]);
             ++qi;
             if (u >= total) break;
-            const int u_next = atomicAdd(a.sched, 1);
+            const int u_next = leader ? atomicAdd(a.sched, 1) : 0;
             TileInfo t;
             decode_tile(a, pv, u, t);
             u = u_next;
-            const int nb = (t.n + kBoxRowsB - 1) / kBoxRowsB;
-            const uint32_t bytes = NUM_A * kTileABytes + NUM_B * nb * (kBoxRowsB * 128);
+            // token rows of B this CTA loads: all of the tile (one CTA) or its
+            // half of the MMA's N (pair; N rounded up to 32)
+            const int half = PAIR ? ((t.n + 31) & ~31) / 2 : 0;
+            const int nb = PAIR ? half / kBoxRowsB : (t.n + kBoxRowsB - 1) / kBoxRowsB;
+            const int brow0 = t.seg + t.n0 + (PAIR ? int(rank) * half : 0);
+            const uint32_t bytes = (NUM_A * kTileABytes + NUM_B * nb * (kBoxRowsB * 128)) * (PAIR ? 2 : 1);
             const CUtensorMap* mA = t.shared ? &tmA_sh : &tmA;
             const CUtensorMap* mA1 = (t.shared && a.which == 1) ? &tmA_sh2 : mA;
             const CUtensorMap* mB0 = (a.which == 2 && t.shared) ? &tmB0_sh : &tmB0;
             const CUtensorMap* mB1 = (a.which == 2 && t.shared) ? &tmB1_sh : &tmB1;
+            const int rA0 = t.rowA0 + (PAIR ? row_off : 0);
+            const int rA1 = PAIR ? t.rowA1 + row_off : t.rowA1;
             for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
                 const uint32_t s = it % S, ph = (it / S) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, deadline)) {
+                if (!wait(&empty[s], ph ^ 1)) {
                     ok = false;
                     break;
                 }
                 uint8_t* st = smem + s * C::kStageBytes;
-                mbar_arrive_expect_tx(&full[s], bytes);
-                tma_load_2d(st, mA, &full[s], kb * 64, t.rowA0);
-                if (NUM_A == 2) tma_load_2d(st + kTileABytes, mA1, &full[s], kb * 64, t.rowA1);
                 uint8_t* sb = st + NUM_A * kTileABytes;
-                for (int j = 0; j < nb; ++j) {
-                    const int row = t.seg + t.n0 + j * kBoxRowsB;
-                    tma_load_2d(sb + j * (kBoxRowsB * 128), mB0, &full[s], kb * 64, row);
-                    if (NUM_B == 2)
-                        tma_load_2d(sb + BN * 128 + j * (kBoxRowsB * 128), mB1, &full[s], kb * 64,
-                                    row);
+                if constexpr (PAIR) {
+                    const uint32_t fb = cluster_addr(&full[s], 0);
+                    if (leader) mbar_arrive_expect_tx(&full[s], bytes);
+                    tma_load_2d_pair(st, mA, fb, kb * 64, rA0);
+                    if (NUM_A == 2) tma_load_2d_pair(st + kTileABytes, mA1, fb, kb * 64, rA1);
+                    for (int j = 0; j < nb; ++j) {
+                        const int row = brow0 + j * kBoxRowsB;
+                        tma_load_2d_pair(sb + j * (kBoxRowsB * 128), mB0, fb, kb * 64, row);
+                        if (NUM_B == 2)
+                            tma_load_2d_pair(sb + C::kBRows * 128 + j * (kBoxRowsB * 128), mB1, fb,
+                                             kb * 64, row);
+                    }
+                } else {
+                    mbar_arrive_expect_tx(&full[s], bytes);
+                    tma_load_2d(st, mA, &full[s], kb * 64, rA0);
+                    if (NUM_A == 2) tma_load_2d(st + kTileABytes, mA1, &full[s], kb * 64, rA1);
+                    for (int j = 0; j < nb; ++j) {
+                        const int row = brow0 + j * kBoxRowsB;
+                        tma_load_2d(sb + j * (kBoxRowsB * 128), mB0, &full[s], kb * 64, row);
+                        if (NUM_B == 2)
+                            tma_load_2d(sb + BN * 128 + j * (kBoxRowsB * 128), mB1, &full[s],
+                                        kb * 64, row);
+                    }
                 }
             }
             if (!ok) break;
         }
-        if (!ok) {  // drain: let every issued load land before the CTA exits
+        if (!ok && leader) {  // drain: let every issued load land before the CTA exits
             const uint32_t first = it > uint32_t(S) ? it - S : 0;
             for (uint32_t i = first; i < it; ++i) drain_wait(&full[i % S], (i / S) & 1);
         }
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1 && lane == 0 && leader) {
         // ---------------------------------------------------------- MMA issuer
         uint32_t it = 0, lt = 0, qi = 0;
         bool ok = true;
@@ -285,17 +345,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             TileInfo t;
             decode_tile(a, pv, u, t);
             const uint32_t acc = lt % C::kBufs, aph = (lt / C::kBufs) & 1;
-            if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag, deadline)) {
+            if (!wait(&tempty[acc], aph ^ 1)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t nmma = uint32_t((t.n + 15) & ~15);
-            const uint32_t idesc = idesc_bf16_m128(nmma);
+            const uint32_t nmma = PAIR ? uint32_t((t.n + 31) & ~31) : uint32_t((t.n + 15) & ~15);
+            const uint32_t idesc = PAIR ? idesc_bf16_m256(nmma) : idesc_bf16_m128(nmma);
             const uint32_t d0 = tmem_base + acc * C::kAccCols;
             for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
                 const uint32_t s = it % S, ph = (it / S) & 1;
-                if (!mbar_wait(&full[s], ph, abort_flag, deadline)) {
+                if (!wait(&full[s], ph)) {
                     ok = false;
                     break;
                 }
@@ -308,18 +368,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const uint64_t ad = desc_k_sw128(st + ai * kTileABytes) + 2 * kk;
 #pragma unroll
                         for (int bi = 0; bi < NUM_B; ++bi) {
-                            const uint64_t bd =
-                                desc_k_sw128(st + NUM_A * kTileABytes + bi * BN * 128) + 2 * kk;
-                            mma_bf16(d0 + ai * BN, ad, bd, idesc, (kb != t.kb0 || kk || bi));
+                            const uint64_t bd = desc_k_sw128(st + NUM_A * kTileABytes +
+                                                             bi * C::kBRows * 128) +
+                                                2 * kk;
+                            const uint32_t accum = (kb != t.kb0 || kk || bi);
+                            if constexpr (PAIR) mma_bf16_pair(d0 + ai * BN, ad, bd, idesc, accum);
+                            else mma_bf16(d0 + ai * BN, ad, bd, idesc, accum);
                         }
                     }
                 }
-                mma_commit(&empty[s]);
+                if constexpr (PAIR) {  // the stage is free in both CTAs
+                    mma_commit_pair(smem_u32(&empty[s]));
+                    mma_commit_pair(cluster_addr(&empty[s], 1));
+                } else {
+                    mma_commit(&empty[s]);
+                }
             }
             if (!ok) break;
-            mma_commit(&tfull[acc]);
+            if constexpr (PAIR) {
+                mma_commit_pair(smem_u32(&tfull[acc]));
+                mma_commit_pair(cluster_addr(&tfull[acc], 1));
+            } else {
+                mma_commit(&tfull[acc]);
+            }
         }
-        mma_commit(final_bar);  // completes once every MMA issued above is done
+        // completes once every MMA issued above is done
+        if constexpr (PAIR) mma_commit_pair(smem_u32(final_bar));
+        else mma_commit(final_bar);
         drain_wait(final_bar, 0);
     } else if (warp >= 2) {
         // ---------------------------------------------------------- epilogue
@@ -328,20 +403,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint32_t lt = 0, qi = 0;
         for (;; ++lt) {
             const uint32_t qs = qi % kTileQ;
-            if (!mbar_wait(&tq_full[qs], (qi / kTileQ) & 1, abort_flag, deadline)) break;
+            if (!wait(&tq_full[qs], (qi / kTileQ) & 1)) break;
             const int u = tile_q[qs];
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tq_empty[qs]);
+            if (lane == 0) {
+                if (leader) mbar_arrive(&tq_empty[qs]);
+                else mbar_arrive_remote(cluster_addr(&tq_empty[qs], 0));
+            }
             ++qi;
             if (u >= total) break;
             TileInfo t;
             decode_tile(a, pv, u, t);
             const uint32_t acc = lt % C::kBufs, aph = (lt / C::kBufs) & 1;
-            if (!mbar_wait(&tfull[acc], aph, abort_flag, deadline)) break;
+            if (!wait(&tfull[acc], aph)) break;
             tc_fence_after();
             const uint32_t ta = tmem_base + (uint32_t(q * 32) << 16) + acc * C::kAccCols;
-            const bool rv = r < t.mvalid;
-            const bool rv1 = r + 128 < t.mvalid;  // second down row block
+            const int rr = r + (PAIR ? row_off : 0);  // weight row inside the tile
+            const bool rv = rr < t.mvalid;
+            const bool rv1 = !PAIR && r + 128 < t.mvalid;  // second down row block (one CTA)
             // columns per TMEM load: 32, or 16 for 16-token tiles (an x32 load
             // would reach past the allocated columns)
             constexpr int CW = BN < 32 ? BN : 32;
@@ -365,8 +444,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 const float m = swiglu(__uint_as_float(v0[j]), __uint_as_float(v1[j]));
                                 const uint16_t hi = f32_to_bf16_rne(m);
                                 const uint16_t lo = f32_to_bf16_rne(__fsub_rn(m, bf16_to_f32(hi)));
-                                a.mid_hi[pos * a.Imax + t.m0 + r] = hi;
-                                a.mid_lo[pos * a.Imax + t.m0 + r] = lo;
+                                a.mid_hi[pos * a.Imax + t.m0 + rr] = hi;
+                                a.mid_lo[pos * a.Imax + t.m0 + rr] = lo;
                             }
                         }
                     }
@@ -376,7 +455,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const int col = c0 + j;
                         if (col < t.n) {
                             const size_t pos = size_t(t.seg + t.n0 + col);
-                            float* yr = a.y + t.yoff + pos * a.H + t.m0 + r;
+                            float* yr = a.y + t.yoff + pos * a.H + t.m0 + rr;
                             if (rv) yr[0] = __uint_as_float(v0[j]);
                             if (NUM_A == 2 && rv1) yr[128] = __uint_as_float(v1[j]);
                         }
@@ -385,15 +464,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (lane == 0) {
+                if (leader) mbar_arrive(&tempty[acc]);
+                else mbar_arrive_remote(cluster_addr(&tempty[acc], 0));
+            }
         }
     }
     __syncwarp();  // reconverge warps 0 and 1 (one lane of each ran a role loop)
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // no remote arrive or TMEM write targets a finished CTA
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::kTmemCols);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::kTmemCols);
+        else tmem_dealloc(tmem_base, C::kTmemCols);
     }
     if (threadIdx.x == 0) {
         if (*abort_flag) atomicOr(a.err, 1);
@@ -406,6 +490,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             __threadfence();
         }
     }
+}
+
+template <int NUM_A, int NUM_B, int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    k_moe_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_sh,
+               const __grid_constant__ CUtensorMap tmA_sh2,
+               const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
+               const __grid_constant__ CUtensorMap tmB0_sh,
+               const __grid_constant__ CUtensorMap tmB1_sh, GemmArgs a) {
+    gemm_body<NUM_A, NUM_B, BN, false>(tmA, tmA_sh, tmA_sh2, tmB0, tmB1, tmB0_sh, tmB1_sh, a);
+}
+
+template <int NUM_A, int NUM_B, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    k_moe_gemm_pair(const __grid_constant__ CUtensorMap tmA,
+                    const __grid_constant__ CUtensorMap tmA_sh,
+                    const __grid_constant__ CUtensorMap tmA_sh2,
+                    const __grid_constant__ CUtensorMap tmB0,
+                    const __grid_constant__ CUtensorMap tmB1,
+                    const __grid_constant__ CUtensorMap tmB0_sh,
+                    const __grid_constant__ CUtensorMap tmB1_sh, GemmArgs a) {
+    gemm_body<NUM_A, NUM_B, BN, true>(tmA, tmA_sh, tmA_sh2, tmB0, tmB1, tmB0_sh, tmB1_sh, a);
 }
 
 // ============================================================ activation gather
@@ -451,10 +557,37 @@ __global__ void __launch_bounds__(256) k_gather_x(GatherArgs a) {
 }
 
 // ============================================================ host launchers
-template <int NUM_A, int NUM_B, int BN>
+// Grid of a pair kernel: two CTAs per cluster that can be resident at once
+// (an odd SM left in a GPC cannot host a pair), at most `want`.
+static int pair_grid(const void* kern, int smem, int want) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> cache;  // (kernel, device) -> CTAs
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find({kern, dev});
+    if (it == cache.end()) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(unsigned(want & ~1));
+        cfg.blockDim = dim3(kGemmThreads);
+        cfg.dynamicSmemBytes = size_t(smem);
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+            cudaGetLastError();
+            clusters = want / 2;
+        }
+        it = cache.emplace(std::make_pair(kern, dev), 2 * clusters).first;
+    }
+    return std::max(2, std::min(want & ~1, it->second));
+}
+
+template <int NUM_A, int NUM_B, int BN, bool PAIR = false>
 static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cudaStream_t st) {
-    using C = GemmCfg<NUM_A, NUM_B, BN>;
-    auto kern = k_moe_gemm<NUM_A, NUM_B, BN>;
+    using C = GemmCfg<NUM_A, NUM_B, BN, PAIR>;
+    auto kern = [] {
+        if constexpr (PAIR) return k_moe_gemm_pair<NUM_A, NUM_B, BN>;
+        else return k_moe_gemm<NUM_A, NUM_B, BN>;
+    }();
     GemmArgs args = a;
     const int plan_bytes = ((3 * a.pl.G + 1) * 4 + 15) & ~15;
     int smem = C::kSmem;
@@ -463,12 +596,19 @@ static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cuda
     else if (!a.plan) return fail(HF_ERR_ARG, "plan-free GEMM needs its shared-memory plan slot");
     if (!a.sched) return fail(HF_ERR_ARG, "GEMM launch without a tile-scheduler counter");
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(kern), smem));
+    if (PAIR) grid = pair_grid(reinterpret_cast<const void*>(kern), smem, grid);
     kern<<<grid, kGemmThreads, smem, st>>>(m.A, m.A_sh, m.A_sh2, m.B0, m.B1, m.B0_sh, m.B1_sh, args);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }
 
 hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid, cudaStream_t st) {
+    if (a.pair && a.which == 1) {  // prefill gate/up: 256-row tiles on CTA pairs
+        if (a.bn == 128 && a.mrows == 256)
+            return num_b == 1 ? launch_one<2, 1, 128, true>(m, a, grid, st)
+                              : launch_one<2, 2, 128, true>(m, a, grid, st);
+        return fail(HF_ERR_ARG, "unsupported pair GEMM tile");
+    }
     if (a.which == 1) {
         if (a.bn == 32) return num_b == 1 ? launch_one<2, 1, 32>(m, a, grid, st)
                                           : launch_one<2, 2, 32>(m, a, grid, st);

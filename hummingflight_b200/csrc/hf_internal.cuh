@@ -105,7 +105,8 @@ struct RouteArgs {
     int gemv_max;             // AUTO threshold
     int gemm_ok;              // shapes allow the tcgen05 GEMM (64-aligned)
     int gemm_bn1, gemm_bn2;   // token tile (columns per tile) of GEMM1 / GEMM2
-    int gemm_m2;              // weight rows per GEMM2 tile (128 or 256)
+    int gemm_m1, gemm_m2;     // weight rows per GEMM1 / GEMM2 tile (128 or 256)
+    int gemm_pair;            // GEMM tiles run on CTA pairs
     int lsplit;               // logits are the sum of lsplit planes of [T x E] (split-K router)
     int* route_counter;       // zeroed device int: router + routing in one launch (null: two)
 };
@@ -244,7 +245,8 @@ struct GemmArgs {
     PlanLayout pl;
     int which;              // 1: gate/up + SwiGLU -> mid hi/lo; 2: down -> y
     int H, I, Is, Imax, bn;
-    int mrows;              // weight rows per tile: 128, or 256 for GEMM2 with two row blocks
+    int mrows;              // weight rows per tile: 128, or 256 (two row blocks, or a CTA pair)
+    int pair;               // tiles run on CTA pairs (cta_group::2), 128 weight rows per CTA
     uint16_t* mid_hi;       // [slots x Imax] bf16
     uint16_t* mid_lo;
     float* y;               // [slots x H] fp32

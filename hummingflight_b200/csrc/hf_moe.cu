@@ -160,12 +160,15 @@ int gemv_threshold(const hf_moe_ctx* c, int rows) {
 // shared memory to the weight ring -- gate/up 32-token tiles (two 16 KB
 // weight boxes + 4 KB of tokens a stage, 6 stages), down 256 weight rows x
 // 16 tokens (32 KB + 4 KB, 6 stages: as many weight bytes in flight as
-// gate/up, against 9 x 16 KB for 128 x 32 tiles). Prefill (>= 1024 rows): down tiles of 256 weight rows x 128 tokens
-// load each activation tile once per 256 output rows (a third fewer operand
-// bytes per MMA flop than 128 x 128). Gate/up keeps 128 x 128 tiles with two
-// accumulators: at 256 tokens the single TMEM buffer it would need measured
-// slower.
+// gate/up, against 9 x 16 KB for 128 x 32 tiles). Prefill (>= 1024 rows):
+// 256 weight rows a tile. Gate/up runs on CTA pairs (cta_group::2, 256
+// intermediate rows x 128 tokens): each SM loads half the activations of a
+// one-CTA tile and the TMEM accumulators stay double-buffered (7 % faster on
+// config 2). Down keeps one CTA with two 128-row accumulators x 128 tokens:
+// the pair's 256 x 256 tile measured 5 % slower there.
 void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
+    ra.gemm_m1 = 128;
+    ra.gemm_pair = 0;
     if (bn_override) {
         ra.gemm_bn1 = ra.gemm_bn2 = bn_override;
         ra.gemm_m2 = 128;
@@ -173,9 +176,15 @@ void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
         ra.gemm_bn1 = 32;
         ra.gemm_bn2 = 16;
         ra.gemm_m2 = 256;
-    } else {
+    } else if (rows < 1024) {
         ra.gemm_bn1 = ra.gemm_bn2 = 128;
-        ra.gemm_m2 = rows < 1024 ? 128 : 256;
+        ra.gemm_m2 = 128;
+    } else {  // prefill: 256 weight rows per tile
+        ra.gemm_pair = 1;  // gate/up on CTA pairs
+        ra.gemm_bn1 = 128;
+        ra.gemm_m1 = 256;
+        ra.gemm_bn2 = 128;  // down on one CTA (two 128-row accumulators)
+        ra.gemm_m2 = 256;
     }
 }
 
@@ -245,7 +254,8 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.Is = c->Is;
         gm.Imax = c->inter_max;
         gm.bn = w.bn1;
-        gm.mrows = 128;
+        gm.mrows = w.m1;
+        gm.pair = w.pair;
         gm.mid_hi = c->mid_hi;
         gm.mid_lo = c->mid_lo;
         gm.y = w.y;
@@ -707,7 +717,9 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
         w.y = c->y;
         w.bn1 = ra.gemm_bn1;
         w.bn2 = ra.gemm_bn2;
+        w.m1 = ra.gemm_m1;
         w.m2 = ra.gemm_m2;
+        w.pair = ra.gemm_pair;
         // segments can only exceed the GEMV threshold when T does
         w.maybe_gemm = ra.gemm_ok && (c->cfg.path == HF_PATH_GEMM || T > ra.gemv_max);
         w.maybe_gemv = !ra.gemm_ok || c->cfg.path == HF_PATH_GEMV ||

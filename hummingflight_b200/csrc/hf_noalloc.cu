@@ -117,7 +117,8 @@ extern "C" hf_status hf_moe_route_noalloc(const uint16_t* router_bf16, const flo
     a.gemm_ok = 0;
     a.gemm_bn1 = a.gemm_bn2 = 64;
     a.lsplit = 1;
-    a.gemm_m2 = 128;
+    a.gemm_m1 = a.gemm_m2 = 128;
+    a.gemm_pair = 0;
     HF_TRY(launch_router_logits(a, st));
     int n = 0;
     HF_TRY(launch_route(a, st, &n));

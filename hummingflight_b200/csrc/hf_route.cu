@@ -320,7 +320,7 @@ __device__ void plan_from_counts(const RouteArgs& a, const int* s_cnt, int* s_of
         v[q][0] = c;
         v[q][1] = gemv ? nch * ((I + kGemv1Rows - 1) / kGemv1Rows) : 0;
         v[q][2] = gemv ? nch * ((H + kGemv2Rows - 1) / kGemv2Rows) : 0;
-        v[q][3] = nt1 * ((I + 127) / 128);
+        v[q][3] = nt1 * ((I + a.gemm_m1 - 1) / a.gemm_m1);
         v[q][4] = nt2 * ((H + a.gemm_m2 - 1) / a.gemm_m2);
         v[q][5] = (g < G - 1 && c > 0) ? 1 : 0;
         v[q][6] = gemv ? 1 : 0;

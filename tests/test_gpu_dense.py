@@ -48,7 +48,7 @@ def run_dense(ws, x):
     return out.cpu().numpy()
 
 
-@pytest.mark.parametrize("T", [1, 2, 17, 100, 300])
+@pytest.mark.parametrize("T", [1, 2, 17, 100, 300, 1100])
 @pytest.mark.parametrize("xdt", ["bf16", "f32"])
 def test_dense_small_matches_oracle(T, xdt):
     need_gpu()
