@@ -376,7 +376,7 @@ def main():
             # rank 0's weight stream per second, and useful flops of the whole job
             "layer_hbm_gbs": layer_bytes * wl.layers / (ms / 1e3) / 1e9,
             "layer_tflops": layer_flops(shape, T_glob) * wl.layers / (ms / 1e3) / 1e12,
-            "phases_ms_per_step": {p: v[0] / args.steps for p, v in prof.items() if v[1]},
+            "phases_ms_per_step": {p: v[0] / args.steps for p, v in prof.items() if v[1] or v[0] > 0},
             "roofline": {"bound": "tensor" if tensor_bound else "hbm", "kernel": dom,
                          "achieved": achieved,
                          "peak": tflops_peak if tensor_bound else hbm,

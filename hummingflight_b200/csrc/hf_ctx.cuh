@@ -107,7 +107,7 @@ struct hf_moe_ctx {
     std::vector<cudaEvent_t> ev_pool;
     struct Mark { int phase; cudaEvent_t a, b; };
     std::vector<Mark> marks;
-    long long launches[HF_MOE_PHASES] = {0, 0, 0, 0, 0, 0, 0};
+    long long launches[HF_MOE_PHASES] = {};
 };
 
 namespace hf {

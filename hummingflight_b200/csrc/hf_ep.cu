@@ -133,10 +133,84 @@ static void build_plan(int W, int El, int T, bool has_shared, const int32_t* sen
         for (int t = 0; t < T; ++t) local_rows[base[El] + t] = p.R + t;
 }
 
+// ------------------------------------------------------------------ decode exchange kernels
+// Small batches (decode) exchange fixed-capacity slabs so that no size has to
+// reach the host: source s sends every destination `cap` rows (its rows for
+// that rank's experts first, the rest unused) plus the per-expert counts, in
+// one NCCL group; the receiver builds its plan from the counts on the device.
+
+// This rank's routed rows into per-destination slabs: the slot at canonical
+// position p (expert-major) goes to rank d = expert / El, slab row
+// p - offsets[d * El].
+__global__ void __launch_bounds__(256) k_ep_pack(const int32_t* perm, const int32_t* ids,
+                                                 const int32_t* offsets, const uint4* x,
+                                                 int row_vec, int n, int k, int El, int cap,
+                                                 uint4* slab) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int p = warp; p < n; p += nw) {
+        const int slot = perm[p];
+        const int d = ids[slot] / El;
+        const int r = p - offsets[d * El];
+        const uint4* src = x + size_t(slot / k) * row_vec;
+        uint4* dst = slab + (size_t(d) * cap + r) * row_vec;
+        for (int c = lane; c < row_vec; c += 32) dst[c] = ld_nc_u4(src + c);
+    }
+}
+
+// Receiver: expert outputs (local positions) back into per-source slabs in
+// the order the rows arrived.
+__global__ void __launch_bounds__(256) k_ep_unpack(const float4* y, const int32_t* row_pos,
+                                                   const int32_t* recv_tot, int W, int cap,
+                                                   int row_vec, float4* slab) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int idx = warp; idx < W * cap; idx += nw) {
+        const int s = idx / cap;
+        if (idx - s * cap >= recv_tot[s]) continue;
+        const float4* src = y + size_t(row_pos[idx]) * row_vec;
+        float4* dst = slab + size_t(idx) * row_vec;
+        for (int c = lane; c < row_vec; c += 32) dst[c] = src[c];
+    }
+}
+
+// Source: returned outputs to canonical positions; then the shared expert's
+// outputs from the last group of the local plan.
+__global__ void __launch_bounds__(256) k_ep_return(const int32_t* perm, const int32_t* ids,
+                                                   const int32_t* offsets, int n, int k, int El,
+                                                   int cap, const float4* slab, const float4* y_loc,
+                                                   const int32_t* loc_shared_off, int n_shared,
+                                                   int row_vec, float4* yrecv) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int p = warp; p < n + n_shared; p += nw) {
+        const float4* src;
+        if (p < n) {
+            const int slot = perm[p];
+            const int d = ids[slot] / El;
+            src = slab + (size_t(d) * cap + (p - offsets[d * El])) * row_vec;
+        } else {
+            src = y_loc + size_t(*loc_shared_off + (p - n)) * row_vec;
+        }
+        float4* dst = yrecv + size_t(p) * row_vec;
+        for (int c = lane; c < row_vec; c += 32) dst[c] = src[c];
+    }
+}
+
+static int copy_grid(int nsm, int rows) { return std::max(1, std::min(nsm * 8, (rows + 7) / 8)); }
+
+constexpr size_t kEpSlabBytes = size_t(64) << 20;  // largest fp32 slab set for the decode exchange
+
 // ------------------------------------------------------------------ state
 struct EpState {
     ncclComm_t comm = nullptr;
     size_t R_cap = 0;
+    int cap = 0;               // decode exchange: rows per source slab (0: not used)
+    char* xslab_send = nullptr;   // [W x cap] rows
+    char* xslab_recv = nullptr;   // [W x cap] received rows, then T_max local tokens
+    float* yslab_send = nullptr;  // [W x cap x H]
+    float* yslab_recv = nullptr;  // [W x cap x H]
+    int32_t* recv_tot = nullptr;  // [W]
     void* xsend = nullptr;     // [T_max*k x H] activation rows in canonical order
     void* xall = nullptr;      // [(R_cap + T_max) x H] received rows, then local tokens
     float* ysend = nullptr;    // [R_cap x H] expert outputs in arrival order
@@ -176,6 +250,18 @@ hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
     HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_perm), sizeof(int32_t) * (e->R_cap + T)));
     HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_rowpos), sizeof(int32_t) * e->R_cap));
     HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_loc), sizeof(int32_t) * (El + 1)));
+    // decode exchange slabs when they are small (each holds every row a source
+    // could send one rank: T_max tokens x min(k, El) slots)
+    const size_t cap = T * size_t(std::min(c->k, El));
+    if (size_t(W) * cap * c->H * 4 <= kEpSlabBytes) {
+        e->cap = int(cap);
+        const size_t row4 = size_t(c->H) * 4;  // fp32 activations are the widest rows
+        HF_TRY(dalloc(&e->xslab_send, size_t(W) * cap * row4));
+        HF_TRY(dalloc(&e->xslab_recv, (size_t(W) * cap + T) * row4));
+        HF_TRY(dalloc(&e->yslab_send, size_t(W) * cap * c->H));
+        HF_TRY(dalloc(&e->yslab_recv, size_t(W) * cap * c->H));
+        HF_TRY(dalloc(&e->recv_tot, size_t(W)));
+    }
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof(id));
     HF_NCCL(n.CommInitRank(&e->comm, W, id, c->rank));
@@ -186,7 +272,9 @@ void ep_destroy(hf_moe_ctx* c) {
     EpState* e = c->ep;
     if (!e) return;
     if (e->comm) nccl().CommDestroy(e->comm);
-    void* d[] = {e->xsend, e->xall, e->ysend, e->yrecv, e->cnt_recv, e->loc_counts, e->row_pos};
+    void* d[] = {e->xsend,      e->xall,       e->ysend,      e->yrecv,     e->cnt_recv,
+                 e->loc_counts, e->row_pos,    e->xslab_send, e->xslab_recv, e->yslab_send,
+                 e->yslab_recv, e->recv_tot};
     for (void* p : d) cudaFree(p);
     void* h[] = {e->h_src, e->h_recv, e->h_perm, e->h_rowpos, e->h_loc};
     for (void* p : h)
@@ -196,8 +284,113 @@ void ep_destroy(hf_moe_ctx* c) {
 }
 
 // ------------------------------------------------------------------ forward
-hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T, float* out,
-                     const hf_moe_routing* r, cudaStream_t st) {
+// Decode exchange: fixed-capacity slabs, counts and plan stay on the device.
+static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T,
+                                  float* out, const hf_moe_routing* r, cudaStream_t st) {
+    EpState& e = *c->ep;
+    NcclApi& n = nccl();
+    const int W = c->world, El = c->E_local, k = c->k, H = c->H, cap = e.cap;
+    const size_t rowb = size_t(H) * (xd == HF_F32 ? 4 : 2);
+    const bool has_shared = c->Is > 0;
+    const int rows = W * cap;
+
+    // 1. route the local tokens over all experts; rows into per-destination slabs
+    const RouteArgs ra = route_args(c, L, x, xd, T);
+    if (T > 0) {
+        HF_TRY(run_route(c, L, ra, st));
+        PhaseTimer p1(c, st, 1);
+        k_ep_pack<<<copy_grid(c->nsm, T * k), 256, 0, st>>>(
+            c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, static_cast<const uint4*>(x),
+            int(rowb / 16), T * k, k, El, cap, reinterpret_cast<uint4*>(e.xslab_send));
+        HF_CUDA(cudaGetLastError());
+        p1.done(1);
+    } else {
+        HF_CUDA(cudaMemsetAsync(c->plan_src + c->pl_src.counts, 0, sizeof(int32_t) * c->G_src, st));
+    }
+    // 2. counts and slabs to every rank in one group; local tokens after the slabs
+    const int32_t* cnt_src = c->plan_src + c->pl_src.counts;
+    PhaseTimer px(c, st, 7);
+    HF_NCCL(n.GroupStart());
+    for (int d = 0; d < W; ++d) {
+        HF_NCCL(n.Send(cnt_src + d * El, El, ncclInt32, d, e.comm, st));
+        HF_NCCL(n.Recv(e.cnt_recv + d * El, El, ncclInt32, d, e.comm, st));
+        HF_NCCL(n.Send(e.xslab_send + size_t(d) * cap * rowb, size_t(cap) * rowb, ncclChar, d,
+                       e.comm, st));
+        HF_NCCL(n.Recv(e.xslab_recv + size_t(d) * cap * rowb, size_t(cap) * rowb, ncclChar, d,
+                       e.comm, st));
+    }
+    HF_NCCL(n.GroupEnd());
+    if (T > 0)
+        HF_CUDA(cudaMemcpyAsync(e.xslab_recv + size_t(rows) * rowb, x, size_t(T) * rowb,
+                                cudaMemcpyDeviceToDevice, st));
+    px.done(0);
+
+    // 3. receiver plan on the device, then the local experts. Tiles and the
+    // GEMV threshold follow the whole job's batch (T x W tokens): each local
+    // expert sees about as many rows as it would on one GPU.
+    RouteArgs rl = ra;
+    rl.plan = c->plan;
+    rl.pl = c->pl;
+    set_gemm_tiles(c->gemm_bn, T * W, rl);
+    rl.gemv_max = gemv_threshold(c, T * W);
+    {
+        PhaseTimer pp(c, st, 1);
+        HF_TRY(launch_ep_plan(rl, e.cnt_recv, W, El, cap, T, c->perm, e.row_pos, e.recv_tot, st));
+        pp.done(1);
+    }
+    ExpertWork w{};
+    w.plan = c->plan;
+    w.pl = c->pl;
+    w.perm = c->perm;
+    w.x = e.xslab_recv;
+    w.x_f32 = xd == HF_F32;
+    w.T = rows + T;
+    w.k = 1;
+    w.y = c->y;
+    w.bn1 = rl.gemm_bn1;
+    w.bn2 = rl.gemm_bn2;
+    w.m1 = rl.gemm_m1;
+    w.m2 = rl.gemm_m2;
+    w.pair = rl.gemm_pair;
+    w.maybe_gemm = rl.gemm_ok && (c->cfg.path == HF_PATH_GEMM || rows + T > rl.gemv_max);
+    w.maybe_gemv = !rl.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
+                   (c->cfg.path == HF_PATH_AUTO && rl.gemv_max > 0);
+    HF_TRY(run_experts(c, L, w, st));
+
+    // 4. outputs back to their sources in arrival order, then to canonical positions
+    const int row4 = H / 4;
+    PhaseTimer py(c, st, 8);
+    k_ep_unpack<<<copy_grid(c->nsm, rows), 256, 0, st>>>(reinterpret_cast<const float4*>(c->y), e.row_pos,
+                                                 e.recv_tot, W, cap, row4,
+                                                 reinterpret_cast<float4*>(e.yslab_send));
+    HF_CUDA(cudaGetLastError());
+    HF_NCCL(n.GroupStart());
+    for (int d = 0; d < W; ++d) {
+        HF_NCCL(n.Send(e.yslab_send + size_t(d) * cap * H, size_t(cap) * H, ncclFloat32, d, e.comm,
+                       st));
+        HF_NCCL(n.Recv(e.yslab_recv + size_t(d) * cap * H, size_t(cap) * H, ncclFloat32, d, e.comm,
+                       st));
+    }
+    HF_NCCL(n.GroupEnd());
+    const int n_shared = has_shared ? T : 0;
+    if (T > 0) {
+        k_ep_return<<<copy_grid(c->nsm, T * k + n_shared), 256, 0, st>>>(
+            c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, T * k, k, El, cap,
+            reinterpret_cast<const float4*>(e.yslab_recv), reinterpret_cast<const float4*>(c->y),
+            c->plan + c->pl.offsets + El, n_shared, row4, reinterpret_cast<float4*>(e.yrecv));
+        HF_CUDA(cudaGetLastError());
+    }
+    py.done(T > 0 ? 2 : 1);
+    if (T > 0) {
+        // 5. combine in the reference order at the source
+        HF_TRY(run_combine(c, e.yrecv, T, out, r ? r->slot_out : nullptr, st));
+    }
+    return HF_OK;
+}
+
+// Large batches: per-forward counts sized on the host, exact-size exchange.
+static hf_status ep_forward_sized(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T,
+                                  float* out, const hf_moe_routing* r, cudaStream_t st) {
     EpState& e = *c->ep;
     NcclApi& n = nccl();
     const int W = c->world, El = c->E_local, k = c->k, H = c->H;
@@ -217,6 +410,7 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     }
     // 2. per-expert counts to every rank; read them back to size the exchange
     const int32_t* cnt_src = c->plan_src + c->pl_src.counts;
+    PhaseTimer px(c, st, 7);
     HF_NCCL(n.GroupStart());
     for (int d = 0; d < W; ++d) {
         HF_NCCL(n.Send(cnt_src + d * El, El, ncclInt32, d, e.comm, st));
@@ -259,15 +453,20 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     }
     HF_NCCL(n.GroupEnd());
     if (T > 0) HF_CUDA(cudaMemcpyAsync(xa + size_t(R) * rowb, x, size_t(T) * rowb, cudaMemcpyDeviceToDevice, st));
+    px.done(0);
 
     // 4. local experts over received rows, shared expert over local tokens
     RouteArgs rl = ra;
     rl.plan = c->plan;
     rl.pl = c->pl;
     rl.T = R + T;
-    set_gemm_tiles(c->gemm_bn, R + T, rl);
-    rl.gemv_max = gemv_threshold(c, R + T);
-    HF_TRY(launch_plan_from_counts(rl, e.loc_counts, st));
+    set_gemm_tiles(c->gemm_bn, T * W, rl);
+    rl.gemv_max = gemv_threshold(c, T * W);
+    {
+        PhaseTimer pp(c, st, 1);
+        HF_TRY(launch_plan_from_counts(rl, e.loc_counts, st));
+        pp.done(1);
+    }
     ExpertWork w{};
     w.plan = c->plan;
     w.pl = c->pl;
@@ -288,6 +487,7 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     if (npos > 0) HF_TRY(run_experts(c, L, w, st));
 
     // 5. outputs back to their sources, at canonical slot positions
+    PhaseTimer py(c, st, 8);
     if (R > 0) HF_TRY(launch_gather_rows(e.ysend, c->y, size_t(H) * 4, R, e.row_pos, 1, st));
     const size_t yrow = size_t(H) * 4;
     char* ys = reinterpret_cast<char*>(e.ysend);
@@ -303,9 +503,16 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     if (T > 0 && has_shared)
         HF_CUDA(cudaMemcpyAsync(yr + size_t(T) * k * yrow, c->y + size_t(R) * H, size_t(T) * yrow,
                                 cudaMemcpyDeviceToDevice, st));
+    py.done(R > 0 ? 1 : 0);
     // 6. combine in the reference order at the source
     if (T > 0) HF_TRY(run_combine(c, e.yrecv, T, out, r ? r->slot_out : nullptr, st));
     return HF_OK;
+}
+
+hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T, float* out,
+                     const hf_moe_routing* r, cudaStream_t st) {
+    if (c->ep->cap > 0) return ep_forward_slabs(c, L, x, xd, T, out, r, st);
+    return ep_forward_sized(c, L, x, xd, T, out, r, st);
 }
 
 }  // namespace hf

@@ -809,7 +809,7 @@ hf_status hf_moe_profile(hf_moe_ctx* ctx, int enable) {
 hf_status hf_moe_profile_read(hf_moe_ctx* ctx, double* phase_ms, long long* launches) {
     if (!ctx) return fail(HF_ERR_ARG, "hf_moe_profile_read: null context");
     DeviceGuard dg(ctx->cfg.device);
-    double ms[HF_MOE_PHASES] = {0, 0, 0, 0, 0, 0, 0};
+    double ms[HF_MOE_PHASES] = {};
     hf_status s = HF_OK;
     for (auto& m : ctx->marks) {
         float t = 0.f;

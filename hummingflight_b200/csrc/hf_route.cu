@@ -545,6 +545,68 @@ hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cud
     return HF_OK;
 }
 
+// Expert-parallel receiver plan from counts already on the device (the
+// decode exchange, no host round trip). Source s sent its rows for local
+// expert j (cnt[s * El + j] of them) in expert order at the start of its
+// slab of `cap` rows. Local positions are expert-major, then source, then
+// arrival -- the order the host plan of the large-batch exchange uses -- and
+// the shared expert's T_loc local tokens come last (rows W * cap + t). Also
+// writes row_pos (slab row -> local position) and recv_tot[s] (rows from s).
+__global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cnt, int W, int El,
+                                                  int cap, int T_loc, int32_t* perm,
+                                                  int32_t* row_pos, int32_t* recv_tot) {
+    extern __shared__ __align__(16) uint32_t sm[];
+    const int G = a.pl.G;  // El + 1
+    int* s_cnt = reinterpret_cast<int*>(sm);  // [G]
+    int* s_off = s_cnt + G;                   // [G + 1]
+    int* warp_tot = s_off + G + 1;            // [kPlanScratch]
+    int* s_src = warp_tot + kPlanScratch;     // [W x El] row of (s, j) inside s's slab
+    int* s_pos = s_src + W * El;              // [W x El] position of (s, j) inside expert j
+    for (int j = threadIdx.x; j < El; j += blockDim.x) {
+        int acc = 0;
+        for (int s = 0; s < W; ++s) {
+            s_pos[s * El + j] = acc;
+            acc += cnt[s * El + j];
+        }
+        s_cnt[j] = acc;
+    }
+    for (int s = threadIdx.x; s < W; s += blockDim.x) {
+        int acc = 0;
+        for (int j = 0; j < El; ++j) {
+            s_src[s * El + j] = acc;
+            acc += cnt[s * El + j];
+        }
+        recv_tot[s] = acc;
+    }
+    if (threadIdx.x == 0) s_cnt[El] = a.has_shared ? T_loc : 0;
+    __syncthreads();
+    plan_from_counts(a, s_cnt, s_off, warp_tot);  // ends with a barrier: s_off is complete
+    const int rows = W * cap;
+    for (int sj = threadIdx.x; sj < W * El; sj += blockDim.x) {
+        const int n = cnt[sj];
+        const int pos0 = s_off[sj % El] + s_pos[sj];
+        const int row0 = (sj / El) * cap + s_src[sj];
+        for (int i = 0; i < n; ++i) {
+            perm[pos0 + i] = row0 + i;  // slot id = row of [slabs | local tokens] (k = 1)
+            row_pos[row0 + i] = pos0 + i;
+        }
+    }
+    if (a.has_shared)  // slot ids past all rows name the local tokens (token_of_slot)
+        for (int t = threadIdx.x; t < T_loc; t += blockDim.x)
+            perm[s_off[El] + t] = (rows + T_loc) + (rows + t);
+}
+
+hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, int W, int El, int cap, int T_loc,
+                         int32_t* perm, int32_t* row_pos, int32_t* recv_tot, cudaStream_t st) {
+    const int G = a.pl.G;
+    if (G != El + 1 || G > 2 * 1024) return fail(HF_ERR_ARG, "expert-parallel plan: bad group count");
+    const size_t smem = sizeof(int) * (G + G + 1 + kPlanScratch + 2 * W * El);
+    HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_ep_plan), int(smem)));
+    k_ep_plan<<<1, 1024, smem, st>>>(a, cnt, W, El, cap, T_loc, perm, row_pos, recv_tot);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
 // Plan of a dense MLP pass: a single group (the shared-expert slot, G = 1)
 // holding all T tokens in order (perm = identity, slot id = token with k = 0).
 // Block 0 also writes the group's weight pointers and clears the error word.

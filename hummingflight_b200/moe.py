@@ -212,7 +212,7 @@ class MoELayer:
         return dict(active_experts=a.value, gemv_segments=b.value, gemm_segments=c.value)
 
     PHASES = ("router", "route", "gemv_gate_up", "gemv_down", "gemm_gate_up", "gemm_down",
-              "combine")
+              "combine", "ep_dispatch", "ep_return")
 
     def profile(self, enable: bool = True):
         call("hf_moe_profile", self._h, int(enable))

@@ -221,8 +221,10 @@ HF_API hf_status hf_moe_last_stats(hf_moe_ctx* ctx, int* active_experts, int* ge
  * reference, whose GPU timing is one event pair per expert,
  * cuda_backend.cpp:464-477). Phases: 0 router logits, 1 top-k + permutation
  * + plan, 2 GEMV gate/up, 3 GEMV down, 4 GEMM gate/up, 5 GEMM down,
- * 6 combine. Kernel launches are counted whether or not timing is on. */
-#define HF_MOE_PHASES 7
+ * 6 combine, 7 expert-parallel dispatch (counts + rows to their ranks), 8
+ * expert-parallel return (outputs back to their sources). Kernel launches
+ * (of this library) are counted whether or not timing is on. */
+#define HF_MOE_PHASES 9
 HF_API hf_status hf_moe_profile(hf_moe_ctx* ctx, int enable);
 /* Waits for the recorded work, writes each phase's milliseconds and kernel
  * launches since the previous read (either pointer may be NULL), then resets. */

@@ -33,7 +33,9 @@ def main():
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     cases = [("small_gemm", LayerShape(256, 16, 4, 128, 192, 2.5, True), 48, "gemm", 41),
              ("small_auto", LayerShape(256, 16, 4, 128, 192, 2.5, True), 40, "auto", 42),
-             ("glm_auto", GLM, 16, "auto", 0)]
+             ("glm_auto", GLM, 16, "auto", 0),
+             # slabs above the decode-exchange size: counts sized on the host
+             ("glm_sized", GLM, 256, "auto", 3)]
     results = {}
     for name, shape, t_local, path, wseed in cases:
         T = t_local * world
