@@ -630,6 +630,7 @@ hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid,
         if (a.bn == 16) return launch_one<2, 2, 16>(m, a, grid, st);
         if (a.bn == 128) return launch_one<2, 2, 128>(m, a, grid, st);
     } else if (a.mrows == 128) {
+        if (a.bn == 16) return launch_one<1, 2, 16>(m, a, grid, st);
         if (a.bn == 32) return launch_one<1, 2, 32>(m, a, grid, st);
         if (a.bn == 64) return launch_one<1, 2, 64>(m, a, grid, st);
         if (a.bn == 128) return launch_one<1, 2, 128>(m, a, grid, st);

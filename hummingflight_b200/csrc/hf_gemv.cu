@@ -15,6 +15,10 @@
 // (GEMV2) with 16-byte L1-bypassing loads, 8 loads in flight per lane, the
 // chunk's activations sitting in shared memory; fp32 accumulation, butterfly
 // shuffles, SwiGLU in the GEMV1 epilogue, mid kept fp32.
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "hf_internal.cuh"
 
 namespace hf {
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(256) k_gemv1(GemvArgs a) {
     void* xs = smem_raw;
     const int G = a.pl.G;
     const int H = a.H;
-    int32_t* sp = reinterpret_cast<int32_t*>(smem_raw + size_t(kGemvTE) * H * (XF32 ? 4 : 2));
+    int32_t* sp = reinterpret_cast<int32_t*>(smem_raw + size_t(a.te_cap) * H * (XF32 ? 4 : 2));
     stage_plan(sp, a.plan + a.pl.u1, a.plan, a.pl);
     __syncthreads();
     const int32_t* u1 = sp;
@@ -223,7 +227,7 @@ __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float* ms = reinterpret_cast<float*>(smem_raw);
     const int G = a.pl.G;
-    int32_t* sp = reinterpret_cast<int32_t*>(smem_raw + size_t(kGemvTE) * a.inter_max * 4);
+    int32_t* sp = reinterpret_cast<int32_t*>(smem_raw + size_t(a.te_cap) * a.inter_max * 4);
     stage_plan(sp, a.plan + a.pl.u2, a.plan, a.pl);
     __syncthreads();
     const int32_t* u2 = sp;
@@ -260,15 +264,15 @@ __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
     }
 }
 
-size_t gemv1_smem(int H, bool xf32, int G) {
-    return size_t(kGemvTE) * H * (xf32 ? 4 : 2) + plan_smem_bytes(G);
+size_t gemv1_smem(int H, bool xf32, int G, int te) {
+    return size_t(te) * H * (xf32 ? 4 : 2) + plan_smem_bytes(G);
 }
-size_t gemv2_smem(int inter_max, int G) {
-    return size_t(kGemvTE) * inter_max * 4 + plan_smem_bytes(G);
+size_t gemv2_smem(int inter_max, int G, int te) {
+    return size_t(te) * inter_max * 4 + plan_smem_bytes(G);
 }
 
 hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st) {
-    const size_t s1 = gemv1_smem(a.H, a.x_f32 != 0, a.pl.G);
+    const size_t s1 = gemv1_smem(a.H, a.x_f32 != 0, a.pl.G, a.te_cap);
     if (a.x_f32) {
         HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_gemv1<true>), (int)s1));
         k_gemv1<true><<<a.grid1, 256, s1, st>>>(a);
@@ -281,27 +285,38 @@ hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st) {
 }
 
 hf_status launch_gemv2(const GemvArgs& a, cudaStream_t st) {
-    const size_t s2 = gemv2_smem(a.inter_max, a.pl.G);
+    const size_t s2 = gemv2_smem(a.inter_max, a.pl.G, a.te_cap);
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_gemv2), (int)s2));
     k_gemv2<<<a.grid2, 256, s2, st>>>(a);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }
 
-int gemv_grid(int device, bool first, bool xf32, int H, int inter_max, int G) {
+// Persistent grid: SMs x resident blocks at the shared memory a launch with
+// chunks of up to `te` tokens stages (cached per shape).
+int gemv_grid(int device, bool first, bool xf32, int H, int inter_max, int G, int te) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, bool, bool, int, int, int, int>, int> cache;
+    const auto key = std::make_tuple(device, first, xf32, H, inter_max, G, te);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
     int per_sm = 1;
     if (first) {
-        const size_t s = gemv1_smem(H, xf32, G);
+        const size_t s = gemv1_smem(H, xf32, G, te);
         auto kern = xf32 ? k_gemv1<true> : k_gemv1<false>;
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s);
+        // raise-only (another launch may already need a larger opt-in)
+        ensure_smem(reinterpret_cast<const void*>(kern), (int)s);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, s);
     } else {
-        const size_t s = gemv2_smem(inter_max, G);
-        cudaFuncSetAttribute(k_gemv2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s);
+        const size_t s = gemv2_smem(inter_max, G, te);
+        ensure_smem(reinterpret_cast<const void*>(k_gemv2), (int)s);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv2, 256, s);
     }
     if (per_sm < 1) per_sm = 1;
-    return per_sm * num_sms(device);
+    const int grid = per_sm * num_sms(device);
+    cache.emplace(key, grid);
+    return grid;
 }
 
 // ============================================================ combine

@@ -235,13 +235,14 @@ struct GemvArgs {
     float* mid;             // [(T*k+T) x inter_max] fp32
     float* y;               // [(T*k+T) x H] fp32
     int grid1, grid2;
+    int te_cap;             // most tokens in one chunk: min(T, kGemvTE); sizes the staging
 };
 hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st);
 hf_status launch_gemv2(const GemvArgs& a, cudaStream_t st);
 // Persistent grid (SM count x resident blocks) of GEMV1 (first) or GEMV2.
-int gemv_grid(int device, bool first, bool xf32, int H, int inter_max, int G);
-size_t gemv1_smem(int H, bool xf32, int G);
-size_t gemv2_smem(int inter_max, int G);
+int gemv_grid(int device, bool first, bool xf32, int H, int inter_max, int G, int te = kGemvTE);
+size_t gemv1_smem(int H, bool xf32, int G, int te = kGemvTE);
+size_t gemv2_smem(int inter_max, int G, int te = kGemvTE);
 
 // tcgen05 grouped GEMM (hf_gemm.cu).
 struct GemmArgs {

@@ -236,8 +236,11 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
     ga.inter_max = c->inter_max;
     ga.mid = c->mid;
     ga.y = w.y;
-    ga.grid1 = w.x_f32 ? c->grid1_f32 : c->grid1_bf16;
-    ga.grid2 = c->grid2;
+    // chunks hold at most min(T, kGemvTE) tokens (a segment has at most T
+    // slots): stage that many rows, and fit more blocks per SM when T is small
+    ga.te_cap = std::max(1, std::min(w.k == 1 ? kGemvTE : w.T, kGemvTE));
+    ga.grid1 = gemv_grid(c->cfg.device, true, w.x_f32 != 0, c->H, c->inter_max, c->G, ga.te_cap);
+    ga.grid2 = gemv_grid(c->cfg.device, false, false, c->H, c->inter_max, c->G, ga.te_cap);
     const bool gemv_possible = w.maybe_gemv;
     if (gemv_possible) {
         PhaseTimer p2(c, st, 2);
