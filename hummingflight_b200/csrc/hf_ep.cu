@@ -32,6 +32,7 @@
 #include <numeric>
 
 #include "hf_ctx.cuh"
+#include "hf_sm100.cuh"
 
 namespace hf {
 
@@ -180,7 +181,14 @@ __global__ void __launch_bounds__(256) k_ep_return(const int32_t* perm, const in
                                                    const int32_t* offsets, int n, int k, int El,
                                                    int cap, const float4* slab, const float4* y_loc,
                                                    const int32_t* loc_shared_off, int n_shared,
-                                                   int row_vec, float4* yrecv) {
+                                                   int row_vec, float4* yrecv,
+                                                   const unsigned long long* flags, int W,
+                                                   unsigned long long seq,
+                                                   unsigned long long timeout_ns, int* err) {
+    if (flags) {  // peer-memory exchange: every rank's outputs are in the slabs
+        if (threadIdx.x == 0) sm100::wait_flags_sys(flags, W, seq, timeout_ns, err);
+        __syncthreads();
+    }
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int nw = (gridDim.x * blockDim.x) >> 5;
     for (int p = warp; p < n + n_shared; p += nw) {
@@ -201,6 +209,86 @@ static int copy_grid(int nsm, int rows) { return std::max(1, std::min(nsm * 8, (
 
 constexpr size_t kEpSlabBytes = size_t(64) << 20;  // largest fp32 slab set for the decode exchange
 
+// ---- decode exchange over peer memory (NVLink): the same slabs, written by
+// the producing kernels straight into the other GPUs' buffers (CUDA IPC
+// mappings), with a per-forward sequence number as the arrival flag.
+constexpr int kEpMaxRanks = 16;
+struct PeerPtrs {                              // rank d's buffers, as mapped here
+    char* x[kEpMaxRanks];                      // xslab_recv
+    float* y[kEpMaxRanks];                     // yslab_recv
+    int32_t* cnt[kEpMaxRanks];                 // cnt_recv
+    unsigned long long* flags[kEpMaxRanks];    // [2W]: rows from s arrived / outputs from s
+};
+
+// The block that finishes last (device counter, reset by it) runs `tail`;
+// every block fences its stores system-wide before counting itself in.
+template <typename F>
+__device__ __forceinline__ void ep_last_block(int* done, F tail) {
+    __shared__ int s_last;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(done, 1) == int(gridDim.x) - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence_system();
+    tail();
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) *done = 0;
+}
+
+// Rows into the destinations' slabs (at this rank's slab) in peer memory;
+// then counts, then flags[d][rank] = seq on every rank.
+__global__ void __launch_bounds__(256) k_ep_pack_p2p(const int32_t* perm, const int32_t* ids,
+                                                     const int32_t* offsets, const uint4* x,
+                                                     int row_vec, int n, int k, int El, int cap,
+                                                     int rank, int W, const int32_t* cnt_src,
+                                                     PeerPtrs pp, int* done,
+                                                     unsigned long long seq) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int p = warp; p < n; p += nw) {
+        const int slot = perm[p];
+        const int d = ids[slot] / El;
+        const int r = p - offsets[d * El];
+        const uint4* src = x + size_t(slot / k) * row_vec;
+        uint4* dst = reinterpret_cast<uint4*>(pp.x[d]) + (size_t(rank) * cap + r) * row_vec;
+        for (int c = lane; c < row_vec; c += 32) dst[c] = ld_nc_u4(src + c);
+    }
+    ep_last_block(done, [&] {
+        for (int i = threadIdx.x; i < W * El; i += blockDim.x)
+            pp.cnt[i / El][rank * El + i % El] = cnt_src[i];
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x < W) sm100::st_release_sys(pp.flags[threadIdx.x] + rank, seq);
+    });
+}
+
+// Receiver: outputs back into each source's slab (at this rank's slab) in
+// peer memory; then flags[s][W + rank] = seq.
+__global__ void __launch_bounds__(256) k_ep_unpack_p2p(const float4* y, const int32_t* row_pos,
+                                                       const int32_t* recv_tot, int W, int cap,
+                                                       int row_vec, int rank, PeerPtrs pp,
+                                                       int* done, unsigned long long seq) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int idx = warp; idx < W * cap; idx += nw) {
+        const int s = idx / cap, i = idx - s * cap;
+        if (i >= recv_tot[s]) continue;
+        const float4* src = y + size_t(row_pos[idx]) * row_vec;
+        float4* dst = reinterpret_cast<float4*>(pp.y[s]) + (size_t(rank) * cap + i) * row_vec;
+        for (int c = lane; c < row_vec; c += 32) dst[c] = src[c];
+    }
+    ep_last_block(done, [&] {
+        if (threadIdx.x < W) sm100::st_release_sys(pp.flags[threadIdx.x] + W + rank, seq);
+    });
+}
+
+__global__ void k_ep_wait(const unsigned long long* flags, int n, unsigned long long seq,
+                          unsigned long long timeout_ns, int* err) {
+    if (threadIdx.x == 0) sm100::wait_flags_sys(flags, n, seq, timeout_ns, err);
+}
+
 // ------------------------------------------------------------------ state
 struct EpState {
     ncclComm_t comm = nullptr;
@@ -211,6 +299,12 @@ struct EpState {
     float* yslab_send = nullptr;  // [W x cap x H]
     float* yslab_recv = nullptr;  // [W x cap x H]
     int32_t* recv_tot = nullptr;  // [W]
+    // peer-memory exchange (decode): this rank's flags and the peers' mappings
+    bool p2p = false;
+    unsigned long long* flags = nullptr;  // [2W], this rank's arrival flags
+    unsigned long long seq = 0;           // forwards exchanged so far
+    PeerPtrs peers{};
+    std::vector<void*> opened;            // IPC mappings to close
     void* xsend = nullptr;     // [T_max*k x H] activation rows in canonical order
     void* xall = nullptr;      // [(R_cap + T_max) x H] received rows, then local tokens
     float* ysend = nullptr;    // [R_cap x H] expert outputs in arrival order
@@ -228,6 +322,60 @@ struct EpState {
 size_t ep_recv_cap(const hf_moe_ctx* c) {
     const size_t T = size_t(std::max(1, c->cfg.max_tokens));
     return size_t(c->world) * T * size_t(std::min(c->k, c->E_local));
+}
+
+// Maps every rank's slab receive buffers, counts and flags into this process
+// (CUDA IPC handles gathered over the communicator). Any failure leaves the
+// NCCL slab exchange in place.
+static hf_status setup_p2p(hf_moe_ctx* c) {
+    EpState& e = *c->ep;
+    NcclApi& n = nccl();
+    const int W = c->world, me = c->rank;
+    if (W > kEpMaxRanks) return fail(HF_ERR_ARG, "peer-memory exchange: too many ranks");
+    HF_TRY(dalloc(&e.flags, size_t(2) * W));
+    HF_CUDA(cudaMemset(e.flags, 0, sizeof(unsigned long long) * 2 * W));
+    constexpr int kBufs = 4;
+    void* mine_ptr[kBufs] = {e.xslab_recv, e.yslab_recv, e.cnt_recv, e.flags};
+    cudaIpcMemHandle_t mine[kBufs];
+    for (int i = 0; i < kBufs; ++i) HF_CUDA(cudaIpcGetMemHandle(&mine[i], mine_ptr[i]));
+    const size_t hb = sizeof(mine);
+    char* dev = nullptr;
+    HF_TRY(dalloc(&dev, size_t(W) * hb));
+    cudaStream_t st = nullptr;
+    hf_status s = HF_OK;
+    std::vector<cudaIpcMemHandle_t> all(size_t(W) * kBufs);
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMemcpy(dev + size_t(me) * hb, mine, hb, cudaMemcpyHostToDevice) != cudaSuccess) {
+        s = fail(HF_ERR_CUDA, "peer-memory exchange: handle staging failed");
+    } else {
+        n.GroupStart();
+        for (int d = 0; d < W; ++d) {
+            if (d == me) continue;
+            n.Send(dev + size_t(me) * hb, hb, ncclChar, d, e.comm, st);
+            n.Recv(dev + size_t(d) * hb, hb, ncclChar, d, e.comm, st);
+        }
+        if (n.GroupEnd() != ncclSuccess || cudaStreamSynchronize(st) != cudaSuccess ||
+            cudaMemcpy(all.data(), dev, size_t(W) * hb, cudaMemcpyDeviceToHost) != cudaSuccess)
+            s = fail(HF_ERR_NCCL, "peer-memory exchange: handle exchange failed");
+    }
+    if (st) cudaStreamDestroy(st);
+    cudaFree(dev);
+    HF_TRY(s);
+    for (int d = 0; d < W; ++d) {
+        void* p[kBufs] = {mine_ptr[0], mine_ptr[1], mine_ptr[2], mine_ptr[3]};
+        if (d != me)
+            for (int i = 0; i < kBufs; ++i) {
+                HF_CUDA(cudaIpcOpenMemHandle(&p[i], all[size_t(d) * kBufs + i],
+                                             cudaIpcMemLazyEnablePeerAccess));
+                e.opened.push_back(p[i]);
+            }
+        e.peers.x[d] = static_cast<char*>(p[0]);
+        e.peers.y[d] = static_cast<float*>(p[1]);
+        e.peers.cnt[d] = static_cast<int32_t*>(p[2]);
+        e.peers.flags[d] = static_cast<unsigned long long*>(p[3]);
+    }
+    e.p2p = true;
+    return HF_OK;
 }
 
 hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
@@ -265,16 +413,23 @@ hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof(id));
     HF_NCCL(n.CommInitRank(&e->comm, W, id, c->rank));
+    if (e->cap > 0 && !std::getenv("HF_EP_NCCL_ONLY") && setup_p2p(c) != HF_OK) {
+        cudaGetLastError();  // keep the NCCL slab exchange
+        for (void* p : e->opened) cudaIpcCloseMemHandle(p);
+        e->opened.clear();
+        e->p2p = false;
+    }
     return HF_OK;
 }
 
 void ep_destroy(hf_moe_ctx* c) {
     EpState* e = c->ep;
     if (!e) return;
+    for (void* p : e->opened) cudaIpcCloseMemHandle(p);
     if (e->comm) nccl().CommDestroy(e->comm);
     void* d[] = {e->xsend,      e->xall,       e->ysend,      e->yrecv,     e->cnt_recv,
                  e->loc_counts, e->row_pos,    e->xslab_send, e->xslab_recv, e->yslab_send,
-                 e->yslab_recv, e->recv_tot};
+                 e->yslab_recv, e->recv_tot, e->flags};
     for (void* p : d) cudaFree(p);
     void* h[] = {e->h_src, e->h_recv, e->h_perm, e->h_rowpos, e->h_loc};
     for (void* p : h)
@@ -294,36 +449,54 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     const bool has_shared = c->Is > 0;
     const int rows = W * cap;
 
+    // every forward on every rank takes the next sequence number (peer memory)
+    const unsigned long long seq = e.p2p ? ++e.seq : 0;
+    int* err = c->plan + c->pl.stats + 3;
+
     // 1. route the local tokens over all experts; rows into per-destination slabs
     const RouteArgs ra = route_args(c, L, x, xd, T);
     if (T > 0) {
         HF_TRY(run_route(c, L, ra, st));
-        PhaseTimer p1(c, st, 1);
-        k_ep_pack<<<copy_grid(c->nsm, T * k), 256, 0, st>>>(
-            c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, static_cast<const uint4*>(x),
-            int(rowb / 16), T * k, k, El, cap, reinterpret_cast<uint4*>(e.xslab_send));
-        HF_CUDA(cudaGetLastError());
-        p1.done(1);
     } else {
         HF_CUDA(cudaMemsetAsync(c->plan_src + c->pl_src.counts, 0, sizeof(int32_t) * c->G_src, st));
     }
-    // 2. counts and slabs to every rank in one group; local tokens after the slabs
     const int32_t* cnt_src = c->plan_src + c->pl_src.counts;
-    PhaseTimer px(c, st, 7);
-    HF_NCCL(n.GroupStart());
-    for (int d = 0; d < W; ++d) {
-        HF_NCCL(n.Send(cnt_src + d * El, El, ncclInt32, d, e.comm, st));
-        HF_NCCL(n.Recv(e.cnt_recv + d * El, El, ncclInt32, d, e.comm, st));
-        HF_NCCL(n.Send(e.xslab_send + size_t(d) * cap * rowb, size_t(cap) * rowb, ncclChar, d,
-                       e.comm, st));
-        HF_NCCL(n.Recv(e.xslab_recv + size_t(d) * cap * rowb, size_t(cap) * rowb, ncclChar, d,
-                       e.comm, st));
+    if (e.p2p) {
+        // 2. rows straight into the destinations' slabs over NVLink, then the
+        // counts and this rank's arrival flag on every rank (even with T = 0)
+        PhaseTimer px(c, st, 7);
+        k_ep_pack_p2p<<<copy_grid(c->nsm, std::max(1, T * k)), 256, 0, st>>>(
+            c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, static_cast<const uint4*>(x),
+            int(rowb / 16), T * k, k, El, cap, c->rank, W, cnt_src, e.peers, c->sched + 6, seq);
+        HF_CUDA(cudaGetLastError());
+        px.done(1);
+    } else {
+        if (T > 0) {
+            PhaseTimer p1(c, st, 1);
+            k_ep_pack<<<copy_grid(c->nsm, T * k), 256, 0, st>>>(
+                c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, static_cast<const uint4*>(x),
+                int(rowb / 16), T * k, k, El, cap, reinterpret_cast<uint4*>(e.xslab_send));
+            HF_CUDA(cudaGetLastError());
+            p1.done(1);
+        }
+        // 2. counts and slabs to every rank in one NCCL group
+        PhaseTimer px(c, st, 7);
+        HF_NCCL(n.GroupStart());
+        for (int d = 0; d < W; ++d) {
+            HF_NCCL(n.Send(cnt_src + d * El, El, ncclInt32, d, e.comm, st));
+            HF_NCCL(n.Recv(e.cnt_recv + d * El, El, ncclInt32, d, e.comm, st));
+            HF_NCCL(n.Send(e.xslab_send + size_t(d) * cap * rowb, size_t(cap) * rowb, ncclChar, d,
+                           e.comm, st));
+            HF_NCCL(n.Recv(e.xslab_recv + size_t(d) * cap * rowb, size_t(cap) * rowb, ncclChar, d,
+                           e.comm, st));
+        }
+        HF_NCCL(n.GroupEnd());
+        px.done(0);
     }
-    HF_NCCL(n.GroupEnd());
+    // local tokens after the slabs
     if (T > 0)
         HF_CUDA(cudaMemcpyAsync(e.xslab_recv + size_t(rows) * rowb, x, size_t(T) * rowb,
                                 cudaMemcpyDeviceToDevice, st));
-    px.done(0);
 
     // 3. receiver plan on the device, then the local experts. Tiles and the
     // GEMV threshold follow the whole job's batch (T x W tokens): each local
@@ -335,7 +508,8 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     rl.gemv_max = gemv_threshold(c, T * W);
     {
         PhaseTimer pp(c, st, 1);
-        HF_TRY(launch_ep_plan(rl, e.cnt_recv, W, El, cap, T, c->perm, e.row_pos, e.recv_tot, st));
+        HF_TRY(launch_ep_plan(rl, e.cnt_recv, W, El, cap, T, c->perm, e.row_pos, e.recv_tot,
+                              e.p2p ? e.flags : nullptr, seq, c->timeout_ns, err, st));
         pp.done(1);
     }
     ExpertWork w{};
@@ -359,32 +533,42 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
 
     // 4. outputs back to their sources in arrival order, then to canonical positions
     const int row4 = H / 4;
-    PhaseTimer py(c, st, 8);
-    k_ep_unpack<<<copy_grid(c->nsm, rows), 256, 0, st>>>(reinterpret_cast<const float4*>(c->y), e.row_pos,
-                                                 e.recv_tot, W, cap, row4,
-                                                 reinterpret_cast<float4*>(e.yslab_send));
-    HF_CUDA(cudaGetLastError());
-    HF_NCCL(n.GroupStart());
-    for (int d = 0; d < W; ++d) {
-        HF_NCCL(n.Send(e.yslab_send + size_t(d) * cap * H, size_t(cap) * H, ncclFloat32, d, e.comm,
-                       st));
-        HF_NCCL(n.Recv(e.yslab_recv + size_t(d) * cap * H, size_t(cap) * H, ncclFloat32, d, e.comm,
-                       st));
-    }
-    HF_NCCL(n.GroupEnd());
     const int n_shared = has_shared ? T : 0;
+    PhaseTimer py(c, st, 8);
+    if (e.p2p) {
+        k_ep_unpack_p2p<<<copy_grid(c->nsm, rows), 256, 0, st>>>(
+            reinterpret_cast<const float4*>(c->y), e.row_pos, e.recv_tot, W, cap, row4, c->rank,
+            e.peers, c->sched + 7, seq);
+        HF_CUDA(cudaGetLastError());
+        if (T == 0) {  // no outputs to collect, but every rank waits for every rank
+            k_ep_wait<<<1, 32, 0, st>>>(e.flags + W, W, seq, c->timeout_ns, err);
+            HF_CUDA(cudaGetLastError());
+        }
+    } else {
+        k_ep_unpack<<<copy_grid(c->nsm, rows), 256, 0, st>>>(
+            reinterpret_cast<const float4*>(c->y), e.row_pos, e.recv_tot, W, cap, row4,
+            reinterpret_cast<float4*>(e.yslab_send));
+        HF_CUDA(cudaGetLastError());
+        HF_NCCL(n.GroupStart());
+        for (int d = 0; d < W; ++d) {
+            HF_NCCL(n.Send(e.yslab_send + size_t(d) * cap * H, size_t(cap) * H, ncclFloat32, d,
+                           e.comm, st));
+            HF_NCCL(n.Recv(e.yslab_recv + size_t(d) * cap * H, size_t(cap) * H, ncclFloat32, d,
+                           e.comm, st));
+        }
+        HF_NCCL(n.GroupEnd());
+    }
     if (T > 0) {
         k_ep_return<<<copy_grid(c->nsm, T * k + n_shared), 256, 0, st>>>(
             c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, T * k, k, El, cap,
             reinterpret_cast<const float4*>(e.yslab_recv), reinterpret_cast<const float4*>(c->y),
-            c->plan + c->pl.offsets + El, n_shared, row4, reinterpret_cast<float4*>(e.yrecv));
+            c->plan + c->pl.offsets + El, n_shared, row4, reinterpret_cast<float4*>(e.yrecv),
+            e.p2p ? e.flags + W : nullptr, W, seq, c->timeout_ns, err);
         HF_CUDA(cudaGetLastError());
     }
     py.done(T > 0 ? 2 : 1);
-    if (T > 0) {
-        // 5. combine in the reference order at the source
-        HF_TRY(run_combine(c, e.yrecv, T, out, r ? r->slot_out : nullptr, st));
-    }
+    // 5. combine in the reference order at the source
+    if (T > 0) HF_TRY(run_combine(c, e.yrecv, T, out, r ? r->slot_out : nullptr, st));
     return HF_OK;
 }
 

@@ -208,9 +208,12 @@ void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra);
 // already in device memory (expert-parallel receivers, dense MLP).
 hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cudaStream_t st);
 // Expert-parallel receiver plan from device counts (fixed-capacity slabs of
-// `cap` rows per source); see k_ep_plan.
+// `cap` rows per source); see k_ep_plan. With `flags` it first waits (bounded)
+// for every source's arrival flag to reach `seq` (peer-memory exchange).
 hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, int W, int El, int cap, int T_loc,
-                         int32_t* perm, int32_t* row_pos, int32_t* recv_tot, cudaStream_t st);
+                         int32_t* perm, int32_t* row_pos, int32_t* recv_tot,
+                         const unsigned long long* flags, unsigned long long seq,
+                         unsigned long long timeout_ns, int* err, cudaStream_t st);
 // Dense MLP pass: one group of all T tokens in order; writes groups[0] = w.
 hf_status launch_dense_plan(const RouteArgs& a, const GroupW& w, GroupW* groups, int32_t* perm,
                             int* sched, cudaStream_t st);

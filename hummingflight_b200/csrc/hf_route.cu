@@ -11,6 +11,7 @@
 // popcount of the mask bits below its token, so the result is deterministic
 // without sorting.
 #include "hf_internal.cuh"
+#include "hf_sm100.cuh"
 
 #include <math.h>
 
@@ -554,8 +555,17 @@ hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cud
 // writes row_pos (slab row -> local position) and recv_tot[s] (rows from s).
 __global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cnt, int W, int El,
                                                   int cap, int T_loc, int32_t* perm,
-                                                  int32_t* row_pos, int32_t* recv_tot) {
+                                                  int32_t* row_pos, int32_t* recv_tot,
+                                                  const unsigned long long* flags,
+                                                  unsigned long long seq,
+                                                  unsigned long long timeout_ns, int* err) {
     extern __shared__ __align__(16) uint32_t sm[];
+    // peer-memory exchange: counts and rows are in place once every source's
+    // flag shows this forward's sequence number
+    if (flags) {
+        if (threadIdx.x == 0) sm100::wait_flags_sys(flags, W, seq, timeout_ns, err);
+        __syncthreads();
+    }
     const int G = a.pl.G;  // El + 1
     int* s_cnt = reinterpret_cast<int*>(sm);  // [G]
     int* s_off = s_cnt + G;                   // [G + 1]
@@ -597,12 +607,15 @@ __global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cn
 }
 
 hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, int W, int El, int cap, int T_loc,
-                         int32_t* perm, int32_t* row_pos, int32_t* recv_tot, cudaStream_t st) {
+                         int32_t* perm, int32_t* row_pos, int32_t* recv_tot,
+                         const unsigned long long* flags, unsigned long long seq,
+                         unsigned long long timeout_ns, int* err, cudaStream_t st) {
     const int G = a.pl.G;
     if (G != El + 1 || G > 2 * 1024) return fail(HF_ERR_ARG, "expert-parallel plan: bad group count");
     const size_t smem = sizeof(int) * (G + G + 1 + kPlanScratch + 2 * W * El);
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_ep_plan), int(smem)));
-    k_ep_plan<<<1, 1024, smem, st>>>(a, cnt, W, El, cap, T_loc, perm, row_pos, recv_tot);
+    k_ep_plan<<<1, 1024, smem, st>>>(a, cnt, W, El, cap, T_loc, perm, row_pos, recv_tot, flags, seq,
+                                     timeout_ns, err);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }

@@ -284,5 +284,31 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// ------------------------------------------------------------------ flags across GPUs
+// A producer on one GPU publishes data in another GPU's memory (peer stores
+// over NVLink), fences system-wide and stores a sequence number with release
+// semantics; the consumer loads it with acquire semantics.
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Waits (bounded) until flags[0..n) have all reached seq; on timeout sets bit
+// 2 of the error word and gives up (that forward's outputs are invalid).
+__device__ __forceinline__ void wait_flags_sys(const unsigned long long* flags, int n,
+                                               unsigned long long seq, unsigned long long timeout_ns,
+                                               int* err) {
+    const uint64_t dl = globaltimer() + timeout_ns;
+    for (int i = 0; i < n; ++i)
+        while (ld_acquire_sys(flags + i) < seq)
+            if (globaltimer() > dl) {
+                atomicOr(err, 2);
+                return;
+            }
+}
+
 }  // namespace sm100
 }  // namespace hf
