@@ -335,8 +335,8 @@ def main():
 
     if rank == 0:
         hbm, tflops_peak, peak_kind = peaks()
-        # the library's AUTO rule: single-token segments on the GEMV in passes of <= 16 rows
-        gemv_max = args.gemv_max or (1 if T <= 16 else 0)
+        # the library's AUTO rule: the GEMV only for a single token
+        gemv_max = args.gemv_max or (1 if T <= 1 else 0)
         pb = phase_bytes(shape, counts, T, L.k, args.path, gemv_max)
         dom = max(("gemv_gate_up", "gemv_down", "router", "route", "combine",
                    "gemm_gate_up", "gemm_down"), key=lambda p: prof[p][0])

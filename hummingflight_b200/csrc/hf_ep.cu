@@ -207,7 +207,8 @@ __global__ void __launch_bounds__(256) k_ep_return(const int32_t* perm, const in
 
 static int copy_grid(int nsm, int rows) { return std::max(1, std::min(nsm * 8, (rows + 7) / 8)); }
 
-constexpr size_t kEpSlabBytes = size_t(64) << 20;  // largest fp32 slab set for the decode exchange
+constexpr size_t kEpSlabBytes = size_t(64) << 20;     // largest slab set sent whole over NCCL
+constexpr size_t kEpP2PSlabBytes = size_t(8) << 30;   // largest slab set reserved for peer stores
 
 // ---- decode exchange over peer memory (NVLink): the same slabs, written by
 // the producing kernels straight into the other GPUs' buffers (CUDA IPC
@@ -386,38 +387,56 @@ hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
     const size_t T = size_t(std::max(1, c->T_max));
     e->R_cap = ep_recv_cap(c);
     const int W = c->world, El = c->E_local;
-    HF_TRY(dalloc(reinterpret_cast<float**>(&e->xsend), T * c->k * c->H));
-    HF_TRY(dalloc(reinterpret_cast<float**>(&e->xall), (e->R_cap + T) * c->H));
-    HF_TRY(dalloc(&e->ysend, e->R_cap * c->H));
     HF_TRY(dalloc(&e->yrecv, (T * c->k + T) * c->H));
     HF_TRY(dalloc(&e->cnt_recv, size_t(W) * El));
-    HF_TRY(dalloc(&e->loc_counts, size_t(El) + 1));
     HF_TRY(dalloc(&e->row_pos, e->R_cap));
-    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_src), sizeof(int32_t) * (c->E + 1)));
-    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_recv), sizeof(int32_t) * W * El));
-    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_perm), sizeof(int32_t) * (e->R_cap + T)));
-    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_rowpos), sizeof(int32_t) * e->R_cap));
-    HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_loc), sizeof(int32_t) * (El + 1)));
-    // decode exchange slabs when they are small (each holds every row a source
-    // could send one rank: T_max tokens x min(k, El) slots)
-    const size_t cap = T * size_t(std::min(c->k, El));
-    if (size_t(W) * cap * c->H * 4 <= kEpSlabBytes) {
-        e->cap = int(cap);
-        const size_t row4 = size_t(c->H) * 4;  // fp32 activations are the widest rows
-        HF_TRY(dalloc(&e->xslab_send, size_t(W) * cap * row4));
-        HF_TRY(dalloc(&e->xslab_recv, (size_t(W) * cap + T) * row4));
-        HF_TRY(dalloc(&e->yslab_send, size_t(W) * cap * c->H));
-        HF_TRY(dalloc(&e->yslab_recv, size_t(W) * cap * c->H));
-        HF_TRY(dalloc(&e->recv_tot, size_t(W)));
-    }
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof(id));
     HF_NCCL(n.CommInitRank(&e->comm, W, id, c->rank));
-    if (e->cap > 0 && !std::getenv("HF_EP_NCCL_ONLY") && setup_p2p(c) != HF_OK) {
-        cudaGetLastError();  // keep the NCCL slab exchange
+
+    // Slabs: every rank reserves, per source, room for every row that source
+    // could send it (T_max tokens x min(k, El) slots). Over peer memory only
+    // the rows that exist cross NVLink, so the slabs are used whenever they
+    // fit kEpP2PSlabBytes; over NCCL the whole slab travels, so only while
+    // small (kEpSlabBytes). Otherwise the exchange is sized on the host.
+    const size_t cap = T * size_t(std::min(c->k, El));
+    const size_t row4 = size_t(c->H) * 4;  // fp32 activations are the widest rows
+    const size_t slab_bytes = size_t(W) * cap * row4;
+    const bool try_p2p = !std::getenv("HF_EP_NCCL_ONLY") && W <= kEpMaxRanks &&
+                         slab_bytes <= kEpP2PSlabBytes;
+    if (try_p2p || slab_bytes <= kEpSlabBytes) {
+        HF_TRY(dalloc(&e->xslab_recv, (size_t(W) * cap + T) * row4));
+        HF_TRY(dalloc(&e->yslab_recv, size_t(W) * cap * c->H));
+        HF_TRY(dalloc(&e->recv_tot, size_t(W)));
+    }
+    if (try_p2p && setup_p2p(c) != HF_OK) {
+        cudaGetLastError();  // no peer mappings: the NCCL exchanges below
         for (void* p : e->opened) cudaIpcCloseMemHandle(p);
         e->opened.clear();
         e->p2p = false;
+    }
+    if (e->p2p) {
+        e->cap = int(cap);
+    } else if (slab_bytes <= kEpSlabBytes) {
+        e->cap = int(cap);
+        HF_TRY(dalloc(&e->xslab_send, size_t(W) * cap * row4));
+        HF_TRY(dalloc(&e->yslab_send, size_t(W) * cap * c->H));
+    } else {
+        cudaFree(e->xslab_recv);
+        cudaFree(e->yslab_recv);
+        e->xslab_recv = nullptr;
+        e->yslab_recv = nullptr;
+    }
+    if (e->cap == 0) {  // host-sized exchange
+        HF_TRY(dalloc(reinterpret_cast<float**>(&e->xsend), T * c->k * c->H));
+        HF_TRY(dalloc(reinterpret_cast<float**>(&e->xall), (e->R_cap + T) * c->H));
+        HF_TRY(dalloc(&e->ysend, e->R_cap * c->H));
+        HF_TRY(dalloc(&e->loc_counts, size_t(El) + 1));
+        HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_src), sizeof(int32_t) * (c->E + 1)));
+        HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_recv), sizeof(int32_t) * W * El));
+        HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_perm), sizeof(int32_t) * (e->R_cap + T)));
+        HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_rowpos), sizeof(int32_t) * e->R_cap));
+        HF_CUDA(cudaMallocHost(reinterpret_cast<void**>(&e->h_loc), sizeof(int32_t) * (El + 1)));
     }
     return HF_OK;
 }
@@ -439,7 +458,8 @@ void ep_destroy(hf_moe_ctx* c) {
 }
 
 // ------------------------------------------------------------------ forward
-// Decode exchange: fixed-capacity slabs, counts and plan stay on the device.
+// Slab exchange (peer memory at any size, NCCL for small batches): fixed
+// per-source regions, counts and plan stay on the device.
 static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T,
                                   float* out, const hf_moe_routing* r, cudaStream_t st) {
     EpState& e = *c->ep;

@@ -37,11 +37,13 @@ constexpr int kSmallRouteT = 128;  // single-CTA routing up to this many tokens
 constexpr int kGemvTE = 4;         // tokens per grouped-GEMV chunk
 constexpr int kGemv1Rows = 16;     // gate/up rows per GEMV1 unit (8 warps x 2)
 constexpr int kGemv2Rows = 32;     // down rows per GEMV2 unit (8 warps x 4)
-// AUTO with gemv_max_tokens = 0: in passes of up to kGemvAutoBatch rows,
-// single-token segments take the GEMV; larger passes run every segment on the
-// tcgen05 GEMM (measured faster from 64 rows: its weight stream runs at the
-// copy rate, the GEMV pair at 75-88% of it).
-constexpr int kGemvAutoBatch = 16;
+// AUTO with gemv_max_tokens = 0: a single token runs on the GEMV; every
+// larger pass runs every segment on the tcgen05 GEMM, whose weight stream runs
+// at the copy rate (the GEMV pair at 75-88 % of it). Measured on the GLM
+// layer: 1 token GEMV 0.169 vs GEMM 0.197 ms; 2 / 4 / 8 / 16 tokens GEMM
+// 0.29 / 0.48 / 0.70 / 1.04 ms vs single-token segments on the GEMV 0.37 /
+// 0.55 / 0.78 / 1.09 ms.
+constexpr int kGemvAutoBatch = 1;
 constexpr int kGemvAutoMax = 1;
 
 // Weights of one expert group (routed expert or the shared expert).

@@ -76,7 +76,7 @@ typedef struct hf_moe_config {
     int device;                    /* CUDA device ordinal                          */
     int path;                      /* hf_path                                      */
     int gemv_max_tokens;           /* AUTO: segments up to this use the GEMV; 0 = by pass
-                                      size (single-token segments of passes of <= 16 rows) */
+                                      size (the GEMV for single-token passes only) */
     /* expert parallelism (experts [r*E/W, (r+1)*E/W) on rank r); W=1: none */
     int ep_rank;
     int ep_world;

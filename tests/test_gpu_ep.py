@@ -22,10 +22,16 @@ def _port():
         return s.getsockname()[1]
 
 
-def test_expert_parallel_matches_single_gpu():
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_expert_parallel_matches_single_gpu(transport):
+    """peer: rows and outputs as peer-memory stores into fixed slabs (all
+    cases). nccl: the same slabs over NCCL for the small cases and the
+    host-sized exchange for the large one."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    if transport == "nccl":
+        env["HF_EP_NCCL_ONLY"] = "1"
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
            f"--master-port={_port()}", os.path.join(HERE, "ep_worker.py")]
