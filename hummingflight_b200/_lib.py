@@ -58,6 +58,8 @@ SIGNATURES = {
     "hf_moe_forward": (c_int, [c_vp, c_int, c_vp, c_int, c_int, c_vp, ctypes.POINTER(HfMoeRouting), c_vp]),
     "hf_moe_forward_host": (c_int, [c_vp, c_int, c_vp, c_int, c_int, c_vp, c_vp]),
     "hf_moe_layer": (c_int, [c_vp, c_int, c_vp, c_vp]),
+    "hf_moe_block_forward": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_float, c_int, c_int,
+                                     ctypes.POINTER(HfMoeRouting), c_vp]),
     "hf_moe_route": (c_int, [c_vp, c_int, c_vp, c_int, c_int, ctypes.POINTER(HfMoeRouting), c_vp]),
     "hf_ep_unique_id": (c_int, [c_vp]),
     "hf_ep_plan": (c_int, [c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
@@ -74,6 +76,9 @@ SIGNATURES = {
     "hf_dense_mlp_workspace_size": (c_size, [c_int, c_int, c_int]),
     "hf_dense_mlp_forward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_size, c_vp]),
     "hf_dense_mlp_status": (c_int, [c_vp, c_vp]),
+    "hf_dense_block_forward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_float, c_int, c_vp, c_vp, c_int,
+                                       c_int, c_int, c_vp, c_size, c_vp]),
+    "hf_rmsnorm": (c_int, [c_vp, c_vp, c_float, c_int, c_int, c_vp, c_int, c_vp]),
     "hf_synth_bf16_normal": (c_int, [c_vp, c_u64, c_u64, c_u32, c_u32, c_u32, ctypes.c_double, c_vp]),
     "hf_synth_f32_uniform": (c_int, [c_vp, c_u64, c_u64, c_u32, c_u32, c_u32, c_float, c_float, c_vp]),
     "hf_moe_synth_layer": (c_int, [c_vp, c_int, c_u64, c_u32, c_vp, c_vp]),

@@ -182,14 +182,14 @@ struct RouterTiles {
 RouterTiles router_tiles(int T, int E, int H, int nsm);
 bool use_tc_router(const hf_moe_ctx* c, const LayerBuf& L, const void* x, hf_dtype xd, int T);
 hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st);
-hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, float* slot_out,
-                      cudaStream_t st);
+hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, const float* resid,
+                      float* slot_out, cudaStream_t st);
 
 // hf_ep.cu
 hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id);
 void ep_destroy(hf_moe_ctx* c);
 hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T, float* out,
-                     const hf_moe_routing* r, cudaStream_t st);
+                     const float* resid, const hf_moe_routing* r, cudaStream_t st);
 size_t ep_recv_cap(const hf_moe_ctx* c);
 
 }  // namespace hf

@@ -461,7 +461,8 @@ void ep_destroy(hf_moe_ctx* c) {
 // Slab exchange (peer memory at any size, NCCL for small batches): fixed
 // per-source regions, counts and plan stay on the device.
 static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T,
-                                  float* out, const hf_moe_routing* r, cudaStream_t st) {
+                                  float* out, const float* resid, const hf_moe_routing* r,
+                                  cudaStream_t st) {
     EpState& e = *c->ep;
     NcclApi& n = nccl();
     const int W = c->world, El = c->E_local, k = c->k, H = c->H, cap = e.cap;
@@ -588,13 +589,14 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     }
     py.done(T > 0 ? 2 : 1);
     // 5. combine in the reference order at the source
-    if (T > 0) HF_TRY(run_combine(c, e.yrecv, T, out, r ? r->slot_out : nullptr, st));
+    if (T > 0) HF_TRY(run_combine(c, e.yrecv, T, out, resid, r ? r->slot_out : nullptr, st));
     return HF_OK;
 }
 
 // Large batches: per-forward counts sized on the host, exact-size exchange.
 static hf_status ep_forward_sized(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T,
-                                  float* out, const hf_moe_routing* r, cudaStream_t st) {
+                                  float* out, const float* resid, const hf_moe_routing* r,
+                                  cudaStream_t st) {
     EpState& e = *c->ep;
     NcclApi& n = nccl();
     const int W = c->world, El = c->E_local, k = c->k, H = c->H;
@@ -709,14 +711,14 @@ static hf_status ep_forward_sized(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
                                 cudaMemcpyDeviceToDevice, st));
     py.done(R > 0 ? 1 : 0);
     // 6. combine in the reference order at the source
-    if (T > 0) HF_TRY(run_combine(c, e.yrecv, T, out, r ? r->slot_out : nullptr, st));
+    if (T > 0) HF_TRY(run_combine(c, e.yrecv, T, out, resid, r ? r->slot_out : nullptr, st));
     return HF_OK;
 }
 
 hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T, float* out,
-                     const hf_moe_routing* r, cudaStream_t st) {
-    if (c->ep->cap > 0) return ep_forward_slabs(c, L, x, xd, T, out, r, st);
-    return ep_forward_sized(c, L, x, xd, T, out, r, st);
+                     const float* resid, const hf_moe_routing* r, cudaStream_t st) {
+    if (c->ep->cap > 0) return ep_forward_slabs(c, L, x, xd, T, out, resid, r, st);
+    return ep_forward_sized(c, L, x, xd, T, out, resid, r, st);
 }
 
 }  // namespace hf

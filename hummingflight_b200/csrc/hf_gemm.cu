@@ -449,7 +449,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                             }
                         }
                     }
-                } else {  // down rows m0 + r (and m0 + 128 + r) -> fp32 outputs
+                } else if (!a.resid) {  // down rows m0 + r (and m0 + 128 + r) -> fp32 outputs
 #pragma unroll
                     for (int j = 0; j < CW; ++j) {
                         const int col = c0 + j;
@@ -458,6 +458,29 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                             float* yr = a.y + t.yoff + pos * a.H + t.m0 + rr;
                             if (rv) yr[0] = __uint_as_float(v0[j]);
                             if (NUM_A == 2 && rv1) yr[128] = __uint_as_float(v1[j]);
+                        }
+                    }
+                } else {  // residual block (dense MLP): y = resid + down row; the thread
+                          // reads, then writes, its own elements, 8 columns of loads in flight
+#pragma unroll
+                    for (int j0 = 0; j0 < CW; j0 += 8) {
+                        float q0[8], q1[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const int col = c0 + j0 + j;
+                            const size_t yi = size_t(t.seg + t.n0 + col) * a.H + t.m0 + rr;
+                            q0[j] = (col < t.n && rv) ? a.resid[yi] : 0.f;
+                            q1[j] = (NUM_A == 2 && col < t.n && rv1) ? a.resid[yi + 128] : 0.f;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const int col = c0 + j0 + j;
+                            if (col < t.n) {
+                                float* yr = a.y + size_t(t.seg + t.n0 + col) * a.H + t.m0 + rr;
+                                if (rv) yr[0] = __fadd_rn(q0[j], __uint_as_float(v0[j0 + j]));
+                                if (NUM_A == 2 && rv1)
+                                    yr[128] = __fadd_rn(q1[j], __uint_as_float(v1[j0 + j]));
+                            }
                         }
                     }
                 }

@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(256) k_gemv1(GemvArgs a) {
 // Four down rows (h0..h0+3) against NT mid vectors (fp32, shared memory).
 template <int NT>
 __device__ __forceinline__ void gemv2_rows(const GroupW& W, int H, int h0, const float* ms,
-                                           int lane, float* y, int p0) {
+                                           int lane, float* y, int p0, const float* resid) {
     const int I = W.inter;
     if (h0 >= H) return;
     const uint16_t* pr[4];
@@ -220,7 +220,11 @@ __device__ __forceinline__ void gemv2_rows(const GroupW& W, int H, int h0, const
     for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int r = 0; r < 4; ++r)
-            if (lane == 4 * j + r && h0 + r < H) y[size_t(p0 + j) * H + h0 + r] = acc[r][j];
+            if (lane == 4 * j + r && h0 + r < H) {
+                const size_t yi = size_t(p0 + j) * H + h0 + r;
+                // residual block (dense MLP, positions are tokens): read, then write, yi
+                y[yi] = resid ? __fadd_rn(resid[yi], acc[r][j]) : acc[r][j];
+            }
 }
 
 __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
@@ -256,10 +260,10 @@ __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
         __syncthreads();
         const int h0 = rb * kGemv2Rows + warp * 4;
         switch (te) {
-            case 1: gemv2_rows<1>(W, H, h0, ms, lane, a.y, p0); break;
-            case 2: gemv2_rows<2>(W, H, h0, ms, lane, a.y, p0); break;
-            case 3: gemv2_rows<3>(W, H, h0, ms, lane, a.y, p0); break;
-            default: gemv2_rows<4>(W, H, h0, ms, lane, a.y, p0); break;
+            case 1: gemv2_rows<1>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+            case 2: gemv2_rows<2>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+            case 3: gemv2_rows<3>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+            default: gemv2_rows<4>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
         }
     }
 }
@@ -322,6 +326,9 @@ int gemv_grid(int device, bool first, bool xf32, int H, int inter_max, int G, in
 // ============================================================ combine
 // glm_forward.cpp:555-556, 639-640, 658-660: moeOut = 0; moeOut += w_i * y_i in
 // top-k rank order (separate multiply and add); output = moeOut + sharedOut.
+// With a residual (the MLP block, glm_forward.cpp:795-796): output = residual +
+// (moeOut + sharedOut); each thread reads its residual elements before it
+// writes the same elements, so the residual may be the output buffer.
 __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
     const int H4 = a.H >> 2;
     const size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -363,6 +370,13 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
     acc.y = __fadd_rn(acc.y, s.y);
     acc.z = __fadd_rn(acc.z, s.z);
     acc.w = __fadd_rn(acc.w, s.w);
+    if (a.resid) {
+        const float4 rs = *reinterpret_cast<const float4*>(a.resid + size_t(t) * a.H + h);
+        acc.x = __fadd_rn(rs.x, acc.x);
+        acc.y = __fadd_rn(rs.y, acc.y);
+        acc.z = __fadd_rn(rs.z, acc.z);
+        acc.w = __fadd_rn(rs.w, acc.w);
+    }
     *reinterpret_cast<float4*>(a.out + size_t(t) * a.H + h) = acc;
 }
 

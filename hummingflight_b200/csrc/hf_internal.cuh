@@ -239,6 +239,8 @@ struct GemvArgs {
     int inter_max;          // mid row stride
     float* mid;             // [(T*k+T) x inter_max] fp32
     float* y;               // [(T*k+T) x H] fp32
+    const float* resid;     // optional, one group whose positions are tokens (dense MLP):
+                            // y = resid + down row; may alias y
     int grid1, grid2;
     int te_cap;             // most tokens in one chunk: min(T, kGemvTE); sizes the staging
 };
@@ -260,6 +262,9 @@ struct GemmArgs {
     uint16_t* mid_hi;       // [slots x Imax] bf16
     uint16_t* mid_lo;
     float* y;               // [slots x H] fp32
+    // optional (GEMM2, nsplit == 1, one group whose positions are tokens --
+    // the dense MLP): y = resid + down row; may alias y
+    const float* resid;
     int* err;               // error word (plan stats[3])
     unsigned long long timeout_ns;
     int test_stall;         // wait on a barrier nothing signals (test hook)
@@ -306,9 +311,15 @@ struct CombineArgs {
     const float* w;        // [T x k]
     int T, H, k, has_shared;
     float* out;            // [T x H]
+    const float* resid;    // optional [T x H]: out = resid + (routed + shared); may alias out
     float* slot_out;       // optional [(T*k+T) x H] by slot id
 };
 hf_status launch_combine(const CombineArgs& a, cudaStream_t st);
+
+// RMSNorm of fp32 rows with its output form (hf_norm.cu).
+enum NormOut { kNormF32 = 0, kNormBf16 = 1, kNormHiLo = 2 };
+hf_status launch_rmsnorm(const float* x, const uint16_t* w, float eps, int T, int H, int mode,
+                         void* out, uint16_t* out_lo, cudaStream_t st);
 
 hf_status launch_gemv_plain(const uint16_t* A, const float* x, float* y, int M, int K,
                             float alpha, float beta, cudaStream_t st);

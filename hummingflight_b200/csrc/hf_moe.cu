@@ -295,9 +295,10 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
     return HF_OK;
 }
 
-hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, float* slot_out,
-                      cudaStream_t st) {
+hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, const float* resid,
+                      float* slot_out, cudaStream_t st) {
     CombineArgs ca{};
+    ca.resid = resid;
     ca.y = y;
     ca.slot_pos = c->slot_pos;
     ca.w = c->w;
@@ -692,7 +693,8 @@ static hf_status copy_routing(hf_moe_ctx* c, const hf_moe_routing* r, int T, cud
 }
 
 static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype xd, int T,
-                             float* out, const hf_moe_routing* r, cudaStream_t st, bool route_only) {
+                             float* out, const float* resid, const hf_moe_routing* r,
+                             cudaStream_t st, bool route_only) {
     LayerBuf& L = c->layers[layer];
     if (!L.loaded) return fail(HF_ERR_STATE, "layer weights not set (hf_moe_set_router first)");
     if (T < 0 || T > c->T_max) return fail(HF_ERR_ARG, "T out of range (0..max_tokens)");
@@ -703,7 +705,7 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
     c->last_stream = st;
     if (c->world > 1 && !route_only) {
         // every rank takes part in the exchanges, even with no tokens of its own
-        HF_TRY(ep_forward(c, L, x, xd, T, out, r, st));
+        HF_TRY(ep_forward(c, L, x, xd, T, out, resid, r, st));
         return copy_routing(c, r, T, st);
     }
     if (T == 0) return HF_OK;
@@ -729,7 +731,7 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
         w.maybe_gemv = !ra.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
                        (c->cfg.path == HF_PATH_AUTO && ra.gemv_max > 0);
         HF_TRY(run_experts(c, L, w, st));
-        HF_TRY(run_combine(c, c->y, T, out, r ? r->slot_out : nullptr, st));
+        HF_TRY(run_combine(c, c->y, T, out, resid, r ? r->slot_out : nullptr, st));
     }
     return copy_routing(c, r, T, st);
 }
@@ -738,14 +740,14 @@ hf_status hf_moe_forward(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_d
                          float* out, const hf_moe_routing* routing, hf_stream stream) {
     HF_TRY(check_layer(ctx, layer, "hf_moe_forward"));
     DeviceGuard dg(ctx->cfg.device);
-    return run_forward(ctx, layer, x, x_dtype, T, out, routing, as_cuda(stream), false);
+    return run_forward(ctx, layer, x, x_dtype, T, out, nullptr, routing, as_cuda(stream), false);
 }
 
 hf_status hf_moe_route(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_dtype, int T,
                        const hf_moe_routing* routing, hf_stream stream) {
     HF_TRY(check_layer(ctx, layer, "hf_moe_route"));
     DeviceGuard dg(ctx->cfg.device);
-    return run_forward(ctx, layer, x, x_dtype, T, nullptr, routing, as_cuda(stream), true);
+    return run_forward(ctx, layer, x, x_dtype, T, nullptr, nullptr, routing, as_cuda(stream), true);
 }
 
 hf_status hf_moe_forward_host(hf_moe_ctx* ctx, int layer, const void* x_host, hf_dtype x_dtype,
@@ -757,7 +759,8 @@ hf_status hf_moe_forward_host(hf_moe_ctx* ctx, int layer, const void* x_host, hf
     cudaStream_t st = as_cuda(stream);
     const size_t xb = size_t(T) * ctx->H * (x_dtype == HF_F32 ? 4 : 2);
     if (T > 0) HF_CUDA(cudaMemcpyAsync(ctx->x_dev, x_host, xb, cudaMemcpyHostToDevice, st));
-    HF_TRY(run_forward(ctx, layer, ctx->x_dev, x_dtype, T, ctx->out_dev, nullptr, st, false));
+    HF_TRY(run_forward(ctx, layer, ctx->x_dev, x_dtype, T, ctx->out_dev, nullptr, nullptr, st,
+                       false));
     if (T > 0)
         HF_CUDA(cudaMemcpyAsync(out_host, ctx->out_dev, sizeof(float) * T * ctx->H,
                                 cudaMemcpyDeviceToHost, st));
@@ -790,6 +793,42 @@ hf_status hf_moe_debug_stall(hf_moe_ctx* ctx, int enable) {
 
 hf_status hf_moe_layer(hf_moe_ctx* ctx, int layer, const float* input, float* output) {
     return hf_moe_forward_host(ctx, layer, input, HF_F32, 1, output, nullptr);
+}
+
+// glm_forward.cpp:785-796: residual = hidden; hidden = rmsNorm(hidden);
+// mlpOut = moeLayer(hidden); hidden = residual + mlpOut. The normalised rows
+// go to the input staging buffer (fp32 or bf16), the layer runs on them, and
+// the combine writes residual + (routed + shared) into hidden_out.
+hf_status hf_moe_block_forward(hf_moe_ctx* ctx, int layer, const float* hidden_in,
+                               float* hidden_out, const uint16_t* norm_weight, float eps,
+                               hf_dtype act_dtype, int T, const hf_moe_routing* routing,
+                               hf_stream stream) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_block_forward"));
+    if (T < 0 || T > ctx->T_max) return fail(HF_ERR_ARG, "T out of range (0..max_tokens)");
+    if (act_dtype != HF_F32 && act_dtype != HF_BF16)
+        return fail(HF_ERR_ARG, "hf_moe_block_forward: act_dtype must be HF_F32 or HF_BF16");
+    if (T > 0 && (!hidden_in || !hidden_out || !aligned16(hidden_in) || !aligned16(hidden_out)))
+        return fail(HF_ERR_ARG, "hf_moe_block_forward: hidden must be 16-byte aligned device memory");
+    if (norm_weight && !aligned16(norm_weight))
+        return fail(HF_ERR_ARG, "hf_moe_block_forward: norm_weight must be 16-byte aligned");
+    if (hidden_in != hidden_out && T > 0) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(hidden_in);
+        const uintptr_t b = reinterpret_cast<uintptr_t>(hidden_out);
+        const uintptr_t n = sizeof(float) * size_t(T) * ctx->H;
+        if (a < b + n && b < a + n)
+            return fail(HF_ERR_ARG, "hf_moe_block_forward: hidden_in and hidden_out overlap "
+                                    "without being the same buffer");
+    }
+    DeviceGuard dg(ctx->cfg.device);
+    cudaStream_t st = as_cuda(stream);
+    if (T > 0) {
+        PhaseTimer p9(ctx, st, 9);
+        HF_TRY(launch_rmsnorm(hidden_in, norm_weight, eps, T, ctx->H,
+                              act_dtype == HF_F32 ? kNormF32 : kNormBf16, ctx->x_dev, nullptr, st));
+        p9.done(1);
+    }
+    return run_forward(ctx, layer, ctx->x_dev, act_dtype, T, hidden_out, hidden_in, routing, st,
+                       false);
 }
 
 hf_status hf_moe_last_stats(hf_moe_ctx* ctx, int* active, int* gemv_segments, int* gemm_segments) {

@@ -26,6 +26,7 @@ from ._lib import (HF_BF16, HF_F32, HF_MEM_DEVICE, HF_MEM_HOST, HF_PATH_AUTO, HF
 from .configs import GLM, LayerShape
 
 _PATHS = {"auto": HF_PATH_AUTO, "gemv": HF_PATH_GEMV, "gemm": HF_PATH_GEMM}
+_ACT = {"f32": HF_F32, "bf16": HF_BF16}
 
 
 def _torch():
@@ -148,6 +149,25 @@ class MoELayer:
              ctypes.byref(rs) if rs is not None else None, _stream(stream))
         return (out, r) if routing else out
 
+    def block_forward(self, layer: int, hidden, norm_weight=None, eps: float = 1e-5,
+                      act_dtype: str = "f32", out=None, routing: bool = False,
+                      slot_out: bool = False, stream=None):
+        """The MLP residual block (glm_forward.cpp:785-796): returns
+        hidden + moeLayer(rmsNorm(norm_weight, hidden)) as fp32 [T x H].
+
+        hidden: device fp32 [T x H]; norm_weight: device BF16 bits [H] or None;
+        act_dtype "f32" (the reference's hand-off) or "bf16"; out may be
+        `hidden` itself (in place, as the reference updates hiddenStates)."""
+        torch = _torch()
+        T, H = hidden.shape
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.float32, device=hidden.device)
+        r, rs = self._routing_bufs(T, hidden.device, routing, slot_out)
+        call("hf_moe_block_forward", self._h, layer, _ptr(hidden), _ptr(out), _ptr(norm_weight),
+             eps, _ACT[act_dtype], T, ctypes.byref(rs) if rs is not None else None,
+             _stream(stream))
+        return (out, r) if routing else out
+
     def route(self, layer: int, x, stream=None):
         torch = _torch()
         T, _ = x.shape
@@ -212,7 +232,7 @@ class MoELayer:
         return dict(active_experts=a.value, gemv_segments=b.value, gemm_segments=c.value)
 
     PHASES = ("router", "route", "gemv_gate_up", "gemv_down", "gemm_gate_up", "gemm_down",
-              "combine", "ep_dispatch", "ep_return")
+              "combine", "ep_dispatch", "ep_return", "norm")
 
     def profile(self, enable: bool = True):
         call("hf_moe_profile", self._h, int(enable))
@@ -278,6 +298,40 @@ def dense_mlp_forward(gate, up, down, x, out=None, workspace=None, stream=None):
     return out, workspace
 
 
+def dense_block_forward(gate, up, down, hidden, norm_weight=None, eps: float = 1e-5,
+                        act_dtype: str = "f32", out=None, workspace=None, stream=None):
+    """The dense layers' MLP residual block (glm_forward.cpp:785-796 with
+    denseMlp): hidden + denseMlp(rmsNorm(norm_weight, hidden)), fp32 [T x H].
+    out may be `hidden` itself."""
+    torch = _torch()
+    T, H = hidden.shape
+    I = gate.shape[0]
+    if tuple(gate.shape) != (I, H) or tuple(up.shape) != (I, H) or tuple(down.shape) != (H, I):
+        raise ValueError("dense_block_forward: gate/up must be [I x H] and down [H x I]")
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float32, device=hidden.device)
+    need = dense_mlp_workspace_size(T, H, I)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=hidden.device)
+    call("hf_dense_block_forward", _ptr(gate), _ptr(up), _ptr(down), _ptr(norm_weight), eps,
+         _ACT[act_dtype], _ptr(hidden), _ptr(out), T, H, I, _ptr(workspace), workspace.numel(),
+         _stream(stream))
+    return out, workspace
+
+
+def rmsnorm(x, weight=None, eps: float = 1e-5, out_dtype: str = "f32", out=None, stream=None):
+    """GLMForward::rmsNorm (glm_forward.cpp:185-197) over the rows of x [T x H]
+    (device fp32); weight: device BF16 bits [H] or None. Returns fp32 or bf16."""
+    torch = _torch()
+    T, H = x.shape
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float32 if out_dtype == "f32" else torch.bfloat16,
+                          device=x.device)
+    call("hf_rmsnorm", _ptr(x), _ptr(weight), eps, T, H, _ptr(out), _ACT[out_dtype],
+         _stream(stream))
+    return out
+
+
 def dense_mlp_status(workspace, stream=None):
     """Waits for the stream; raises HfError (HF_ERR_TIMEOUT) if the last dense
     forward on this workspace hit a bounded-wait timeout."""
@@ -299,5 +353,6 @@ def synth_f32_uniform(dst, seed: int, layer: int, kind: int, expert: int, lo: fl
 
 
 __all__ = ["MoELayer", "gemv_bf16_f32", "top_k_scores", "dense_mlp_forward",
-           "dense_mlp_workspace_size", "dense_mlp_status", "synth_bf16_normal",
+           "dense_mlp_workspace_size", "dense_mlp_status", "dense_block_forward", "rmsnorm",
+           "synth_bf16_normal",
            "synth_f32_uniform", "HfError", "HF_BF16", "HF_F32"]

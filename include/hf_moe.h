@@ -146,6 +146,23 @@ HF_API hf_status hf_moe_forward_host(hf_moe_ctx* ctx, int layer, const void* x_h
  * vectors of hidden_size, synchronous (model/glm_forward.h:93). */
 HF_API hf_status hf_moe_layer(hf_moe_ctx* ctx, int layer, const float* input, float* output);
 
+/* The MLP residual block of an MoE layer (glm_forward.cpp:785-796):
+ * hidden_out = hidden_in + moeLayer(rmsNorm(post_attention_layernorm, hidden_in)),
+ * asynchronous on `stream`. hidden_in / hidden_out: device fp32 [T x H], 16-byte
+ * aligned, and may be the same buffer (the reference updates hiddenStates in
+ * place). norm_weight: device BF16 [H] (postAttentionLayernorm), or NULL for
+ * x * rms (rmsNorm without a weight pointer, :194-195); eps: config
+ * rms_norm_eps. act_dtype: the form the normalised rows are handed to the
+ * layer in -- HF_F32 (the reference's fp32 hand-off; the expert GEMMs read it
+ * as a bf16 hi + lo pair) or HF_BF16 (rounded once, RNE: half the bytes and the
+ * tensor-core router). The residual add is fused into the combine; the
+ * normalised rows live in the context's input staging buffer. Expert
+ * parallelism as for hf_moe_forward (every rank calls it, T may be 0). */
+HF_API hf_status hf_moe_block_forward(hf_moe_ctx* ctx, int layer, const float* hidden_in,
+                                      float* hidden_out, const uint16_t* norm_weight, float eps,
+                                      hf_dtype act_dtype, int T, const hf_moe_routing* routing,
+                                      hf_stream stream);
+
 /* Routing only (router GEMV, sigmoid, bias, top-k, permutation) into `routing`. */
 HF_API hf_status hf_moe_route(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_dtype, int T,
                        const hf_moe_routing* routing, hf_stream stream);
@@ -222,9 +239,10 @@ HF_API hf_status hf_moe_last_stats(hf_moe_ctx* ctx, int* active_experts, int* ge
  * cuda_backend.cpp:464-477). Phases: 0 router logits, 1 top-k + permutation
  * + plan, 2 GEMV gate/up, 3 GEMV down, 4 GEMM gate/up, 5 GEMM down,
  * 6 combine, 7 expert-parallel dispatch (counts + rows to their ranks), 8
- * expert-parallel return (outputs back to their sources). Kernel launches
+ * expert-parallel return (outputs back to their sources), 9 RMSNorm of the
+ * residual block (hf_moe_block_forward). Kernel launches
  * (of this library) are counted whether or not timing is on. */
-#define HF_MOE_PHASES 9
+#define HF_MOE_PHASES 10
 HF_API hf_status hf_moe_profile(hf_moe_ctx* ctx, int enable);
 /* Waits for the recorded work, writes each phase's milliseconds and kernel
  * launches since the previous read (either pointer may be NULL), then resets. */
@@ -260,6 +278,26 @@ HF_API hf_status hf_dense_mlp_forward(const uint16_t* gate, const uint16_t* up, 
  * workspace hit a bounded-wait timeout (HF_ERR_TIMEOUT) -- no counterpart in
  * the reference, whose CPU GEMVs cannot time out. */
 HF_API hf_status hf_dense_mlp_status(const void* workspace, hf_stream stream);
+
+/* The MLP residual block of a dense layer (glm_forward.cpp:785-796 with
+ * denseMlp): hidden_out = hidden_in + denseMlp(rmsNorm(norm_weight, hidden_in)).
+ * Arguments as hf_dense_mlp_forward and hf_moe_block_forward (hidden_in and
+ * hidden_out may alias; norm_weight NULL = no weight; act_dtype HF_F32 or
+ * HF_BF16); the same workspace size. The RMSNorm writes the GEMM's operand
+ * planes directly and the down projection's epilogue adds the residual. */
+HF_API hf_status hf_dense_block_forward(const uint16_t* gate, const uint16_t* up,
+                                        const uint16_t* down, const uint16_t* norm_weight,
+                                        float eps, hf_dtype act_dtype, const float* hidden_in,
+                                        float* hidden_out, int T, int H, int I, void* workspace,
+                                        size_t workspace_bytes, hf_stream stream);
+
+/* Device twin of GLMForward::rmsNorm (glm_forward.cpp:185-197) over T rows:
+ * out = x * (1 / sqrt(mean(x^2) + eps)) * weight. x: device fp32 [T x H];
+ * weight: device BF16 [H] or NULL (no weight); out: device [T x H] of
+ * out_dtype (HF_F32, or HF_BF16 rounded to nearest even). H a multiple of 4,
+ * pointers 16-byte aligned; out must not overlap x. */
+HF_API hf_status hf_rmsnorm(const float* x, const uint16_t* weight, float eps, int T, int H,
+                            void* out, hf_dtype out_dtype, hf_stream stream);
 
 #ifdef __cplusplus
 }

@@ -57,6 +57,22 @@ void hfo_router_scores(const uint16_t* router_w, const float* x, int E, int H, f
     for (int i = 0; i < E; ++i) scores[i] = 1.0f / (1.0f + expf(-scores[i]));
 }
 
+/* model/glm_forward.cpp:185-197 */
+void hfo_rmsnorm(const float* x, const uint16_t* w, float eps, int n, float* out) {
+    float sq = 0.0f;
+    for (int i = 0; i < n; ++i) sq += x[i] * x[i];
+    const float rms = 1.0f / sqrtf(sq / (float)n + eps);
+    for (int i = 0; i < n; ++i) {
+        const float v = x[i] * rms;
+        out[i] = w ? v * hfg_bf16_to_f32(w[i]) : v;
+    }
+}
+
+/* model/glm_forward.cpp:795-796: hiddenStates = residual; hiddenStates += mlpOut */
+void hfo_residual_add(const float* x, const float* mlp_out, int n, float* out) {
+    for (int i = 0; i < n; ++i) out[i] = x[i] + mlp_out[i];
+}
+
 /* compute/moe_router.h:29-57 (selection by repeated arg-max is the same set
  * and order as the descending partial_sort, with ties to the lower id). */
 int hfo_topk_scores(const float* scores, int E, const float* bias, int top_k, float scale,

@@ -55,6 +55,15 @@ int hfo_topk_scores(const float* scores, int E, const float* bias, int top_k, fl
 void hfo_expert_ffn(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
                     const float* x, float* y, int H, int I);
 
+/* GLMForward::rmsNorm (model/glm_forward.cpp:185-197) on one row of n:
+ * sq = sum x_i^2 (i ascending), rms = 1 / sqrt(sq / n + eps),
+ * out_i = x_i * rms * w_i (w BF16; x_i * rms when w is NULL). out may be x. */
+void hfo_rmsnorm(const float* x, const uint16_t* w, float eps, int n, float* out);
+
+/* The MLP residual block (model/glm_forward.cpp:785-796) of one token:
+ * out = x + mlp(rmsNorm(x)), mlp_out given: out_i = x_i + mlp_out_i. */
+void hfo_residual_add(const float* x, const float* mlp_out, int n, float* out);
+
 /* Canonical permutation of the batched build (no reference counterpart; the
  * reference loops experts per token, glm_forward.cpp:581): order (expert asc,
  * token asc). counts[E+1], offsets[E+2], perm[T*k + T]; slot id t*k+i for

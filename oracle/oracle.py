@@ -78,6 +78,8 @@ def lib():
         L.hfo_router_scores.argtypes = [_c_u16p, _c_f32p, ctypes.c_int, ctypes.c_int, _c_f32p]
         L.hfo_expert_ffn.argtypes = [_c_u16p, _c_u16p, _c_u16p, _c_f32p, _c_f32p, ctypes.c_int,
                                      ctypes.c_int]
+        L.hfo_rmsnorm.argtypes = [_c_f32p, _c_u16p, ctypes.c_float, ctypes.c_int, _c_f32p]
+        L.hfo_residual_add.argtypes = [_c_f32p, _c_f32p, ctypes.c_int, _c_f32p]
         L.hfo_permute.argtypes = [_c_i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                   _c_i32p, _c_i32p, _c_i32p]
         L.hfo_moe_layer_synth.argtypes = [ctypes.POINTER(HfoDims), ctypes.c_uint64,
@@ -207,6 +209,27 @@ def gemv_bf16_f32(A_bf16, x, y=None, alpha=1.0, beta=0.0):
     y = np.zeros(M, np.float32) if y is None else np.array(y, dtype=np.float32)
     lib().hfo_gemv_bf16_f32(_p(A, _c_u16p), _p(x, _c_f32p), _p(y, _c_f32p), M, K, alpha, beta)
     return y
+
+
+def rmsnorm(x, w_bf16=None, eps=1e-5):
+    """GLMForward::rmsNorm (glm_forward.cpp:185-197) on each row of x [T x H]."""
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    w = None if w_bf16 is None else np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    out = np.empty_like(x)
+    for t in range(x.shape[0]):
+        lib().hfo_rmsnorm(_p(x[t], _c_f32p), _p(w, _c_u16p), eps, x.shape[1], _p(out[t], _c_f32p))
+    return out
+
+
+def residual_add(x, mlp_out):
+    """glm_forward.cpp:795-796: hidden = residual + mlpOut, per row."""
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    m = np.ascontiguousarray(np.atleast_2d(mlp_out), dtype=np.float32)
+    out = np.empty_like(x)
+    for t in range(x.shape[0]):
+        lib().hfo_residual_add(_p(x[t], _c_f32p), _p(m[t], _c_f32p), x.shape[1],
+                               _p(out[t], _c_f32p))
+    return out
 
 
 def router_scores(router_bf16, x_f32):

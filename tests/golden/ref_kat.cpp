@@ -6,6 +6,7 @@
 // seeds and distributions) and records what the reference's functions return:
 //   gemv    src/self_test.cpp:73-103     (M=8, K=33, mt19937(42), alpha/beta)
 //   topk    src/self_test.cpp:180-200    (8 scores, k=3, bias -10 on expert 2)
+//   rmsnorm src/self_test.cpp:125-138    (n=128, mt19937(3), eps 1e-5, no weight)
 //   expert  compute/cuda_backend.cpp:497-520 (64x32 case, mt19937(1)); the
 //           expected output is the CPU forward's math (expertFFNRaw,
 //           model/glm_forward.cpp:434-449) on gemv_bf16_f32
@@ -89,6 +90,22 @@ int main() {
             std::snprintf(nm, sizeof nm, "%s_w", c.name);
             put_f32(nm, r.weights, r.k);
         }
+    }
+    {  // self_test.cpp:125-138: the RMSNorm the reference checks GLMForward::rmsNorm's
+       // math with (n = 128, mt19937(3), U(-1, 1), eps = 1e-5, no weight)
+        const int n = 128;
+        const float eps = 1e-5f;
+        std::vector<float> x(n);
+        std::mt19937 rng(3);
+        std::uniform_real_distribution<float> dist(-1.0f, 1.0f);
+        for (auto& v : x) v = dist(rng);
+        float sqSum = 0.0f;
+        for (int i = 0; i < n; ++i) sqSum += x[i] * x[i];
+        float rms = 1.0f / std::sqrt(sqSum / float(n) + eps);
+        std::vector<float> ref = x;
+        for (int i = 0; i < n; ++i) ref[i] *= rms;
+        put_f32("rmsnorm_x", x.data(), n);
+        put_f32("rmsnorm_y", ref.data(), n);
     }
     {  // cuda_backend.cpp:497-520, case {64, 32}
         const int h = 64, i = 32;

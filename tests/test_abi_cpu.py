@@ -94,3 +94,37 @@ def test_dense_mlp_arguments_checked_before_any_device_call():
     assert call(nb=need - 1) == _lib.HF_ERR_ARG    # workspace too small
     assert call(T=0) == _lib.HF_OK                 # nothing to do
     assert L.hf_dense_mlp_status(None, None) == _lib.HF_ERR_ARG
+
+
+def test_block_and_rmsnorm_arguments_checked_before_any_device_call():
+    """hf_dense_block_forward, hf_moe_block_forward and hf_rmsnorm validate on
+    the host (the fake pointers below are never dereferenced)."""
+    L = _lib.lib()
+    T, H, I = 4, 256, 384
+    need = L.hf_dense_mlp_workspace_size(T, H, I)
+    p, q, ws = 0x10000, 0x20000, 0x100000
+    ok = [p, p, p, p, 1e-5, _lib.HF_F32, p, q, T, H, I, ws, need, None]
+    names = ["gate", "up", "down", "nw", "eps", "dt", "hin", "hout", "T", "H", "I", "ws", "nb",
+             "st"]
+
+    def dense(**kw):
+        a = list(ok)
+        for k, v in kw.items():
+            a[names.index(k)] = v
+        return L.hf_dense_block_forward(*a)
+
+    assert dense(T=-1) == _lib.HF_ERR_ARG
+    assert dense(hin=None) == _lib.HF_ERR_ARG
+    assert dense(dt=7) == _lib.HF_ERR_ARG
+    assert dense(nw=p + 8) == _lib.HF_ERR_ARG          # norm weight not 16-byte aligned
+    assert dense(hout=p + 16) == _lib.HF_ERR_ARG       # overlaps hidden_in, not the same buffer
+    assert dense(nb=need - 1) == _lib.HF_ERR_ARG
+    assert dense(T=0) == _lib.HF_OK
+
+    assert L.hf_moe_block_forward(None, 0, p, p, None, 1e-5, _lib.HF_F32, T, None,
+                                  None) == _lib.HF_ERR_ARG
+    assert L.hf_rmsnorm(p, None, 1e-5, T, 250, q, _lib.HF_F32, None) == _lib.HF_ERR_ARG
+    assert L.hf_rmsnorm(None, None, 1e-5, T, H, q, _lib.HF_F32, None) == _lib.HF_ERR_ARG
+    assert L.hf_rmsnorm(p, None, 1e-5, T, H, q, 7, None) == _lib.HF_ERR_ARG
+    assert L.hf_rmsnorm(p + 4, None, 1e-5, T, H, q, _lib.HF_F32, None) == _lib.HF_ERR_ARG
+    assert L.hf_rmsnorm(p, None, 1e-5, 0, H, q, _lib.HF_F32, None) == _lib.HF_OK

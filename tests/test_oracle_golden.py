@@ -2,7 +2,7 @@
 
 tests/golden/ holds vectors produced by the reference's unmodified
 compute/cpu_kernels.cpp and compute/moe_router.h (tests/golden/make_golden.py):
-its self-test inputs (src/self_test.cpp:73-103, :180-200), its expert-FFN
+its self-test inputs (src/self_test.cpp:73-103, :125-138, :180-200), its expert-FFN
 parity case (compute/cuda_backend.cpp:497-520) and GLMForward::moeLayer
 (model/glm_forward.cpp:509-661) on seeded layers. The oracle restates the
 scalar Linux build, so it must match that build bit for bit.
@@ -49,6 +49,29 @@ def test_gemv_avx2_build_within_selftest_tolerance():
     k = kat("avx2")
     y = O.gemv_bf16_f32(k["gemv_A"].reshape(8, 33), k["gemv_x"])
     assert np.abs(y - k["gemv_y"]).max() < 1e-3
+
+
+def test_rmsnorm_selftest_vector_bit_exact():
+    """self_test.cpp:125-138 (the math GLMForward::rmsNorm runs), no weight."""
+    k = kat("scalar")
+    y = O.rmsnorm(k["rmsnorm_x"], None, 1e-5)[0]
+    assert np.array_equal(y.view(np.uint32), k["rmsnorm_y"].view(np.uint32))
+
+
+def test_rmsnorm_weight_and_residual_follow_reference_order():
+    """glm_forward.cpp:193 multiplies (x * rms) * w left to right; :795-796
+    adds the MLP output to the residual. A weight of ones is the identity."""
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((3, 96)).astype(np.float32)
+    w = O.f32_to_bf16(rng.uniform(0.5, 1.5, 96).astype(np.float32))
+    got = O.rmsnorm(x, w, 1e-5)
+    plain = O.rmsnorm(x, None, 1e-5)
+    wf = O.bf16_to_f32(w)
+    assert np.array_equal(got, (plain * wf).astype(np.float32))
+    ones = O.f32_to_bf16(np.ones(96, np.float32))
+    assert np.array_equal(O.rmsnorm(x, ones, 1e-5), plain)
+    m = rng.standard_normal((3, 96)).astype(np.float32)
+    assert np.array_equal(O.residual_add(x, m), x + m)
 
 
 def test_topk_known_answers():
