@@ -1,5 +1,5 @@
-"""ctypes binding of libhf_moe.so (the C ABI declared in include/hf_moe.h and
-include/hf_synth.h).
+"""ctypes binding of libhf_moe.so (the C ABI declared in include/hf_moe.h,
+include/hf_synth.h and include/hf_ingest.h).
 
 The library is built in-tree by hummingflight_b200/build.py. Loading fails
 loudly when it is missing: there is no CPU fallback.
@@ -34,6 +34,24 @@ class HfMoeConfig(ctypes.Structure):
 class HfMoeRouting(ctypes.Structure):
     _fields_ = [("topk_ids", c_vp), ("topk_weights", c_vp), ("margins", c_vp), ("counts", c_vp),
                 ("offsets", c_vp), ("perm", c_vp), ("slot_out", c_vp)]
+
+
+class HfStOptions(ctypes.Structure):
+    _fields_ = [("require_bf16", c_int), ("allow_f32", ctypes.POINTER(ctypes.c_char_p)),
+                ("num_allow_f32", c_int), ("require_aligned_header", c_int),
+                ("require_aligned_data", c_int)]
+
+
+class HfStStats(ctypes.Structure):
+    _fields_ = [(n, c_u64) for n in ("total", "accepted", "rejected", "duplicate_rejected",
+                                     "dtype_rejected", "f32_allowed_accepted", "shape_rejected",
+                                     "bounds_rejected", "byte_mismatch_rejected",
+                                     "alignment_rejected")]
+
+
+class HfIngestStats(ctypes.Structure):
+    _fields_ = [("bytes", c_u64), ("tensors", c_int), ("experts", c_int),
+                ("skipped_experts", c_int), ("has_bias", c_int), ("seconds", ctypes.c_double)]
 
 
 class HfError(RuntimeError):
@@ -82,6 +100,21 @@ SIGNATURES = {
     "hf_synth_bf16_normal": (c_int, [c_vp, c_u64, c_u64, c_u32, c_u32, c_u32, ctypes.c_double, c_vp]),
     "hf_synth_f32_uniform": (c_int, [c_vp, c_u64, c_u64, c_u32, c_u32, c_u32, c_float, c_float, c_vp]),
     "hf_moe_synth_layer": (c_int, [c_vp, c_int, c_u64, c_u32, c_vp, c_vp]),
+    "hf_moe_set_expert_parts": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int]),
+    "hf_st_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(HfStOptions), ctypes.POINTER(c_vp),
+                           ctypes.POINTER(HfStStats)]),
+    "hf_st_close": (c_int, [c_vp]),
+    "hf_st_count": (c_int, [c_vp]),
+    "hf_st_tensor": (c_int, [c_vp, c_int, ctypes.POINTER(ctypes.c_char_p),
+                             ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(c_int),
+                             ctypes.POINTER(ctypes.c_int64), c_int, ctypes.POINTER(c_u64),
+                             ctypes.POINTER(c_u64)]),
+    "hf_st_find": (c_int, [c_vp, ctypes.c_char_p]),
+    "hf_st_read": (c_int, [c_vp, c_int, c_vp, c_u64]),
+    "hf_st_upload": (c_int, [c_vp, c_int, c_vp, c_u64, c_int]),
+    "hf_moe_load_safetensors": (c_int, [c_vp, c_int, c_int, ctypes.POINTER(ctypes.c_char_p), c_int,
+                                        ctypes.POINTER(HfIngestStats)]),
+    "hf_ingest_release_staging": (c_int, []),
 }
 
 _lib = None

@@ -185,6 +185,9 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
 hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, const float* resid,
                       float* slot_out, cudaStream_t st);
 
+// Allocates a layer's weight buffers and tensor maps on first use (hf_moe.cu).
+hf_status ctx_layer_alloc(hf_moe_ctx* c, int layer);
+
 // hf_ep.cu
 hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id);
 void ep_destroy(hf_moe_ctx* c);

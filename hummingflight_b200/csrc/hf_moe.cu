@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "hf_ctx.cuh"
+#include "hf_ingest.h"
 #include "hf_synth.h"
 
 namespace hf {
@@ -623,6 +624,23 @@ hf_status hf_moe_set_expert(hf_moe_ctx* ctx, int layer, int eid, const uint16_t*
     return HF_OK;
 }
 
+hf_status hf_moe_set_expert_parts(hf_moe_ctx* ctx, int layer, int eid, const uint16_t* gate,
+                                  const uint16_t* up, const uint16_t* down, hf_mem_kind kind) {
+    HF_TRY(check_layer(ctx, layer, "hf_moe_set_expert_parts"));
+    if (!gate || !up || !down) return fail(HF_ERR_ARG, "hf_moe_set_expert_parts: null projection");
+    if (eid < ctx->e_begin || eid >= ctx->e_begin + ctx->E_local)
+        return fail(HF_ERR_ARG, "hf_moe_set_expert_parts: expert id not owned by this context");
+    DeviceGuard dg(ctx->cfg.device);
+    HF_TRY(layer_alloc(ctx, layer));
+    LayerBuf& L = ctx->layers[layer];
+    uint16_t* b = L.experts + size_t(eid - ctx->e_begin) * ctx->expert_elems;
+    const size_t n = size_t(ctx->I) * ctx->H;
+    HF_CUDA(cudaMemcpy(b, gate, sizeof(uint16_t) * n, kind_of(kind)));
+    HF_CUDA(cudaMemcpy(b + n, up, sizeof(uint16_t) * n, kind_of(kind)));
+    HF_CUDA(cudaMemcpy(b + 2 * n, down, sizeof(uint16_t) * n, kind_of(kind)));
+    return HF_OK;
+}
+
 hf_status hf_moe_set_shared(hf_moe_ctx* ctx, int layer, const uint16_t* gate, const uint16_t* up,
                             const uint16_t* down, hf_mem_kind kind) {
     HF_TRY(check_layer(ctx, layer, "hf_moe_set_shared"));
@@ -926,3 +944,7 @@ hf_status hf_moe_synth_layer(hf_moe_ctx* ctx, int layer, uint64_t seed, uint32_t
 }
 
 }  // extern "C"
+
+namespace hf {
+hf_status ctx_layer_alloc(hf_moe_ctx* c, int layer) { return layer_alloc(c, layer); }
+}  // namespace hf

@@ -122,6 +122,23 @@ class MoELayer:
         b = None if bias is None else np.ascontiguousarray(bias, np.float32)
         call("hf_moe_synth_layer", self._h, layer, seed, gen_layer, _ptr(b), _stream(stream))
 
+    def set_expert_parts(self, layer: int, eid: int, gate, up, down):
+        """One expert from its three checkpoint tensors (experts.<e>.{gate,up,down}_proj)."""
+        g, u, d = _host_u16(gate), _host_u16(up), _host_u16(down)
+        call("hf_moe_set_expert_parts", self._h, layer, eid, _ptr(g), _ptr(u), _ptr(d), _kind(g))
+
+    def load_safetensors(self, layer: int, shard_paths, model_layer: Optional[int] = None):
+        """Makes `layer` resident from safetensors shards holding model layer
+        `model_layer` (default: the same index); returns the ingest stats."""
+        from ._lib import HfIngestStats
+        from .safetensors import shard_paths_arg
+        paths = [str(p) for p in shard_paths]
+        st = HfIngestStats()
+        call("hf_moe_load_safetensors", self._h, layer,
+             layer if model_layer is None else model_layer, shard_paths_arg(paths), len(paths),
+             ctypes.byref(st))
+        return {n: getattr(st, n) for n, _ in HfIngestStats._fields_}
+
     def expert_device_ptr(self, layer: int, eid: int) -> int:
         p = ctypes.c_void_p()
         call("hf_moe_expert_device_ptr", self._h, layer, eid, ctypes.byref(p))

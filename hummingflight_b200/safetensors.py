@@ -1,0 +1,119 @@
+"""Safetensors shards and checkpoint ingest (include/hf_ingest.h).
+
+``SafeTensors(path)`` is the reference's SafeTensorsFile
+(model/safetensors.h:64-80): the header is parsed and validated by
+libhf_moe.so with the checkpoint loader's strict options unless others are
+given; ``tensors()`` lists the accepted ones, ``read()`` returns a tensor's
+bytes, ``upload()`` sends them to device memory through the pinned ring.
+``MoELayer.load_safetensors`` (hummingflight_b200.moe) makes a whole MoE
+layer resident from its shards.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import HfStOptions, HfStStats, call
+
+_NP = {"BF16": np.uint16, "F32": np.float32, "F16": np.float16, "F64": np.float64,
+       "I64": np.int64, "I32": np.int32, "I16": np.int16, "I8": np.int8, "U64": np.uint64,
+       "U32": np.uint32, "U16": np.uint16, "U8": np.uint8, "BOOL": np.bool_}
+
+
+@dataclass
+class TensorInfo:
+    name: str
+    dtype: str
+    shape: tuple
+    file_offset: int
+    nbytes: int
+
+
+def options(require_bf16=True, allow_f32=("e_score_correction_bias",), aligned_header=True,
+            aligned_data=True) -> HfStOptions:
+    """SafeTensorsOptions (model/safetensors.h:38-48)."""
+    arr = (ctypes.c_char_p * max(1, len(allow_f32)))(*[s.encode() for s in allow_f32])
+    o = HfStOptions(int(require_bf16), ctypes.cast(arr, ctypes.POINTER(ctypes.c_char_p)),
+                    len(allow_f32), int(aligned_header), int(aligned_data))
+    o._keep = arr  # the fragments must outlive the call
+    return o
+
+
+class SafeTensors:
+    def __init__(self, path: str, opts: Optional[HfStOptions] = None):
+        self.path = path
+        self.stats = HfStStats()
+        h = ctypes.c_void_p()
+        call("hf_st_open", path.encode(), ctypes.byref(opts) if opts is not None else None,
+             ctypes.byref(h), ctypes.byref(self.stats))
+        self._h = h
+
+    def stats_dict(self) -> Dict[str, int]:
+        return {n: int(getattr(self.stats, n)) for n, _ in HfStStats._fields_}
+
+    def __len__(self) -> int:
+        return int(_lib.lib().hf_st_count(self._h))
+
+    def info(self, i: int) -> TensorInfo:
+        name, dtype = ctypes.c_char_p(), ctypes.c_char_p()
+        nd = ctypes.c_int()
+        cap = 64
+        shape = (ctypes.c_int64 * cap)()
+        off, nb = ctypes.c_uint64(), ctypes.c_uint64()
+        call("hf_st_tensor", self._h, i, ctypes.byref(name), ctypes.byref(dtype), ctypes.byref(nd),
+             shape, cap, ctypes.byref(off), ctypes.byref(nb))
+        return TensorInfo(name.value.decode(), dtype.value.decode(),
+                          tuple(shape[d] for d in range(nd.value)), off.value, nb.value)
+
+    def tensors(self) -> List[TensorInfo]:
+        return [self.info(i) for i in range(len(self))]
+
+    def find(self, name: str) -> int:
+        return int(_lib.lib().hf_st_find(self._h, name.encode()))
+
+    def read(self, name: str) -> np.ndarray:
+        i = self.find(name)
+        if i < 0:
+            raise KeyError(name)
+        t = self.info(i)
+        out = np.empty(t.shape, _NP[t.dtype])
+        call("hf_st_read", self._h, i, out.ctypes.data, out.nbytes)
+        return out
+
+    def upload(self, name: str, dst, device: int = 0):
+        """Copies tensor `name` into device tensor `dst` (at least as many bytes)."""
+        i = self.find(name)
+        if i < 0:
+            raise KeyError(name)
+        nbytes = dst.numel() * dst.element_size()
+        call("hf_st_upload", self._h, i, dst.data_ptr(), nbytes, device)
+        return dst
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.lib().hf_st_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def shard_paths_arg(paths: Sequence[str]):
+    arr = (ctypes.c_char_p * len(paths))(*[p.encode() for p in paths])
+    return arr
+
+
+__all__ = ["SafeTensors", "TensorInfo", "options", "shard_paths_arg"]
