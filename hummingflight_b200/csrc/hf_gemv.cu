@@ -15,6 +15,9 @@
 // (GEMV2) with 16-byte L1-bypassing loads, 8 loads in flight per lane, the
 // chunk's activations sitting in shared memory; fp32 accumulation, butterfly
 // shuffles, SwiGLU in the GEMV1 epilogue, mid kept fp32.
+#include <algorithm>
+#include <cstdlib>
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -389,29 +392,127 @@ hf_status launch_combine(const CombineArgs& a, cudaStream_t st) {
 }
 
 // ============================================================ gemv_bf16_f32 twin
-// compute/cpu_kernels.cpp:43-94: y[i] = alpha * dot(A[i,:], x) + beta * y[i].
+// compute/cpu_kernels.cpp:43-94: y[i] = alpha * dot(A[i,:], x) + beta * y[i],
+// y read even when beta == 0. The call sites (the attention projections,
+// glm_forward.cpp:314-408, and the router) are single vectors, so the kernel is
+// a pure weight stream. A block of 256 threads is cut into 256 / TPR groups;
+// a group owns R rows and its TPR threads walk them together in 16-byte chunks
+// (contiguous spans of TPR * 16 bytes per row), 8 / R chunks of each row in
+// flight per thread (eight 16-byte loads), x from L1; the partial sums of each
+// row are added across the group. TPR follows K (short rows: small groups, so
+// no thread idles) and R the row-block size; the grid is persistent (the
+// resident blocks of all SMs walk the row blocks), so no wave tail or block
+// turnover leaves an SM without loads in flight.
+template <int R, int TPR>
+__global__ void __launch_bounds__(256) k_gemv_rows(const uint16_t* __restrict__ A,
+                                                   const float* __restrict__ x, float* y, int M,
+                                                   int K, float alpha, float beta) {
+    constexpr int G = 256 / TPR, WPG = TPR / 32, U = 8 / R;
+    const int grp = threadIdx.x / TPR, t = threadIdx.x % TPR;
+    const int nc = K >> 3;  // 16-byte chunks per row
+    const int nblk = (M + G * R - 1) / (G * R);
+    __shared__ float part[8][R];
+    // persistent: the grid fills the SMs once and walks the row blocks
+    for (int bi = blockIdx.x; bi < nblk; bi += gridDim.x) {
+    const int r0 = (bi * G + grp) * R;
+    const uint16_t* rows[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) rows[r] = A + size_t(min(r0 + r, M - 1)) * K;
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    const float4* xv = reinterpret_cast<const float4*>(x);
+    int c = t;
+    // U chunks of each of the R rows per thread in flight (R * U = 8 loads)
+    for (; c + (U - 1) * TPR < nc; c += U * TPR) {
+        uint4 w[U][R];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int r = 0; r < R; ++r) w[u][r] = ld_stream_u4(rows[r] + size_t(c + u * TPR) * 8);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int cu = c + u * TPR;
+            const float4 a0 = __ldg(xv + 2 * cu), a1 = __ldg(xv + 2 * cu + 1);
+            const float xa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float f[8];
+                unpack8(w[u][r], f);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[r] = fmaf(f[e], xa[e], acc[r]);
+            }
+        }
+    }
+    for (; c < nc; c += TPR) {
+        const float4 a0 = __ldg(xv + 2 * c), a1 = __ldg(xv + 2 * c + 1);
+        const float xa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            float f[8];
+            unpack8(ld_stream_u4(rows[r] + size_t(c) * 8), f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[r] = fmaf(f[e], xa[e], acc[r]);
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const float v = warp_sum(acc[r]);
+        if (lane == 0) part[warp][r] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < G * R) {
+        const int g = threadIdx.x / R, r = threadIdx.x % R;
+        const int row = (bi * G + g) * R + r;
+        if (row < M) {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < WPG; ++w) v += part[g * WPG + w][r];
+            y[row] = __fadd_rn(__fmul_rn(alpha, v), __fmul_rn(beta, y[row]));
+        }
+    }
+    __syncthreads();  // part[] is rewritten by the next row block
+    }
+}
+
+// Launches one persistent grid: at most the resident blocks of all SMs.
+template <int R, int TPR>
+cudaError_t launch_rows(unsigned nblk, int dev, const uint16_t* A, const float* x, float* y,
+                        int M, int K, float alpha, float beta, cudaStream_t st) {
+    static std::atomic<int> per_sm{0};
+    int b = per_sm.load(std::memory_order_relaxed);
+    if (b == 0) {
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_gemv_rows<R, TPR>,
+                                                                      256, 0);
+        if (e != cudaSuccess || b <= 0) b = 1;
+        per_sm.store(b, std::memory_order_relaxed);
+    }
+    const unsigned grid = std::min<unsigned>(nblk, unsigned(b * num_sms(dev)));
+    k_gemv_rows<R, TPR><<<grid, 256, 0, st>>>(A, x, y, M, K, alpha, beta);
+    return cudaGetLastError();
+}
+
+template <int TPR>
+cudaError_t launch_gemv_tpr(int R, unsigned nblk, int dev, const uint16_t* A, const float* x,
+                            float* y, int M, int K, float alpha, float beta, cudaStream_t st) {
+    switch (R) {
+        case 8: return launch_rows<8, TPR>(nblk, dev, A, x, y, M, K, alpha, beta, st);
+        case 4: return launch_rows<4, TPR>(nblk, dev, A, x, y, M, K, alpha, beta, st);
+        case 2: return launch_rows<2, TPR>(nblk, dev, A, x, y, M, K, alpha, beta, st);
+        default: return launch_rows<1, TPR>(nblk, dev, A, x, y, M, K, alpha, beta, st);
+    }
+}
+
+// Any K or alignment: one warp per row, scalar loads.
 __global__ void __launch_bounds__(256) k_gemv_plain(const uint16_t* A, const float* x, float* y,
-                                                    int M, int K, float alpha, float beta,
-                                                    int vec) {
+                                                    int M, int K, float alpha, float beta) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
     if (row >= M) return;
     const uint16_t* ar = A + size_t(row) * K;
     float acc = 0.0f;
-    if (vec) {
-        for (int c = lane; c < (K >> 3); c += 32) {
-            float wf[8];
-            unpack8(ld_stream_u4(ar + size_t(c) * 8), wf);
-            const float4 x0 = __ldg(reinterpret_cast<const float4*>(x + c * 8));
-            const float4 x1 = __ldg(reinterpret_cast<const float4*>(x + c * 8) + 1);
-            acc = fmaf(wf[0], x0.x, acc); acc = fmaf(wf[1], x0.y, acc);
-            acc = fmaf(wf[2], x0.z, acc); acc = fmaf(wf[3], x0.w, acc);
-            acc = fmaf(wf[4], x1.x, acc); acc = fmaf(wf[5], x1.y, acc);
-            acc = fmaf(wf[6], x1.z, acc); acc = fmaf(wf[7], x1.w, acc);
-        }
-    } else {
-        for (int j = lane; j < K; j += 32) acc = fmaf(bf16_to_f32(ar[j]), __ldg(x + j), acc);
-    }
+    for (int j = lane; j < K; j += 32) acc = fmaf(bf16_to_f32(ar[j]), __ldg(x + j), acc);
     acc = warp_sum(acc);
     if (lane == 0) y[row] = __fadd_rn(__fmul_rn(alpha, acc), __fmul_rn(beta, y[row]));
 }
@@ -419,9 +520,39 @@ __global__ void __launch_bounds__(256) k_gemv_plain(const uint16_t* A, const flo
 hf_status launch_gemv_plain(const uint16_t* A, const float* x, float* y, int M, int K,
                             float alpha, float beta, cudaStream_t st) {
     if (M == 0) return HF_OK;
-    const int vec = (K % 8 == 0) && (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
-                    (reinterpret_cast<uintptr_t>(x) % 16 == 0);
-    k_gemv_plain<<<(M + 7) / 8, 256, 0, st>>>(A, x, y, M, K, alpha, beta, vec);
+    const bool vec = (K % 8 == 0) && (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+    if (!vec) {
+        k_gemv_plain<<<(M + 7) / 8, 256, 0, st>>>(A, x, y, M, K, alpha, beta);
+    } else {
+        // threads per row group: two or more chunks each. Rows per group: 4
+        // while there are as many row blocks as SMs (a sweep of 1, 2, 4 and 8
+        // rows and of 2, 4 and 8 chunks per thread on the attention shapes:
+        // 4 rows and 2 chunks fastest or within 5 % everywhere but q_b, where
+        // 8 chunks gain 15 %), else 2, else 1.
+        const int nc = K / 8;
+        const int tpr = nc >= 512 ? 256 : nc >= 256 ? 128 : nc >= 128 ? 64 : 32;
+        const int G = 256 / tpr;
+        int dev = 0;
+        HF_CUDA(cudaGetDevice(&dev));
+        const long long nsm = num_sms(dev);
+        int R = 1;
+        for (int r : {4, 2})
+            if ((M + G * r - 1) / (G * r) >= nsm) {
+                R = r;
+                break;
+            }
+
+        const unsigned g = unsigned((M + G * R - 1) / (G * R));
+        cudaError_t e;
+        switch (tpr) {
+            case 256: e = launch_gemv_tpr<256>(R, g, dev, A, x, y, M, K, alpha, beta, st); break;
+            case 128: e = launch_gemv_tpr<128>(R, g, dev, A, x, y, M, K, alpha, beta, st); break;
+            case 64: e = launch_gemv_tpr<64>(R, g, dev, A, x, y, M, K, alpha, beta, st); break;
+            default: e = launch_gemv_tpr<32>(R, g, dev, A, x, y, M, K, alpha, beta, st); break;
+        }
+        HF_CUDA(e);
+    }
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }

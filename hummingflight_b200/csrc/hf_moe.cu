@@ -8,6 +8,7 @@
 // caller's stream. A forward is three phases -- routing, experts, combine --
 // that the expert-parallel path (hf_ep.cu) reuses around its exchanges.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -38,9 +39,15 @@ hf_status cuda_fail(cudaError_t e, const char* what) {
 }
 
 int num_sms(int device) {
+    static std::atomic<int> cache[64];
+    if (device >= 0 && device < 64) {
+        const int c = cache[device].load(std::memory_order_relaxed);
+        if (c > 0) return c;
+    }
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
         n = 148;
+    if (device >= 0 && device < 64) cache[device].store(n, std::memory_order_relaxed);
     return n;
 }
 
