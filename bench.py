@@ -284,30 +284,40 @@ def main():
         step()
     torch.cuda.synchronize()
     L.profile_read()  # drop warm-up launch counts
-    L.profile(True)
+
+    def timed_pass():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        m = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([m], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            m = float(t.item())
+        return m
+
+    # pass 1 (the value): K steps as a user runs them. Pass 2: the same K steps
+    # with a CUDA event pair around every phase, for the per-kernel durations of
+    # the roofline; those events cost a few us per phase boundary, so they stay
+    # out of the first pass.
     clk = ClockSampler(local)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    ms = timed_pass()
+    launches = int(sum(v[1] for v in L.profile_read().values()))
+    L.profile(True)
+    ms_profiled = timed_pass()
     clocks = clk.stop()
     L.profile(False)
-    ms = e0.elapsed_time(e1) / args.steps
     prof = L.profile_read()
-    if world > 1:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
     tokens_per_step = T_glob * wl.layers
     value = tokens_per_step / (ms / 1e3)
-    launches = int(sum(v[1] for v in prof.values()))
 
     # end to end through hf_moe_forward_host: pinned host x in, pinned host out back
     xh = torch.empty((T, H), dtype=torch.int16, pin_memory=True)
@@ -318,6 +328,7 @@ def main():
         for l in range(wl.layers):
             L.forward_host(l, xh_np, oh_np, stream=stream)
     e_steps = max(3, args.steps // 4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -373,6 +384,9 @@ def main():
                     "h2d_bytes_per_step": T_glob * H * 2 * wl.layers,
                     "d2h_bytes_per_step": T_glob * H * 4 * wl.layers},
             "gpu_launches": launches,
+            "phase_timing": {"pass": "second timed pass of the same K steps with per-phase "
+                                     "CUDA events on the forward's stream",
+                             "ms_per_step_with_events": ms_profiled},
             # rank 0's weight stream per second, and useful flops of the whole job
             "layer_hbm_gbs": layer_bytes * wl.layers / (ms / 1e3) / 1e9,
             "layer_tflops": layer_flops(shape, T_glob) * wl.layers / (ms / 1e3) / 1e12,

@@ -121,6 +121,18 @@ __global__ void __launch_bounds__(256) k_gemv1(GemvArgs a) {
     void* xs = smem_raw;
     const int G = a.pl.G;
     const int H = a.H;
+    if (a.prefetch_shared) {
+        // the shared expert's weights do not depend on the routing: stream them
+        // into L2 while the routing kernel still runs (HBM is idle then); its
+        // units run first below, the down rows stay for GEMV2 (evict_last)
+        const GroupW S = a.groups[G - 1];
+        const size_t n = size_t(S.inter) * H * 2;
+        prefetch_l2<false>(S.gate, n);
+        prefetch_l2<false>(S.up, n);
+        prefetch_l2<true>(S.down, n);
+    }
+    griddep_wait();  // the plan and permutation come from the routing kernel
+    griddep_launch_dependents();
     int32_t* sp = reinterpret_cast<int32_t*>(smem_raw + size_t(a.te_cap) * H * (XF32 ? 4 : 2));
     stage_plan(sp, a.plan + a.pl.u1, a.plan, a.pl);
     __syncthreads();
@@ -129,7 +141,8 @@ __global__ void __launch_bounds__(256) k_gemv1(GemvArgs a) {
     const int32_t* offs = sp + 2 * G + 1;
     const int total = u1[G];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+    for (int ui = blockIdx.x; ui < total; ui += gridDim.x) {
+        const int u = a.prefetch_shared ? total - 1 - ui : ui;  // shared expert first
         const int g = find_group(u1, G, u);
         const int cnt = cnts[g];
         const int nch = (cnt + kGemvTE - 1) / kGemvTE;
@@ -234,6 +247,8 @@ __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float* ms = reinterpret_cast<float*>(smem_raw);
     const int G = a.pl.G;
+    griddep_wait();  // mid comes from GEMV1
+    griddep_launch_dependents();
     int32_t* sp = reinterpret_cast<int32_t*>(smem_raw + size_t(a.te_cap) * a.inter_max * 4);
     stage_plan(sp, a.plan + a.pl.u2, a.plan, a.pl);
     __syncthreads();
@@ -243,7 +258,8 @@ __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
     const int total = u2[G];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = a.H;
-    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+    for (int ui = blockIdx.x; ui < total; ui += gridDim.x) {
+        const int u = a.prefetch_shared ? total - 1 - ui : ui;  // shared expert first
         const int g = find_group(u2, G, u);
         const int cnt = cnts[g];
         const int nch = (cnt + kGemvTE - 1) / kGemvTE;
@@ -268,6 +284,13 @@ __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
             case 3: gemv2_rows<3>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
             default: gemv2_rows<4>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
         }
+        if (a.prefetch_shared && g == G - 1 && ch == nch - 1 && h0 < H) {
+            // last use of these shared down rows: back to normal L2 priority
+            const int nr = min(4, H - h0);
+            const char* base = reinterpret_cast<const char*>(W.down + size_t(h0) * I);
+            for (int l = lane; l < nr * I * 2 / 128; l += 32)
+                asm volatile("applypriority.global.L2::evict_normal [%0], 128;" ::"l"(base + l * 128));
+        }
     }
 }
 
@@ -282,20 +305,18 @@ hf_status launch_gemv1(const GemvArgs& a, cudaStream_t st) {
     const size_t s1 = gemv1_smem(a.H, a.x_f32 != 0, a.pl.G, a.te_cap);
     if (a.x_f32) {
         HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_gemv1<true>), (int)s1));
-        k_gemv1<true><<<a.grid1, 256, s1, st>>>(a);
+        HF_CUDA(launch_pdl(k_gemv1<true>, dim3(a.grid1), dim3(256), s1, st, a));
     } else {
         HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_gemv1<false>), (int)s1));
-        k_gemv1<false><<<a.grid1, 256, s1, st>>>(a);
+        HF_CUDA(launch_pdl(k_gemv1<false>, dim3(a.grid1), dim3(256), s1, st, a));
     }
-    HF_CUDA(cudaGetLastError());
     return HF_OK;
 }
 
 hf_status launch_gemv2(const GemvArgs& a, cudaStream_t st) {
     const size_t s2 = gemv2_smem(a.inter_max, a.pl.G, a.te_cap);
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_gemv2), (int)s2));
-    k_gemv2<<<a.grid2, 256, s2, st>>>(a);
-    HF_CUDA(cudaGetLastError());
+    HF_CUDA(launch_pdl(k_gemv2, dim3(a.grid2), dim3(256), s2, st, a));
     return HF_OK;
 }
 
@@ -333,6 +354,7 @@ int gemv_grid(int device, bool first, bool xf32, int H, int inter_max, int G, in
 // (moeOut + sharedOut); each thread reads its residual elements before it
 // writes the same elements, so the residual may be the output buffer.
 __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
+    griddep_wait();  // expert outputs of the previous kernel
     const int H4 = a.H >> 2;
     const size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= size_t(a.T) * H4) return;
@@ -386,8 +408,7 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
 hf_status launch_combine(const CombineArgs& a, cudaStream_t st) {
     const size_t n = size_t(a.T) * (a.H >> 2);
     if (n == 0) return HF_OK;
-    k_combine<<<unsigned((n + 255) / 256), 256, 0, st>>>(a);
-    HF_CUDA(cudaGetLastError());
+    HF_CUDA(launch_pdl(k_combine, dim3(unsigned((n + 255) / 256)), dim3(256), 0, st, a));
     return HF_OK;
 }
 

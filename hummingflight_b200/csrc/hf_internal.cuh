@@ -113,7 +113,48 @@ struct RouteArgs {
     int* route_counter;       // zeroed device int: router + routing in one launch (null: two)
 };
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with launch_pdl may start while the previous kernel of the
+// stream still runs; it must call griddep_wait() before it reads anything that
+// kernel writes (the wait returns once that grid has completed and its writes
+// are visible). griddep_launch_dependents() lets the next PDL launch start
+// early (without it, the next kernel starts when this one exits). Without a
+// PDL predecessor griddep_wait() returns at once.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // ------------------------------------------------------------------ device helpers
+// Pulls [p, p + bytes) into L2, the grid's threads striding over 128-byte lines.
+template <bool EVICT_LAST>
+__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
+    const char* c = static_cast<const char*>(p);
+    const size_t lines = bytes / 128, nthr = size_t(gridDim.x) * blockDim.x;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < lines; i += nthr) {
+        if constexpr (EVICT_LAST)
+            asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(c + i * 128));
+        else
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(c + i * 128));
+    }
+}
+
 // Read-only 16-byte loads (weights and activations never change during a
 // kernel); not volatile, so the compiler may batch them for memory-level
 // parallelism.
@@ -241,6 +282,10 @@ struct GemvArgs {
     float* y;               // [(T*k+T) x H] fp32
     const float* resid;     // optional, one group whose positions are tokens (dense MLP):
                             // y = resid + down row; may alias y
+    // the last group (the shared expert) is pulled into L2 by GEMV1 before it
+    // waits for the routing kernel, its units run first (set when its three
+    // matrices fit in L2 with room to spare)
+    int prefetch_shared;
     int grid1, grid2;
     int te_cap;             // most tokens in one chunk: min(T, kGemvTE); sizes the staging
 };

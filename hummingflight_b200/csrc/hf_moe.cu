@@ -248,6 +248,10 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
     // chunks hold at most min(T, kGemvTE) tokens (a segment has at most T
     // slots): stage that many rows, and fit more blocks per SM when T is small
     ga.te_cap = std::max(1, std::min(w.k == 1 ? kGemvTE : w.T, kGemvTE));
+    // every segment on the GEMV (so the shared expert too) and its three
+    // matrices well inside L2: GEMV1 prefetches them during the routing kernel
+    ga.prefetch_shared = !w.maybe_gemm && c->Is > 0 &&
+                         size_t(3) * c->Is * c->H * 2 <= (size_t(96) << 20);
     ga.grid1 = gemv_grid(c->cfg.device, true, w.x_f32 != 0, c->H, c->inter_max, c->G, ga.te_cap);
     ga.grid2 = gemv_grid(c->cfg.device, false, false, c->H, c->inter_max, c->G, ga.te_cap);
     const bool gemv_possible = w.maybe_gemv;

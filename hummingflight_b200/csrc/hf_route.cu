@@ -468,6 +468,7 @@ template <bool XF32, int NPL>
 __global__ void __launch_bounds__(256) k_router_route(RouteArgs a) {
     extern __shared__ __align__(16) uint32_t sm[];
     __shared__ int s_last;
+    griddep_launch_dependents();  // the expert kernel may take its place in the queue now
     router_rows<XF32>(a);
     __threadfence();
     __syncthreads();
