@@ -65,7 +65,7 @@ struct GemmCfg {
     static_assert((2 * kStages + 6 + 2 * kTileQ) * 8 + kTileQ * 4 + 8 <= kBarBytes,
                   "barrier area overflow");
     static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
-    static_assert(!PAIR || (BN % 32 == 0 && kBufs == 2), "pair tiles: BN/2 in 16-row boxes, 2 buffers");
+    static_assert(!PAIR || BN % 32 == 0, "pair tiles: BN/2 in 16-row boxes");
 };
 
 struct TileInfo {
@@ -630,6 +630,9 @@ hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid,
         if (a.bn == 128 && a.mrows == 256)
             return num_b == 1 ? launch_one<2, 1, 128, true>(m, a, grid, st)
                               : launch_one<2, 2, 128, true>(m, a, grid, st);
+        if (a.bn == 256 && a.mrows == 256)  // 128 tokens per CTA; one TMEM buffer
+            return num_b == 1 ? launch_one<2, 1, 256, true>(m, a, grid, st)
+                              : launch_one<2, 2, 256, true>(m, a, grid, st);
         return fail(HF_ERR_ARG, "unsupported pair GEMM tile");
     }
     if (a.which == 1) {

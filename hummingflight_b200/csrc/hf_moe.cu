@@ -171,10 +171,14 @@ int gemv_threshold(const hf_moe_ctx* c, int rows) {
 // 16 tokens (32 KB + 4 KB, 6 stages: as many weight bytes in flight as
 // gate/up, against 9 x 16 KB for 128 x 32 tiles). Prefill (>= 1024 rows):
 // 256 weight rows a tile. Gate/up runs on CTA pairs (cta_group::2, 256
-// intermediate rows x 128 tokens): each SM loads half the activations of a
-// one-CTA tile and the TMEM accumulators stay double-buffered (7 % faster on
-// config 2). Down keeps one CTA with two 128-row accumulators x 128 tokens:
-// the pair's 256 x 256 tile measured 5 % slower there.
+// intermediate rows x 256 tokens, 128 of them loaded by each CTA; 7 % faster
+// than one CTA's 128 x 128 tile on config 2 at 128 tokens per pair). The
+// 256-token pair tile fills TMEM with one accumulator buffer, but each weight
+// stage feeds twice the tokens, so segments and the shared expert with more
+// than 128 tokens re-read their weight tiles half as often (config 2 gate/up
+// 2.80 -> 2.64 ms against 128-token pair tiles). Down keeps one CTA with two
+// 128-row accumulators x 128 tokens: the pair's 256 x 256 tile measured 5 %
+// slower there.
 void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
     ra.gemm_m1 = 128;
     ra.gemm_pair = 0;
@@ -189,8 +193,12 @@ void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
         ra.gemm_bn1 = ra.gemm_bn2 = 128;
         ra.gemm_m2 = 128;
     } else {  // prefill: 256 weight rows per tile
+        static const int pair_bn = [] {  // tuning knob: HF_GEMM_PAIR_BN = 128 or 256
+            const char* e = std::getenv("HF_GEMM_PAIR_BN");
+            return (e && std::atoi(e) == 128) ? 128 : 256;
+        }();
         ra.gemm_pair = 1;  // gate/up on CTA pairs
-        ra.gemm_bn1 = 128;
+        ra.gemm_bn1 = pair_bn;
         ra.gemm_m1 = 256;
         ra.gemm_bn2 = 128;  // down on one CTA (two 128-row accumulators)
         ra.gemm_m2 = 256;
