@@ -115,9 +115,9 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p
         t.rowA1 = t.shared ? t.m0 : base + Ig + t.m0;
         t.mvalid = Ig - t.m0;
         t.kb1 = (a.H + 63) / 64;
-    } else {  // down rows; a second accumulator takes the next 128 rows
+    } else {  // down rows; a second accumulator takes the next 128 rows (256 on a pair)
         t.rowA0 = t.shared ? t.m0 : g * 3 * a.H + 2 * a.H + t.m0;
-        t.rowA1 = t.rowA0 + 128;
+        t.rowA1 = t.rowA0 + (a.pair ? 256 : 128);
         t.mvalid = a.H - t.m0;
         t.kb1 = (Ig + 63) / 64;
     }
@@ -420,7 +420,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             const uint32_t ta = tmem_base + (uint32_t(q * 32) << 16) + acc * C::kAccCols;
             const int rr = r + (PAIR ? row_off : 0);  // weight row inside the tile
             const bool rv = rr < t.mvalid;
-            const bool rv1 = !PAIR && r + 128 < t.mvalid;  // second down row block (one CTA)
+            // second down row block: the next 128 rows on one CTA; on a pair (a
+            // 512-row tile) the second 256-row MMA block, this CTA's half of it
+            constexpr int kRow1 = PAIR ? 256 : 128;
+            const bool rv1 = rr + kRow1 < t.mvalid;
             // columns per TMEM load: 32, or 16 for 16-token tiles (an x32 load
             // would reach past the allocated columns)
             constexpr int CW = BN < 32 ? BN : 32;
@@ -457,7 +460,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                             const size_t pos = size_t(t.seg + t.n0 + col);
                             float* yr = a.y + t.yoff + pos * a.H + t.m0 + rr;
                             if (rv) yr[0] = __uint_as_float(v0[j]);
-                            if (NUM_A == 2 && rv1) yr[128] = __uint_as_float(v1[j]);
+                            if (NUM_A == 2 && rv1) yr[kRow1] = __uint_as_float(v1[j]);
                         }
                     }
                 } else {  // residual block (dense MLP): y = resid + down row; the thread
@@ -470,7 +473,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                             const int col = c0 + j0 + j;
                             const size_t yi = size_t(t.seg + t.n0 + col) * a.H + t.m0 + rr;
                             q0[j] = (col < t.n && rv) ? a.resid[yi] : 0.f;
-                            q1[j] = (NUM_A == 2 && col < t.n && rv1) ? a.resid[yi + 128] : 0.f;
+                            q1[j] = (NUM_A == 2 && col < t.n && rv1) ? a.resid[yi + kRow1] : 0.f;
                         }
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
@@ -479,7 +482,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                                 float* yr = a.y + size_t(t.seg + t.n0 + col) * a.H + t.m0 + rr;
                                 if (rv) yr[0] = __fadd_rn(q0[j], __uint_as_float(v0[j0 + j]));
                                 if (NUM_A == 2 && rv1)
-                                    yr[128] = __fadd_rn(q1[j], __uint_as_float(v1[j0 + j]));
+                                    yr[kRow1] = __fadd_rn(q1[j], __uint_as_float(v1[j0 + j]));
                             }
                         }
                     }
@@ -626,6 +629,9 @@ static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cuda
 }
 
 hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid, cudaStream_t st) {
+    if (a.pair && a.which == 2 && a.mrows == 512 && a.bn == 128 && num_b == 2)
+        // prefill down: 512-row tiles on CTA pairs (two 256-row MMA blocks)
+        return launch_one<2, 2, 128, true>(m, a, grid, st);
     if (a.pair && a.which == 1) {  // prefill gate/up: 256-row tiles on CTA pairs
         if (a.bn == 128 && a.mrows == 256)
             return num_b == 1 ? launch_one<2, 1, 128, true>(m, a, grid, st)

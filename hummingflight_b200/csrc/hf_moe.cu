@@ -178,7 +178,8 @@ int gemv_threshold(const hf_moe_ctx* c, int rows) {
 // than 128 tokens re-read their weight tiles half as often (config 2 gate/up
 // 2.80 -> 2.64 ms against 128-token pair tiles). Down keeps one CTA with two
 // 128-row accumulators x 128 tokens: the pair's 256 x 256 tile measured 5 %
-// slower there.
+// slower, a pair with two 256-row blocks (512 rows x 128 tokens, half the
+// token-operand loads per SM) the same (2.17 vs 2.14 ms on config 2).
 void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
     ra.gemm_m1 = 128;
     ra.gemm_pair = 0;
@@ -197,11 +198,15 @@ void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
             const char* e = std::getenv("HF_GEMM_PAIR_BN");
             return (e && std::atoi(e) == 128) ? 128 : 256;
         }();
+        static const int pair_down = [] {  // tuning knob: HF_GEMM_PAIR_DOWN = 0 or 1
+            const char* e = std::getenv("HF_GEMM_PAIR_DOWN");
+            return (e && std::atoi(e) == 1) ? 1 : 0;
+        }();
         ra.gemm_pair = 1;  // gate/up on CTA pairs
         ra.gemm_bn1 = pair_bn;
         ra.gemm_m1 = 256;
-        ra.gemm_bn2 = 128;  // down on one CTA (two 128-row accumulators)
-        ra.gemm_m2 = 256;
+        ra.gemm_bn2 = 128;  // down: two accumulators x 128 tokens, 256 rows on one CTA
+        ra.gemm_m2 = pair_down ? 512 : 256;  // or 512 rows on a CTA pair
     }
 }
 
