@@ -171,10 +171,21 @@ def run_reference(args, wl):
             "impl": "reference",
             "config": {"workload": wl.name, "tokens_per_step": ntok, "layers": 1},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
-                             "sample": sample},
+                             "cpu": cpu_model(), "nproc": os.cpu_count(), "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def cpu_baseline(wl, budget_s):
@@ -190,6 +201,7 @@ def cpu_baseline(wl, budget_s):
         passes += 1
     R.close()
     return {"value": n / t, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "cpu": cpu_model(), "nproc": os.cpu_count(),
             "sample": f"{passes} passes over the first {x.shape[0]} tokens of {wl.name} "
                       f"({t:.1f} s of CPU time), reference AVX2 build, per-token moeLayer"}
 
@@ -398,6 +410,9 @@ def main():
                          "frac": (achieved / (tflops_peak if tensor_bound else hbm))
                          if achieved else None,
                          "peak_kind": peak_kind, "traffic": traffic,
+                         # against the nominal 8 TB/s HBM3e and 2.25 PFLOP/s dense BF16
+                         "frac_nominal": (achieved / (2250.0 if tensor_bound else 8000.0))
+                         if achieved else None,
                          "algorithmic_bytes_per_launch": alg,
                          "algorithmic_flops_per_launch": flops,
                          "launch_ms": per_launch_ms},
