@@ -215,45 +215,59 @@ __device__ __forceinline__ void topk_warp(const float* row, int planes, size_t p
         }
     }
     // k (+1 for the margin) rounds of a warp argmax; lane r keeps the r-th
-    // pick. The round loop stays rolled: this code runs once per token, so
-    // its instruction footprint (cold at every launch) costs more than the
-    // loop overhead.
-    uint32_t taken = 0;
+    // pick. Scores become order-preserving 32-bit keys (-0 as +0; NaN and
+    // absent experts 0, below every real score), so a round is one local
+    // scan, one redux.sync max and a ballot; equal scores on several lanes
+    // (rare) take the lowest expert id with a redux.sync min. A picked key is
+    // cleared to 0. The round loop stays rolled: this code runs once per
+    // token, so its instruction footprint (cold at every launch) costs more
+    // than the loop overhead.
+    uint32_t key[NPL];
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+        uint32_t b = __float_as_uint(v[j]);
+        if (b == 0x80000000u) b = 0u;
+        key[j] = (j * 32 + lane < E && v[j] == v[j]) ? ((b & 0x80000000u) ? ~b : (b | 0x80000000u))
+                                                      : 0u;
+    }
     int my_i = 0;
     float my_s = 0.0f;
     float kth = 0.0f, next = -INFINITY;
     const int rounds = (k < E) ? k + 1 : k;
 #pragma unroll 1
     for (int r = 0; r < rounds; ++r) {
-        float bv = -INFINITY, bs = 0.0f;
-        int bi = 0x7fffffff;
+        uint32_t bk = 0u;
+        int bj = 0;
+        float bs = 0.0f;
 #pragma unroll
-        for (int j = 0; j < NPL; ++j) {
-            const int e = j * 32 + lane;
-            if (!((taken >> j) & 1u) && e < E && (v[j] > bv || (v[j] == bv && e < bi))) {
-                bv = v[j];
-                bi = e;
+        for (int j = 0; j < NPL; ++j)
+            if (key[j] > bk) {  // strict: the lowest expert id of this lane on equal keys
+                bk = key[j];
+                bj = j;
                 bs = s[j];
             }
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+        const unsigned cand = __ballot_sync(0xffffffffu, bk == mk);
+        int win;
+        if ((cand & (cand - 1u)) == 0u) {
+            win = __ffs(cand) - 1;
+        } else {
+            const int id = ((cand >> lane) & 1u) ? bj * 32 + lane : 0x7fffffff;
+            win = __reduce_min_sync(0xffffffffu, id) & 31;
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-                bs = os;
-            }
-        }
+        const int wj = __shfl_sync(0xffffffffu, bj, win);
+        const float ws = __shfl_sync(0xffffffffu, bs, win);
+        const float bv = __uint_as_float((mk & 0x80000000u) ? (mk & 0x7fffffffu) : ~mk);
         if (r < k) {
             if (lane == r) {
-                my_i = bi;
-                my_s = bs;
+                my_i = wj * 32 + win;
+                my_s = ws;
             }
             kth = bv;
-            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+            if (lane == win)
+#pragma unroll
+                for (int j = 0; j < NPL; ++j)
+                    if (j == wj) key[j] = 0u;
         } else {
             next = bv;
         }
