@@ -457,7 +457,7 @@ hf_status upload(int device, const std::vector<Copy>& copies) {
         S.threads = reader_threads();
         for (int i = 0; i < S.threads * kSlotsPerThread; ++i) {
             void* p = nullptr;
-            if (cudaHostAlloc(&p, kChunk, cudaHostAllocDefault) != cudaSuccess) {
+            if (cudaHostAlloc(&p, kChunk, cudaHostAllocPortable) != cudaSuccess) {
                 cudaGetLastError();
                 for (void* q : S.bufs) cudaFreeHost(q);
                 S.bufs.clear();
