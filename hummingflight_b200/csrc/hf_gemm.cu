@@ -84,6 +84,9 @@ struct PlanView {
     const int32_t* off;
 };
 
+// PAIR: the kernel runs on CTA pairs (a down tile then spans 512 rows). This is
+// the kernel's own shape, not GemmArgs::pair, which marks the pass.
+template <bool PAIR>
 __device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p, int u,
                                             TileInfo& t) {
     int ks = 0;
@@ -117,7 +120,7 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p
         t.kb1 = (a.H + 63) / 64;
     } else {  // down rows; a second accumulator takes the next 128 rows (256 on a pair)
         t.rowA0 = t.shared ? t.m0 : g * 3 * a.H + 2 * a.H + t.m0;
-        t.rowA1 = t.rowA0 + (a.pair ? 256 : 128);
+        t.rowA1 = t.rowA0 + (PAIR ? 256 : 128);
         t.mvalid = a.H - t.m0;
         t.kb1 = (Ig + 63) / 64;
     }
@@ -274,7 +277,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             if (u >= total) break;
             const int u_next = leader ? atomicAdd(a.sched, 1) : 0;
             TileInfo t;
-            decode_tile(a, pv, u, t);
+            decode_tile<PAIR>(a, pv, u, t);
             u = u_next;
             // token rows of B this CTA loads: all of the tile (one CTA) or its
             // half of the MMA's N (pair; N rounded up to 32)
@@ -343,7 +346,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             ++qi;
             if (u >= total) break;
             TileInfo t;
-            decode_tile(a, pv, u, t);
+            decode_tile<PAIR>(a, pv, u, t);
             const uint32_t acc = lt % C::kBufs, aph = (lt / C::kBufs) & 1;
             if (!wait(&tempty[acc], aph ^ 1)) {
                 ok = false;
@@ -413,7 +416,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             ++qi;
             if (u >= total) break;
             TileInfo t;
-            decode_tile(a, pv, u, t);
+            decode_tile<PAIR>(a, pv, u, t);
             const uint32_t acc = lt % C::kBufs, aph = (lt / C::kBufs) & 1;
             if (!wait(&tfull[acc], aph)) break;
             tc_fence_after();

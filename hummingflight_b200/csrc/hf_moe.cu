@@ -179,7 +179,7 @@ int gemv_threshold(const hf_moe_ctx* c, int rows) {
 // 2.80 -> 2.64 ms against 128-token pair tiles). Down keeps one CTA with two
 // 128-row accumulators x 128 tokens: the pair's 256 x 256 tile measured 5 %
 // slower, a pair with two 256-row blocks (512 rows x 128 tokens, half the
-// token-operand loads per SM) the same (2.17 vs 2.14 ms on config 2).
+// token-operand loads per SM) the same (config 2: 4.87 vs 4.86 ms a step).
 void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
     ra.gemm_m1 = 128;
     ra.gemm_pair = 0;
