@@ -28,6 +28,8 @@
 #include <map>
 #include <mutex>
 
+#include <cuda_bf16.h>
+
 #include "hf_internal.cuh"
 #include "hf_sm100.cuh"
 
@@ -35,7 +37,11 @@ namespace hf {
 
 using namespace sm100;
 
-constexpr int kGemmThreads = 192;
+// warp 0: TMA producer, warp 1: MMA issuer and TMEM owner, warps 2-9: epilogue
+// (two per TMEM lane quadrant, alternating 32-column chunks: the SwiGLU of a
+// 256-token tile kept four warps busy long enough to stall the next tile's MMAs)
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kBoxRowsB = 16;
 constexpr uint32_t kTileABytes = 128 * 64 * 2;  // 128 rows x 64 bf16
 constexpr uint64_t kDrainNs = 500ull * 1000 * 1000;
@@ -207,14 +213,15 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], PAIR ? 8 : 4);  // epilogue warps of this CTA (and the peer)
+            // epilogue warps of this CTA (and the peer)
+            mbar_init(&tempty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);
         }
         mbar_init(final_bar, 1);
         mbar_init(stall_bar, 1);
         for (int q = 0; q < kTileQ; ++q) {
             mbar_init(&tq_full[q], 1);
             // MMA thread + 4 epilogue warps (+ the peer's producer and 4 epilogue warps)
-            mbar_init(&tq_empty[q], PAIR ? 10 : 5);
+            mbar_init(&tq_empty[q], PAIR ? 2 * (1 + kEpiWarps) : 1 + kEpiWarps);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -430,7 +437,8 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             // columns per TMEM load: 32, or 16 for 16-token tiles (an x32 load
             // would reach past the allocated columns)
             constexpr int CW = BN < 32 ? BN : 32;
-            for (int c0 = 0; c0 < t.n; c0 += CW) {
+            // the two warps of a quadrant take alternate column chunks
+            for (int c0 = ((warp - 2) / 4) * CW; c0 < t.n; c0 += 2 * CW) {
                 uint32_t v0[CW], v1[CW];
                 if constexpr (CW == 16) {
                     tmem_ld16(ta + c0, v0);
@@ -442,16 +450,19 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                 tmem_ld_wait();
                 if (NUM_A == 2 && a.which == 1) {  // gate/up pair -> SwiGLU -> hi/lo planes
                     if (rv) {
+                        // column c0 of this row in both planes; one row of mid per column
+                        const size_t o0 = size_t(t.seg + t.n0 + c0) * a.Imax + t.m0 + rr;
+                        __nv_bfloat16* ph = reinterpret_cast<__nv_bfloat16*>(a.mid_hi) + o0;
+                        __nv_bfloat16* pl = reinterpret_cast<__nv_bfloat16*>(a.mid_lo) + o0;
 #pragma unroll
                         for (int j = 0; j < CW; ++j) {
-                            const int col = c0 + j;
-                            if (col < t.n) {
-                                const size_t pos = size_t(t.seg + t.n0 + col);
-                                const float m = swiglu(__uint_as_float(v0[j]), __uint_as_float(v1[j]));
-                                const uint16_t hi = f32_to_bf16_rne(m);
-                                const uint16_t lo = f32_to_bf16_rne(__fsub_rn(m, bf16_to_f32(hi)));
-                                a.mid_hi[pos * a.Imax + t.m0 + rr] = hi;
-                                a.mid_lo[pos * a.Imax + t.m0 + rr] = lo;
+                            if (c0 + j < t.n) {
+                                const float m =
+                                    swiglu_fast(__uint_as_float(v0[j]), __uint_as_float(v1[j]));
+                                const __nv_bfloat16 hi = __float2bfloat16_rn(m);
+                                ph[size_t(j) * a.Imax] = hi;
+                                pl[size_t(j) * a.Imax] =
+                                    __float2bfloat16_rn(__fsub_rn(m, __bfloat162float(hi)));
                             }
                         }
                     }
