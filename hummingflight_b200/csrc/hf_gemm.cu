@@ -643,9 +643,11 @@ static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cuda
 }
 
 hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid, cudaStream_t st) {
-    if (a.pair && a.which == 2 && a.mrows == 512 && a.bn == 128 && num_b == 2)
+    if (a.pair && a.which == 2 && a.mrows == 512 && num_b == 2) {
         // prefill down: 512-row tiles on CTA pairs (two 256-row MMA blocks)
-        return launch_one<2, 2, 128, true>(m, a, grid, st);
+        if (a.bn == 128) return launch_one<2, 2, 128, true>(m, a, grid, st);
+        if (a.bn == 256) return launch_one<2, 2, 256, true>(m, a, grid, st);
+    }
     if (a.pair && a.which == 1) {  // prefill gate/up: 256-row tiles on CTA pairs
         if (a.bn == 128 && a.mrows == 256)
             return num_b == 1 ? launch_one<2, 1, 128, true>(m, a, grid, st)

@@ -176,10 +176,13 @@ int gemv_threshold(const hf_moe_ctx* c, int rows) {
 // 256-token pair tile fills TMEM with one accumulator buffer, but each weight
 // stage feeds twice the tokens, so segments and the shared expert with more
 // than 128 tokens re-read their weight tiles half as often (config 2 gate/up
-// 2.80 -> 2.64 ms against 128-token pair tiles). Down keeps one CTA with two
-// 128-row accumulators x 128 tokens: the pair's 256 x 256 tile measured 5 %
-// slower, a pair with two 256-row blocks (512 rows x 128 tokens, half the
-// token-operand loads per SM) the same (config 2: 4.87 vs 4.86 ms a step).
+// 2.80 -> 2.64 ms against 128-token pair tiles). Down runs on CTA pairs too:
+// two 256-row MMA blocks x 256 tokens (512 x 256 a pair, one TMEM buffer; the
+// down epilogue only stores): each MMA instruction does four times the work of
+// a one-CTA 128 x 128 one, and the down kernel spends most of its time issuing
+// MMAs (the hi + lo pass doubles them) -- config 2 down 2.41 -> 2.01 ms. One
+// CTA with two 128-row accumulators x 128 tokens (HF_GEMM_PAIR_DOWN=0) and the
+// pair with 128 tokens (=1) measured the same as each other.
 void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
     ra.gemm_m1 = 128;
     ra.gemm_pair = 0;
@@ -198,15 +201,18 @@ void set_gemm_tiles(int bn_override, int rows, RouteArgs& ra) {
             const char* e = std::getenv("HF_GEMM_PAIR_BN");
             return (e && std::atoi(e) == 128) ? 128 : 256;
         }();
-        static const int pair_down = [] {  // tuning knob: HF_GEMM_PAIR_DOWN = 0 or 1
+        static const int pair_down = [] {  // tuning knob: HF_GEMM_PAIR_DOWN = 0, 1 or 2
             const char* e = std::getenv("HF_GEMM_PAIR_DOWN");
-            return (e && std::atoi(e) == 1) ? 1 : 0;
+            const int v = e ? std::atoi(e) : 2;
+            return (v == 0 || v == 1) ? v : 2;
         }();
         ra.gemm_pair = 1;  // gate/up on CTA pairs
         ra.gemm_bn1 = pair_bn;
         ra.gemm_m1 = 256;
-        ra.gemm_bn2 = 128;  // down: two accumulators x 128 tokens, 256 rows on one CTA
-        ra.gemm_m2 = pair_down ? 512 : 256;  // or 512 rows on a CTA pair
+        // down: 512 rows x 256 tokens on a CTA pair (or x 128 tokens; or 256 rows
+        // x 128 tokens on one CTA)
+        ra.gemm_bn2 = pair_down == 2 ? 256 : 128;
+        ra.gemm_m2 = pair_down ? 512 : 256;
     }
 }
 
