@@ -34,6 +34,8 @@ def main():
     cases = [("small_gemm", LayerShape(256, 16, 4, 128, 192, 2.5, True), 48, "gemm", 41),
              ("small_auto", LayerShape(256, 16, 4, 128, 192, 2.5, True), 40, "auto", 42),
              ("glm_auto", GLM, 16, "auto", 0),
+             # 1200 rows: prefill tiles (CTA pairs) on both sides
+             ("small_prefill", LayerShape(256, 16, 4, 128, 192, 2.5, True), 600, "auto", 43),
              # slabs above the decode-exchange size: counts sized on the host
              ("glm_sized", GLM, 256, "auto", 3)]
     results = {}
