@@ -6,6 +6,7 @@
 // seeds and distributions) and records what the reference's functions return:
 //   gemv    src/self_test.cpp:73-103     (M=8, K=33, mt19937(42), alpha/beta)
 //   topk    src/self_test.cpp:180-200    (8 scores, k=3, bias -10 on expert 2)
+//   bf16    src/self_test.cpp:53-70      (its values and rounding edges, BFloat16::fromF32)
 //   rmsnorm src/self_test.cpp:125-138    (n=128, mt19937(3), eps 1e-5, no weight)
 //   expert  compute/cuda_backend.cpp:497-520 (64x32 case, mt19937(1)); the
 //           expected output is the CPU forward's math (expertFFNRaw,
@@ -90,6 +91,25 @@ int main() {
             std::snprintf(nm, sizeof nm, "%s_w", c.name);
             put_f32(nm, r.weights, r.k);
         }
+    }
+    {  // self_test.cpp:53-70 (BFloat16): its values plus rounding edges (ties to
+       // even both ways, carries into the exponent, subnormals, the largest
+       // finite, infinities), through the reference's BFloat16::fromF32
+        const uint32_t edge[] = {0x3F800000u, 0x40000000u, 0xBFC00000u, 0x3F000000u, 0x00000000u,
+                                 0x80000000u, 0x3DCCCCCDu, 0x3E99999Au, 0x3EAAAAABu, 0x42F6E979u,
+                                 0xC476E9DBu, 0x3A83126Fu, 0x447A0000u, 0x3F808000u, 0x3F818000u,
+                                 0x3F80C000u, 0x3F7FFFFFu, 0x7F7FFFFFu, 0x00000001u, 0x00008000u,
+                                 0x00018000u, 0x807FFFFFu, 0x7F800000u, 0xFF800000u, 0x477FFFFFu,
+                                 0xBF808001u};
+        const size_t n = sizeof(edge) / sizeof(edge[0]);
+        std::vector<float> in(n);
+        std::vector<BFloat16> out(n);
+        for (size_t i = 0; i < n; ++i) {
+            std::memcpy(&in[i], &edge[i], 4);
+            out[i] = BFloat16::fromF32(in[i]);
+        }
+        put_f32("bf16_in", in.data(), n);
+        put_u16("bf16_out", out.data(), n);
     }
     {  // self_test.cpp:125-138: the RMSNorm the reference checks GLMForward::rmsNorm's
        // math with (n = 128, mt19937(3), U(-1, 1), eps = 1e-5, no weight)

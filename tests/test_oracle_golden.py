@@ -2,7 +2,7 @@
 
 tests/golden/ holds vectors produced by the reference's unmodified
 compute/cpu_kernels.cpp and compute/moe_router.h (tests/golden/make_golden.py):
-its self-test inputs (src/self_test.cpp:73-103, :125-138, :180-200), its expert-FFN
+its self-test inputs (src/self_test.cpp:53-70, :73-103, :125-138, :180-200), its expert-FFN
 parity case (compute/cuda_backend.cpp:497-520) and GLMForward::moeLayer
 (model/glm_forward.cpp:509-661) on seeded layers. The oracle restates the
 scalar Linux build, so it must match that build bit for bit.
@@ -27,7 +27,7 @@ def kat(flavour="scalar"):
         a = np.array(v, dtype=np.int64)
         if k.endswith("_idx"):
             out[k] = a.astype(np.int32)
-        elif k in ("gemv_A", "expert_w"):
+        elif k in ("gemv_A", "expert_w", "bf16_out"):
             out[k] = a.astype(np.uint16)
         else:
             out[k] = a.astype(np.uint32).view(np.float32)
@@ -49,6 +49,17 @@ def test_gemv_avx2_build_within_selftest_tolerance():
     k = kat("avx2")
     y = O.gemv_bf16_f32(k["gemv_A"].reshape(8, 33), k["gemv_x"])
     assert np.abs(y - k["gemv_y"]).max() < 1e-3
+
+
+def test_bf16_rounding_known_answers():
+    """BFloat16::fromF32 (dtype_bf16.h:27-33) on self_test.cpp:53-70's values and
+    the rounding edges: ties to even both ways, exponent carries, subnormals,
+    the largest finite value, infinities."""
+    k = kat("scalar")
+    assert np.array_equal(O.f32_to_bf16(k["bf16_in"]), k["bf16_out"])
+    # and the widening back is exact
+    back = O.bf16_to_f32(k["bf16_out"])
+    assert np.array_equal(O.f32_to_bf16(back), k["bf16_out"])
 
 
 def test_rmsnorm_selftest_vector_bit_exact():
