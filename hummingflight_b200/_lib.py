@@ -115,6 +115,7 @@ SIGNATURES = {
     "hf_moe_load_safetensors": (c_int, [c_vp, c_int, c_int, ctypes.POINTER(ctypes.c_char_p), c_int,
                                         ctypes.POINTER(HfIngestStats)]),
     "hf_ingest_release_staging": (c_int, []),
+    "hf_st_layer_shards": (c_int, [ctypes.c_char_p, c_int, c_vp, c_size, ctypes.POINTER(c_int)]),
 }
 
 _lib = None

@@ -21,6 +21,9 @@
 
 #include <algorithm>
 #include <atomic>
+#include <filesystem>
+#include <fstream>
+#include <set>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -638,6 +641,56 @@ hf_status hf_ingest_release_staging(void) {
     std::lock_guard<std::mutex> lk(S.mu);
     for (void* p : S.bufs) cudaFreeHost(p);
     S.bufs.clear();
+    return HF_OK;
+}
+
+hf_status hf_st_layer_shards(const char* dir, int model_layer, char* buf, size_t buf_bytes,
+                            int* num_shards) {
+    namespace fs = std::filesystem;
+    if (!dir || !num_shards) return fail(HF_ERR_ARG, "hf_st_layer_shards: null argument");
+    *num_shards = 0;
+    std::error_code ec;
+    std::vector<std::string> shards;
+    for (fs::directory_iterator it(dir, ec), end; !ec && it != end; it.increment(ec))
+        if (it->path().extension() == ".safetensors") shards.push_back(it->path().string());
+    if (ec) return fail(HF_ERR_ARG, std::string("hf_st_layer_shards: cannot list ") + dir);
+    std::sort(shards.begin(), shards.end());
+    if (shards.empty())
+        return fail(HF_ERR_ARG, std::string("hf_st_layer_shards: no .safetensors files in ") + dir);
+    std::vector<std::string> out = shards;
+    // weight_map of the index, when present and well formed (weight_index.cpp:31-49)
+    std::ifstream f(fs::path(dir) / "model.safetensors.index.json", std::ios::binary);
+    if (f) {
+        const std::string txt((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+        JVal root;
+        const JVal* wm = nullptr;
+        if (JsonReader(txt.data(), txt.size()).parse(root) && root.kind == JVal::Obj)
+            for (const auto& kv : root.obj)
+                if (kv.first == "weight_map" && kv.second.kind == JVal::Obj) wm = &kv.second;
+        if (wm) {
+            const std::string pre = "model.layers." + std::to_string(model_layer) + ".mlp.";
+            std::set<std::string> names;
+            for (const auto& kv : wm->obj)
+                if (kv.second.kind == JVal::Str && kv.first.compare(0, pre.size(), pre) == 0)
+                    names.insert(kv.second.str);
+            out.clear();
+            for (const std::string& n : names) {
+                const std::string p = (fs::path(dir) / n).string();
+                if (!std::binary_search(shards.begin(), shards.end(), p))
+                    return fail(HF_ERR_ARG, "hf_st_layer_shards: the index names a missing shard: " + n);
+                out.push_back(p);
+            }
+        }
+    }
+    size_t need = 0;
+    for (const std::string& p : out) need += p.size() + 1;
+    *num_shards = int(out.size());
+    if (!buf || buf_bytes < need) return fail(HF_ERR_ARG, "hf_st_layer_shards: buffer too small");
+    char* w = buf;
+    for (const std::string& p : out) {
+        std::memcpy(w, p.c_str(), p.size() + 1);
+        w += p.size() + 1;
+    }
     return HF_OK;
 }
 

@@ -139,6 +139,12 @@ class MoELayer:
              ctypes.byref(st))
         return {n: getattr(st, n) for n, _ in HfIngestStats._fields_}
 
+    def load_checkpoint_layer(self, layer: int, checkpoint_dir: str, model_layer: int):
+        """load_safetensors over the shards of `checkpoint_dir` that hold model
+        layer `model_layer` (see hummingflight_b200.safetensors.layer_shards)."""
+        from .safetensors import layer_shards
+        return self.load_safetensors(layer, layer_shards(checkpoint_dir, model_layer), model_layer)
+
     def expert_device_ptr(self, layer: int, eid: int) -> int:
         p = ctypes.c_void_p()
         call("hf_moe_expert_device_ptr", self._h, layer, eid, ctypes.byref(p))

@@ -111,9 +111,29 @@ class SafeTensors:
             pass
 
 
+def layer_shards(checkpoint_dir: str, model_layer: int) -> List[str]:
+    """The shards of a checkpoint directory holding model layer `model_layer`'s
+    MLP tensors (hf_st_layer_shards: the index's weight_map when present, else
+    every *.safetensors file, sorted)."""
+    n = ctypes.c_int()
+    size = 1 << 16
+    while True:
+        buf = ctypes.create_string_buffer(size)
+        st = _lib.lib().hf_st_layer_shards(checkpoint_dir.encode(), model_layer, buf, size,
+                                           ctypes.byref(n))
+        if st == _lib.HF_OK:
+            break
+        if n.value and size < (1 << 26):  # the buffer was too small: retry larger
+            size *= 8
+            continue
+        _lib.check(st, "hf_st_layer_shards")
+    parts = buf.raw.split(b"\0")[:n.value]
+    return [p.decode() for p in parts]
+
+
 def shard_paths_arg(paths: Sequence[str]):
     arr = (ctypes.c_char_p * len(paths))(*[p.encode() for p in paths])
     return arr
 
 
-__all__ = ["SafeTensors", "TensorInfo", "options", "shard_paths_arg"]
+__all__ = ["SafeTensors", "TensorInfo", "options", "layer_shards", "shard_paths_arg"]

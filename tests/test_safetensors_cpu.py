@@ -102,3 +102,44 @@ def test_package_writer_round_trip(tmp_path):
         assert np.array_equal(f.read("c.weight"), c)
     with pytest.raises(ValueError):
         write_file(str(tmp_path / "bad.safetensors"), [("x", "BF16", (3,), a)])
+
+
+def test_layer_shards_follow_the_index(tmp_path):
+    """hf_st_layer_shards: every *.safetensors file (sorted) without an index;
+    with model.safetensors.index.json only the shards its weight_map names for
+    model.layers.<L>.mlp.* (WeightIndex::build, weight_index.cpp:79-130)."""
+    import json as js
+    from hummingflight_b200._lib import HfError
+    S = st()
+    for n in ("model-00002-of-00003.safetensors", "model-00001-of-00003.safetensors",
+              "model-00003-of-00003.safetensors", "notes.txt"):
+        (tmp_path / n).write_bytes(b"")
+    all3 = [str(tmp_path / f"model-0000{i}-of-00003.safetensors") for i in (1, 2, 3)]
+    assert S.layer_shards(str(tmp_path), 3) == all3
+    import ctypes
+    from hummingflight_b200 import _lib
+    n = ctypes.c_int()
+    small = ctypes.create_string_buffer(8)
+    assert _lib.lib().hf_st_layer_shards(str(tmp_path).encode(), 3, small, 8,
+                                         ctypes.byref(n)) == _lib.HF_ERR_ARG
+    assert n.value == 3                               # the count even when the buffer is short
+    wm = {"model.layers.3.mlp.gate.weight": "model-00002-of-00003.safetensors",
+          "model.layers.3.mlp.experts.0.up_proj.weight": "model-00003-of-00003.safetensors",
+          "model.layers.3.mlp.experts.1.up_proj.weight": "model-00002-of-00003.safetensors",
+          "model.layers.3.self_attn.o_proj.weight": "model-00001-of-00003.safetensors",
+          "model.layers.30.mlp.gate.weight": "model-00001-of-00003.safetensors"}
+    idx = tmp_path / "model.safetensors.index.json"
+    idx.write_text(js.dumps({"metadata": {"total_size": 1}, "weight_map": wm}))
+    assert S.layer_shards(str(tmp_path), 3) == all3[1:]
+    assert S.layer_shards(str(tmp_path), 30) == all3[:1]
+    assert S.layer_shards(str(tmp_path), 7) == []
+    wm["model.layers.7.mlp.gate.weight"] = "model-00009-of-00009.safetensors"
+    idx.write_text(js.dumps({"weight_map": wm}))
+    with pytest.raises(HfError, match="missing shard"):
+        S.layer_shards(str(tmp_path), 7)
+    idx.write_text("{not json")                      # unreadable index: every shard
+    assert S.layer_shards(str(tmp_path), 3) == all3
+    empty = tmp_path / "empty"
+    empty.mkdir()
+    with pytest.raises(HfError, match="no .safetensors"):
+        S.layer_shards(str(empty), 3)
