@@ -157,3 +157,20 @@ def test_set_expert_parts_matches_set_expert():
     a = _wrap(A.expert_device_ptr(0, 3), 3 * n).clone()
     assert np.array_equal(a.cpu().numpy().view(np.uint16), g)
     A.close()
+
+
+def test_load_checkpoint_layer_from_directory(shards):
+    """The shards of the checkpoint directory (no index there: both files) hold
+    the whole layer; the result is the synthesized layer's bytes."""
+    need_gpu()
+    M = moe()
+    paths, d = shards
+    from hummingflight_b200.safetensors import layer_shards
+    assert layer_shards(str(d), MODEL_LAYER) == sorted(paths)
+    L = M.MoELayer(SMALL, 1, 8, 0, "auto")
+    st = L.load_checkpoint_layer(0, str(d), MODEL_LAYER)
+    assert st["experts"] == SMALL.num_experts and st["has_bias"] == 1
+    g = O.gen_expert(WSEED, 0, 5, SMALL.hidden, SMALL.inter)
+    got = _wrap(L.expert_device_ptr(0, 5), g.size).clone().cpu().numpy().view(np.uint16)
+    assert np.array_equal(got, g)
+    L.close()
