@@ -5,12 +5,20 @@ hummingflight_b200/libhf_moe.so.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
-One JSON line on rank 0. `value` is MoE-layer tokens/s over the whole job
-(tokens x layers / device time, max over ranks) with inputs resident in HBM;
-`e2e` is the same metric through hf_moe_forward_host (pinned host buffers,
-H2D of x and D2H of the output inside the timed region). Workload: config 1
-by default (decode, 64 tokens, one layer); weights and activations are the
-seeded synthetic tensors of hummingflight_b200/configs.py, generated in HBM.
+One JSON line on rank 0. The workload is config 3 by default: a stack of 8
+GLM MoE layers (seeds 10-17, 155 GB of BF16 weights resident in HBM), 16384
+tokens a step, expert-parallel over the ranks (E/N experts per GPU, the
+global batch split evenly: strong scaling). `value` is MoE-layer tokens/s of
+the whole job (tokens x layers / device time, max over ranks) with inputs
+resident in HBM; `e2e` is the same metric through hf_moe_forward_host
+(pinned host buffers, H2D of x and D2H of the output inside the timed
+region). On one GPU the same run then measures configs 2 (prefill, 4096
+tokens) and 0 (batch-1 decode) on one layer and reports them under
+`sub_results`, each with its own roofline.
+
+Inputs: seeded synthetic tensors (hummingflight_b200/configs.py) generated in
+HBM. The generator is an Irwin-Hall(4) normal, so weights and activations are
+bounded at +-3.46 sigma of the N(0, sigma) the configs name.
 
 `--impl reference` times the reference's own CPU MoE path (compute/cpu_kernels.cpp
 + compute/moe_router.h built unmodified into oracle/_ref, AVX2 build, all host
@@ -25,20 +33,22 @@ import statistics
 import subprocess
 import sys
 import threading
-import time
 
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from hummingflight_b200.configs import GLM, WORKLOADS, layer_flops, zipf_bias  # noqa: E402
+from hummingflight_b200.configs import (GLM, WORKLOADS, ZIPF_BETA, layer_flops,  # noqa: E402
+                                        zipf_bias, zipf_stats)
 
-FALLBACK_HBM_GBS = 6650.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+NOMINAL_HBM_GBS, NOMINAL_TFLOPS = 8000.0, 2250.0
 REASON_BITS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x100: "display_clock_setting"}
+SUB_CONFIGS = (2, 0)
 
 
 def peaks():
@@ -46,12 +56,15 @@ def peaks():
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return FALLBACK_HBM_GBS, 1590.0, "fallback"
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained",
+                                                     d["bf16_tflops"])),
+                "kind": "measured"}
+    return dict(FALLBACK, kind="fallback")
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """nvidia-smi samples of SM clock and throttle reasons during a timed region."""
 
     def __init__(self, device: int, period_ms: int = 50):
         self.rows = []
@@ -125,25 +138,39 @@ def phase_bytes(shape, counts, T, k, path, gemv_max):
         out[f"{name}_down_flops"] = int((2 * c[sel] * inter[sel] * H).sum())
     n_slots = int(c.sum())
     out["router"] = E * H * 2 + T * H * 2 + T * E * 4
+    out["router_flops"] = 2 * T * E * H
     out["combine"] = n_slots * H * 4 + T * H * 4 + T * k * 8
     out["total_weights"] = E * H * 2 + int((3 * inter[live] * H * 2).sum())
     return out
 
 
+def sum_dicts(ds):
+    out = {}
+    for d in ds:
+        for k, v in d.items():
+            out[k] = out.get(k, 0) + v
+    return out
+
+
 # ---------------------------------------------------------------- reference arm (CPU)
-def reference_sample(wl, max_tokens=8):
+def reference_sample(wl, max_tokens):
     from oracle import oracle as O
     s = wl.shape
     d = O.Dims(s.hidden, s.num_experts, s.top_k, s.inter, s.shared_inter, s.scale, s.norm_topk)
-    flavour = "avx2" if O.ref_available("avx2") else "port"
     ntok = min(max_tokens, wl.tokens)
-    x = O.bf16_to_f32(O.gen_x_bf16(wl.x_seed, wl.tokens, s.hidden))[:ntok]
+    x = O.bf16_to_f32(O.gen_x_rows_bf16(wl.x_seed, range(ntok), s.hidden)).reshape(ntok, -1)
     bias = zipf_bias(s.num_experts, wl.weight_seeds[0]) if wl.bias == "zipf" else None
-    if flavour == "avx2":
-        R = O.RefLayer(d, wl.weight_seeds[0], 0, bias=bias, flavour="avx2")
-        R.prepare(x)
-        return R, x, "reference", O.ref_lib("avx2").hfr_threads()
-    raise RuntimeError("oracle/_ref was not built (the reference's CPU kernels)")
+    if not O.ref_available("avx2"):
+        raise RuntimeError("oracle/_ref was not built (the reference's CPU kernels)")
+    R = O.RefLayer(d, wl.weight_seeds[0], 0, bias=bias, flavour="avx2")
+    R.prepare(x)
+    return R, x, "reference", O.ref_lib("avx2").hfr_threads()
+
+
+def sample_text(wl, ntok):
+    return (f"first {ntok} of the {wl.tokens} tokens of {wl.name}, layer 0 of {wl.layers} "
+            f"(every layer has the same shape and per-token cost); weights generated before "
+            f"timing, resident in host RAM; per-token moeLayer")
 
 
 def run_reference(args, wl):
@@ -162,14 +189,14 @@ def run_reference(args, wl):
         t += R.forward(x)["seconds"]
     ntok = x.shape[0]
     value = ntok * args.steps / t
-    sample = (f"first {ntok} tokens of {wl.name} (layer 0), {args.steps} passes; weights "
-              f"generated before timing, resident in host RAM")
+    sample = sample_text(wl, ntok) + f", {args.steps} passes"
     line = {"metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16 weights, fp32 math", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": wl.name, "tokens_per_step": ntok, "layers": 1},
+            "config": {"workload": wl.name, "tokens_per_step": ntok, "layers": 1,
+                       "same_config": ntok == wl.tokens and wl.layers == 1},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
                              "cpu": cpu_model(), "nproc": os.cpu_count(), "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -188,9 +215,9 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def cpu_baseline(wl, budget_s):
+def cpu_baseline(wl, budget_s, ntok):
     try:
-        R, x, kind, cores = reference_sample(wl, 8)
+        R, x, kind, cores = reference_sample(wl, ntok)
     except Exception as e:  # noqa: BLE001
         return {"value": None, "unit": "tokens/s", "cores": None, "kind": "reference",
                 "sample": f"unavailable: {e}"}
@@ -202,25 +229,241 @@ def cpu_baseline(wl, budget_s):
     R.close()
     return {"value": n / t, "unit": "tokens/s", "cores": cores, "kind": kind,
             "cpu": cpu_model(), "nproc": os.cpu_count(),
-            "sample": f"{passes} passes over the first {x.shape[0]} tokens of {wl.name} "
-                      f"({t:.1f} s of CPU time), reference AVX2 build, per-token moeLayer"}
+            "sample": sample_text(wl, x.shape[0]) + f", {passes} passes ({t:.1f} s of CPU "
+                      f"time), reference AVX2 build"}
 
 
 # ---------------------------------------------------------------- our arm (GPU)
+class Job:
+    """One workload resident on this rank: the layers, x and outputs."""
+
+    def __init__(self, wl, args, rank, world, local, dist=None, uid=None):
+        import torch
+
+        from hummingflight_b200.moe import MoELayer, synth_bf16_normal
+        self.wl, self.rank, self.world = wl, rank, world
+        shape = wl.shape
+        T_glob, H = wl.tokens, shape.hidden
+        if T_glob % world or shape.num_experts % world:
+            raise SystemExit(f"{wl.name}: tokens and experts must divide by {world} ranks")
+        self.T = T = T_glob // world
+        self.L = MoELayer(shape, wl.layers, T, local, args.path, args.gemv_max, rank, world, uid)
+        self.bias = zipf_bias(shape.num_experts, wl.weight_seeds[0]) if wl.bias == "zipf" else None
+        for l, seed in enumerate(wl.weight_seeds):
+            self.L.synth_layer(l, seed, 0, self.bias)
+        x_all = torch.empty((T_glob, H), dtype=torch.int16, device="cuda")
+        synth_bf16_normal(x_all, wl.x_seed, 0, 0, 0, 1.0)
+        self.x = x_all[rank * T:(rank + 1) * T].contiguous().view(torch.bfloat16)
+        del x_all
+        self.outs = [torch.empty((T, H), dtype=torch.float32, device="cuda")
+                     for _ in range(wl.layers)]
+        # the routing of every layer (global counts: all ranks' tokens)
+        self.counts_glob, self.counts_rank0 = [], []
+        E, el = shape.num_experts, shape.num_experts // world
+        for l in range(wl.layers):
+            _, r = self.L.forward(l, self.x, out=self.outs[l], routing=True)
+            ids = r["topk_ids"]
+            if world > 1:
+                got = [torch.empty_like(ids) for _ in range(world)]
+                dist.all_gather(got, ids)
+                ids = torch.cat(got)
+            glob = np.bincount(ids.cpu().numpy().ravel(), minlength=E)
+            self.counts_glob.append(glob)
+            # rank 0's expert work: its local experts over the whole batch + shared on its tokens
+            c0 = np.zeros(E + 1, np.int64)
+            c0[:el] = glob[:el]
+            c0[E] = T
+            self.counts_rank0.append(c0)
+        torch.cuda.synchronize()
+
+    def step(self):
+        for l in range(self.wl.layers):
+            self.L.forward(l, self.x, out=self.outs[l])
+
+    def close(self):
+        self.L.close()
+        self.outs = None
+        self.x = None
+
+
+def timed(job, steps, world, dist, stream):
+    """K steps bracketed by a barrier and a device synchronize; CUDA events on
+    the launching stream; the max over ranks."""
+    import torch
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        job.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    m = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([m], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        m = float(t.item())
+    return m
+
+
+def measure(job, args, world, dist, stream, local, steps):
+    """Pass 1 (the value): K steps as a user runs them. Pass 2: the same K
+    steps with a CUDA event pair around every phase, for the per-kernel
+    durations of the roofline (those events cost a few us per phase boundary,
+    so they stay out of the first pass)."""
+    import torch
+    L = job.L
+    for _ in range(args.warmup):
+        job.step()
+    torch.cuda.synchronize()
+    L.profile_read()  # drop warm-up launch counts
+    clk = ClockSampler(local)
+    ms = timed(job, steps, world, dist, stream)
+    launches = int(sum(v[1] for v in L.profile_read().values()))
+    L.profile(True)
+    ms_profiled = timed(job, steps, world, dist, stream)
+    clocks = clk.stop()
+    L.profile(False)
+    prof = L.profile_read()
+    return {"ms": ms, "ms_profiled": ms_profiled, "launches": launches, "prof": prof,
+            "clocks": clocks, "steps": steps}
+
+
+def e2e_ms(job, world, dist, stream, steps):
+    """Same steps through hf_moe_forward_host: pinned host x in, pinned fp32
+    out back, inside the timed region, every layer."""
+    import torch
+    T, H = job.T, job.wl.shape.hidden
+    xh = torch.empty((T, H), dtype=torch.int16, pin_memory=True)
+    xh.copy_(job.x.view(torch.int16).cpu())
+    oh = torch.empty((T, H), dtype=torch.float32, pin_memory=True)
+    xh_np, oh_np = xh.numpy().view(np.uint16), oh.numpy()
+
+    def one():
+        for l in range(job.wl.layers):
+            job.L.forward_host(l, xh_np, oh_np, stream=stream)
+
+    one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        one()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    m = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([m], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        m = float(t.item())
+    return m
+
+
+def roofline(job, meas, args, pk, steps):
+    """The dominant kernel's algorithmic bytes or flops per launch (summed
+    over the layers of a step from each layer's realised routing) over its
+    average CUDA-event duration."""
+    wl, shape = job.wl, job.wl.shape
+    T = job.T
+    gemv_max = args.gemv_max or (1 if T <= 1 else 0)  # the library's AUTO rule
+    pb = sum_dicts(phase_bytes(shape, c, T, job.L.k, args.path, gemv_max)
+                   for c in job.counts_rank0)
+    prof = meas["prof"]
+    dom = max(("gemv_gate_up", "gemv_down", "router", "route", "combine",
+               "gemm_gate_up", "gemm_down"), key=lambda p: prof[p][0])
+    dom_ms, dom_n = prof[dom]
+    per_step_launches = max(1, dom_n // steps)
+    per_launch_ms = dom_ms / max(1, dom_n)
+    alg = pb.get(dom, 0) / per_step_launches
+    flops = pb.get(dom + "_flops", 0) / per_step_launches
+    hbm, tfl = pk["hbm_gbs"], pk["bf16_tflops"]
+    # flops/byte above half the machine balance: report against the tensor peak
+    tensor_bound = bool(flops) and flops / max(1, alg) > 0.5 * 1e3 * tfl / hbm
+    if tensor_bound:
+        achieved = flops / (per_launch_ms / 1e3) / 1e12
+    else:
+        achieved = alg / (per_launch_ms / 1e3) / 1e9 if alg else None
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get(f"{wl.name}:{dom}")
+    peak = tfl if tensor_bound else hbm
+    return pb, {"bound": "tensor" if tensor_bound else "hbm", "kernel": dom,
+                "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                "frac": achieved / peak if achieved else None,
+                "peak_kind": pk["kind"], "traffic": traffic,
+                "frac_nominal": (achieved / (NOMINAL_TFLOPS if tensor_bound else NOMINAL_HBM_GBS))
+                if achieved else None,
+                "algorithmic_bytes_per_launch": alg, "algorithmic_flops_per_launch": flops,
+                "launch_ms": per_launch_ms, "launches_per_step": per_step_launches}
+
+
+def layer_summary(job, meas, pb, pk):
+    """Whole-layer figures: weights + activations streamed, useful flops."""
+    wl, shape = job.wl, job.wl.shape
+    T, H = job.T, shape.hidden
+    ms = meas["ms"]
+    layer_bytes = pb["total_weights"] + wl.layers * (T * H * 2 + T * H * 4)
+    flops = layer_flops(shape, wl.tokens) * wl.layers
+    s = {"hbm_gbs": layer_bytes / (ms / 1e3) / 1e9, "tflops": flops / (ms / 1e3) / 1e12}
+    s["hbm_frac"] = s["hbm_gbs"] / pk["hbm_gbs"]
+    s["tflops_frac_burst"] = s["tflops"] / pk["bf16_tflops"]
+    s["tflops_frac_sustained"] = s["tflops"] / pk["bf16_tflops_sustained"]
+    t_bytes = layer_bytes / (pk["hbm_gbs"] * 1e9) * 1e3
+    t_flops = flops / (pk["bf16_tflops"] * 1e12) * 1e3
+    s["roofline_ms"] = max(t_bytes, t_flops)
+    s["roofline_bound"] = "hbm" if t_bytes >= t_flops else "tensor"
+    s["roofline_frac"] = s["roofline_ms"] / ms
+    s["bytes_per_step"] = layer_bytes
+    s["flops_per_step"] = flops
+    return s
+
+
+def sub_result(wl, args, local, stream, pk):
+    """Config 0 or 2 on one GPU: one layer, its own timing, roofline and clocks."""
+    import torch
+    job = Job(wl, args, 0, 1, local)
+    steps = 1000 if wl.tokens <= 64 else max(args.steps, 30)  # >= ~0.1 s timed
+    meas = measure(job, args, 1, None, stream, local, steps)
+    pb, rl = roofline(job, meas, args, pk, steps)
+    lay = layer_summary(job, meas, pb, pk)
+    out = {"workload": wl.name, "tokens": wl.tokens, "layers": wl.layers,
+           "ms_per_step": meas["ms"], "value": wl.tokens * wl.layers / (meas["ms"] / 1e3),
+           "unit": "tokens/s", "steps": steps, "active_experts": pb["active"],
+           "layer": lay, "roofline": rl, "gpu_launches": meas["launches"],
+           "phases_ms_per_step": {p: v[0] / steps for p, v in meas["prof"].items()
+                                  if v[1] or v[0] > 0},
+           "clocks": meas["clocks"]}
+    job.close()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "gemm"])
-    ap.add_argument("--cpu-budget-s", type=float, default=10.0)
-    ap.add_argument("--ref-tokens", type=int, default=8)
+    ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--ref-tokens", type=int, default=24,
+                    help="tokens of the workload the reference arm runs per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="skip the config 2 / 0 sub-results")
     ap.add_argument("--experts", type=int, default=0,
                     help="profiling case: fewer routed experts (same per-expert shape)")
     ap.add_argument("--tokens", type=int, default=0, help="profiling case: override T")
+    ap.add_argument("--layers", type=int, default=0, help="profiling case: first N layers")
     ap.add_argument("--inter", type=int, default=0,
                     help="profiling case: override the (routed and shared) intermediate size")
     ap.add_argument("--gemv-max", type=int, default=0,
@@ -228,14 +471,16 @@ def main():
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     wl = WORKLOADS[args.config]
-    if args.experts or args.tokens or args.inter:
+    profiling_case = bool(args.experts or args.tokens or args.inter or args.layers)
+    if profiling_case:
         from dataclasses import replace
         shape = replace(wl.shape, num_experts=args.experts or wl.shape.num_experts,
                         inter=args.inter or wl.shape.inter,
                         shared_inter=args.inter or wl.shape.shared_inter)
-        wl = replace(wl, shape=shape, tokens=args.tokens or wl.tokens,
+        seeds = wl.weight_seeds[:args.layers] if args.layers else wl.weight_seeds
+        wl = replace(wl, shape=shape, tokens=args.tokens or wl.tokens, weight_seeds=seeds,
                      name=f"{wl.name}_E{shape.num_experts}_T{args.tokens or wl.tokens}"
-                          f"_I{shape.inter}")
+                          f"_I{shape.inter}_L{len(seeds)}")
     if args.impl == "reference":
         run_reference(args, wl)
         return
@@ -244,8 +489,6 @@ def main():
     import torch.distributed as dist
     from datetime import timedelta
 
-    from hummingflight_b200.moe import MoELayer
-
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -253,175 +496,71 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    shape = wl.shape
-    # strong scaling: the workload's global batch is split across the ranks and
-    # the experts are sharded (expert parallelism, E/world per GPU)
-    T_glob, H = wl.tokens, shape.hidden
-    if T_glob % world or shape.num_experts % world:
-        raise SystemExit(f"{wl.name}: tokens and experts must divide by {world} ranks")
-    T = T_glob // world
     uid = None
     if world > 1:
         from hummingflight_b200.ep import broadcast_unique_id
         uid = broadcast_unique_id(dist, rank, torch.device("cuda", local))
-    L = MoELayer(shape, wl.layers, T, local, args.path, args.gemv_max, rank, world, uid)
-    bias = zipf_bias(shape.num_experts, wl.weight_seeds[0]) if wl.bias == "zipf" else None
-    for l, seed in enumerate(wl.weight_seeds):
-        L.synth_layer(l, seed, 0, bias)
     stream = torch.cuda.current_stream()
-    x_all = torch.empty((T_glob, H), dtype=torch.int16, device="cuda")
-    from hummingflight_b200.moe import synth_bf16_normal
-    synth_bf16_normal(x_all, wl.x_seed, 0, 0, 0, 1.0)
-    x = x_all[rank * T:(rank + 1) * T].contiguous().view(torch.bfloat16)
-    del x_all
-    outs = [torch.empty((T, H), dtype=torch.float32, device="cuda") for _ in range(wl.layers)]
+    pk = peaks()
 
-    def step():
-        for l in range(wl.layers):
-            L.forward(l, x, out=outs[l])
-
-    _, r = L.forward(0, x, out=outs[0], routing=True)
-    ids = r["topk_ids"]
-    if world > 1:
-        got = [torch.empty_like(ids) for _ in range(world)]
-        dist.all_gather(got, ids)
-        ids = torch.cat(got)
-    # rank 0's expert work: its local experts over the whole batch + shared on its tokens
-    glob = np.bincount(ids.cpu().numpy().ravel(), minlength=shape.num_experts)
-    el = shape.num_experts // world
-    counts = np.zeros(shape.num_experts + 1, np.int64)
-    counts[:el] = glob[:el]
-    counts[shape.num_experts] = T
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    L.profile_read()  # drop warm-up launch counts
-
-    def timed_pass():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        m = e0.elapsed_time(e1) / args.steps
-        if world > 1:
-            t = torch.tensor([m], device="cuda", dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            m = float(t.item())
-        return m
-
-    # pass 1 (the value): K steps as a user runs them. Pass 2: the same K steps
-    # with a CUDA event pair around every phase, for the per-kernel durations of
-    # the roofline; those events cost a few us per phase boundary, so they stay
-    # out of the first pass.
-    clk = ClockSampler(local)
-    ms = timed_pass()
-    launches = int(sum(v[1] for v in L.profile_read().values()))
-    L.profile(True)
-    ms_profiled = timed_pass()
-    clocks = clk.stop()
-    L.profile(False)
-    prof = L.profile_read()
-    tokens_per_step = T_glob * wl.layers
-    value = tokens_per_step / (ms / 1e3)
-
-    # end to end through hf_moe_forward_host: pinned host x in, pinned host out back
-    xh = torch.empty((T, H), dtype=torch.int16, pin_memory=True)
-    xh.copy_(x.view(torch.int16).cpu())
-    oh = torch.empty((T, H), dtype=torch.float32, pin_memory=True)
-    xh_np, oh_np = xh.numpy().view(np.uint16), oh.numpy()
-    for _ in range(3):
-        for l in range(wl.layers):
-            L.forward_host(l, xh_np, oh_np, stream=stream)
+    job = Job(wl, args, rank, world, local, dist, uid)
+    meas = measure(job, args, world, dist, stream, local, args.steps)
     e_steps = max(3, args.steps // 4)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0.record(stream)
-    for _ in range(e_steps):
-        for l in range(wl.layers):
-            L.forward_host(l, xh_np, oh_np, stream=stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-
+    e2e = e2e_ms(job, world, dist, stream, e_steps)
+    shape, T_glob, T = wl.shape, wl.tokens, job.T
+    tokens_per_step = T_glob * wl.layers
+    line = None
     if rank == 0:
-        hbm, tflops_peak, peak_kind = peaks()
-        # the library's AUTO rule: the GEMV only for a single token
-        gemv_max = args.gemv_max or (1 if T <= 1 else 0)
-        pb = phase_bytes(shape, counts, T, L.k, args.path, gemv_max)
-        dom = max(("gemv_gate_up", "gemv_down", "router", "route", "combine",
-                   "gemm_gate_up", "gemm_down"), key=lambda p: prof[p][0])
-        dom_ms, dom_n = prof[dom]
-        per_launch_ms = dom_ms / max(1, dom_n)
-        alg = pb.get(dom)
-        flops = pb.get(dom + "_flops")
-        # prefill-sized segments are tensor-bound; decode streams weights (HBM-bound)
-        tensor_bound = bool(flops) and flops / max(1, alg) > 0.5 * 1e3 * tflops_peak / hbm
-        if tensor_bound:
-            achieved = flops / (per_launch_ms / 1e3) / 1e12
-        else:
-            achieved = alg / (per_launch_ms / 1e3) / 1e9 if alg else None
-        traffic = None
-        tp = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tp):
-            with open(tp) as f:
-                traffic = json.load(f).get(f"{wl.name}:{dom}")
-        layer_bytes = pb["total_weights"] + T * H * 2 + T * H * 4
+        pb, rl = roofline(job, meas, args, pk, args.steps)
+        lay = layer_summary(job, meas, pb, pk)
+        H = shape.hidden
         line = {
-            "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic (seeded, generated in HBM)",
+            "metric": "MoE-layer tokens/s", "value": tokens_per_step / (meas["ms"] / 1e3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": meas["ms"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, generated in HBM; Irwin-Hall(4) normals, "
+                    "bounded at +-3.46 sigma)",
             "config": {"workload": wl.name, "tokens": T_glob, "tokens_per_rank": T,
-                       "layers": wl.layers,
-                       "hidden": H, "experts": shape.num_experts, "top_k": shape.top_k,
-                       "inter": shape.inter, "shared_inter": shape.shared_inter,
+                       "layers": wl.layers, "hidden": H, "experts": shape.num_experts,
+                       "top_k": shape.top_k, "inter": shape.inter,
+                       "shared_inter": shape.shared_inter,
                        "parallelism": f"ep{world}" if world > 1 else "single",
-                       "path": args.path, "active_experts": pb["active"],
-                       "l2": "no flush: weights streamed per step (%.1f GB) exceed the 126 MB L2"
-                             % (pb["total_weights"] / 1e9)},
-            "e2e": {"value": tokens_per_step / (e2e_ms / 1e3), "unit": "tokens/s",
+                       "path": args.path,
+                       "active_experts_layer0": int((job.counts_glob[0] > 0).sum()),
+                       "profiling_case": profiling_case,
+                       "l2": "no flush: weights streamed per step (%.1f GB on rank 0) exceed "
+                             "the 126 MB L2" % (pb["total_weights"] / 1e9)},
+            "e2e": {"value": tokens_per_step / (e2e / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T_glob * H * 2 * wl.layers,
-                    "d2h_bytes_per_step": T_glob * H * 4 * wl.layers},
-            "gpu_launches": launches,
+                    "d2h_bytes_per_step": T_glob * H * 4 * wl.layers, "ms_per_step": e2e},
+            "gpu_launches": meas["launches"],
             "phase_timing": {"pass": "second timed pass of the same K steps with per-phase "
-                                     "CUDA events on the forward's stream",
-                             "ms_per_step_with_events": ms_profiled},
-            # rank 0's weight stream per second, and useful flops of the whole job
-            "layer_hbm_gbs": layer_bytes * wl.layers / (ms / 1e3) / 1e9,
-            "layer_tflops": layer_flops(shape, T_glob) * wl.layers / (ms / 1e3) / 1e12,
-            "phases_ms_per_step": {p: v[0] / args.steps for p, v in prof.items() if v[1] or v[0] > 0},
-            "roofline": {"bound": "tensor" if tensor_bound else "hbm", "kernel": dom,
-                         "achieved": achieved,
-                         "peak": tflops_peak if tensor_bound else hbm,
-                         "unit": "TFLOP/s" if tensor_bound else "GB/s",
-                         "frac": (achieved / (tflops_peak if tensor_bound else hbm))
-                         if achieved else None,
-                         "peak_kind": peak_kind, "traffic": traffic,
-                         # against the nominal 8 TB/s HBM3e and 2.25 PFLOP/s dense BF16
-                         "frac_nominal": (achieved / (2250.0 if tensor_bound else 8000.0))
-                         if achieved else None,
-                         "algorithmic_bytes_per_launch": alg,
-                         "algorithmic_flops_per_launch": flops,
-                         "launch_ms": per_launch_ms},
-            "clocks": clocks,
+                                     "CUDA events on the forward's stream (rank 0)",
+                             "ms_per_step_with_events": meas["ms_profiled"]},
+            "layer": lay,
+            "phases_ms_per_step": {p: v[0] / args.steps for p, v in meas["prof"].items()
+                                   if v[1] or v[0] > 0},
+            "roofline": rl,
+            "clocks": meas["clocks"],
         }
+        if wl.bias == "zipf":
+            z = zipf_stats(job.counts_glob[0], wl.weight_seeds[0], shape.top_k)
+            z["beta"] = ZIPF_BETA
+            z["hottest_share_per_layer"] = [float(c.max() / c.sum()) for c in job.counts_glob]
+            z["zero_experts_per_layer"] = [int((c == 0).sum()) for c in job.counts_glob]
+            line["zipf"] = z
+    job.close()
+    del job
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if world == 1 and not args.no_sub and not profiling_case and args.config not in SUB_CONFIGS:
+        line["sub_results"] = {WORKLOADS[c].name: sub_result(WORKLOADS[c], args, local, stream, pk)
+                               for c in SUB_CONFIGS}
+    if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(wl, args.cpu_budget_s)
+            line["cpu_baseline"] = cpu_baseline(wl, args.cpu_budget_s, args.ref_tokens)
         print(json.dumps(line))
-    L.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -756,7 +756,13 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
         HF_TRY(ep_forward(c, L, x, xd, T, out, resid, r, st));
         return copy_routing(c, r, T, st);
     }
-    if (T == 0) return HF_OK;
+    if (T == 0) {  // an empty batch routes nothing: report zero counts and offsets
+        if (r && r->counts)
+            HF_CUDA(cudaMemsetAsync(r->counts, 0, sizeof(int32_t) * c->G_src, st));
+        if (r && r->offsets)
+            HF_CUDA(cudaMemsetAsync(r->offsets, 0, sizeof(int32_t) * (c->G_src + 1), st));
+        return HF_OK;
+    }
     const RouteArgs ra = route_args(c, L, x, xd, T);
     HF_TRY(run_route(c, L, ra, st));
     if (!route_only) {

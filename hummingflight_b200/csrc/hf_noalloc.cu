@@ -83,10 +83,14 @@ extern "C" hf_status hf_moe_route_noalloc(const uint16_t* router_bf16, const flo
         return fail(HF_ERR_ARG, "hf_moe_route_noalloc: x and router must be 16-byte aligned");
     unsigned char* base = nullptr;
     HF_TRY(scratch_for_current_device(&base));
-    if (T == 0) return HF_OK;
     cudaStream_t st = as_cuda(stream);
     const int k = top_k < E ? top_k : E;
     const int G = E + 1;
+    if (T == 0) {  // an empty batch: every count and offset is zero (as hf_moe_route reports)
+        if (counts) HF_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * G, st));
+        if (offsets) HF_CUDA(cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (G + 1), st));
+        return HF_OK;
+    }
     RouteArgs a{};
     a.x = x;
     a.x_f32 = x_dtype == HF_F32;

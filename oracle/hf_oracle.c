@@ -2,7 +2,7 @@
  * hf_oracle.c -- CPU restatement of HummingFlight's MoE layer (parity oracle).
  *
  * TEST INFRASTRUCTURE, never the product. See hf_oracle.h for the contract and
- * the reference lines each function follows. Built with -O2 -fopenmp
+ * the reference lines each function follows. Built with -O3 -fopenmp
  * -ffp-contract=off (oracle/Makefile) so every fp32 operation is the single
  * rounded operation the reference performs.
  */
@@ -132,6 +132,79 @@ void hfo_expert_ffn(const uint16_t* gate, const uint16_t* up, const uint16_t* do
     free(mid);
 }
 
+/* The scalar GEMV of compute/cpu_kernels.cpp:82-93 for n vectors at once:
+ * yT[i*n + t] = alpha * dot(A[i,:], x_t) + beta * yT[i*n + t], with x given
+ * transposed (xT[j*n + t]). Every (row, vector) pair still sums j = 0..K-1
+ * in order with one rounded multiply and one rounded add per term, so each
+ * result is bit-identical to hfo_gemv_bf16_f32 on that vector alone; only
+ * the loop nest changes (four rows share each weight load, and the vectors
+ * sit side by side so the token loop vectorises without reassociation). */
+#define HFO_NB 16
+static void gemv_multi(const uint16_t* A, const float* xT, int n, float* yT, int M, int K,
+                       float alpha, float beta) {
+    const int nrb = (M + 3) / 4;
+#pragma omp parallel for schedule(static)
+    for (int rb = 0; rb < nrb; ++rb) {
+        const int r0 = rb * 4;
+        const int nr = (M - r0) < 4 ? (M - r0) : 4;
+        const uint16_t* rows[4];
+        for (int r = 0; r < 4; ++r) rows[r] = A + (int64_t)(r0 + (r < nr ? r : 0)) * K;
+        for (int t0 = 0; t0 < n; t0 += HFO_NB) {
+            const int nt = (n - t0) < HFO_NB ? (n - t0) : HFO_NB;
+            float acc[4][HFO_NB];
+            for (int r = 0; r < 4; ++r)
+                for (int t = 0; t < HFO_NB; ++t) acc[r][t] = 0.0f;
+            for (int j = 0; j < K; ++j) {
+                const float* xj = xT + (int64_t)j * n + t0;
+                float xv[HFO_NB];
+                for (int t = 0; t < HFO_NB; ++t) xv[t] = t < nt ? xj[t] : 0.0f;
+                for (int r = 0; r < 4; ++r) {
+                    const float w = hfg_bf16_to_f32(rows[r][j]);
+                    for (int t = 0; t < HFO_NB; ++t) {
+                        float p = w * xv[t];
+                        acc[r][t] = acc[r][t] + p;
+                    }
+                }
+            }
+            for (int r = 0; r < nr; ++r)
+                for (int t = 0; t < nt; ++t) {
+                    float* y = yT + (int64_t)(r0 + r) * n + t0 + t;
+                    float a = alpha * acc[r][t];
+                    float c = beta * *y;
+                    *y = a + c;
+                }
+        }
+    }
+}
+
+/* expertFFNRaw (model/glm_forward.cpp:434-449) for n tokens of one expert:
+ * x rows [n x H] -> y rows [n x H] (y is read for the beta * y term of the
+ * down GEMV, as hfo_expert_ffn's zero-filled output is). Bit-identical per
+ * token to hfo_expert_ffn. */
+void hfo_expert_ffn_multi(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                          const float* x, float* y, int n, int H, int I) {
+    if (n <= 0) return;
+    float* xT = (float*)malloc(sizeof(float) * (size_t)H * n);
+    float* g = (float*)calloc((size_t)I * n, sizeof(float));
+    float* u = (float*)calloc((size_t)I * n, sizeof(float));
+    float* yT = (float*)malloc(sizeof(float) * (size_t)H * n);
+    for (int t = 0; t < n; ++t)
+        for (int j = 0; j < H; ++j) xT[(size_t)j * n + t] = x[(size_t)t * H + j];
+    gemv_multi(gate, xT, n, g, I, H, 1.0f, 0.0f);
+    gemv_multi(up, xT, n, u, I, H, 1.0f, 0.0f);
+    /* mid = g / (1 + exp(-g)) * u in fp32, laid out [I x n] for the down GEMV */
+    for (size_t i = 0; i < (size_t)I * n; ++i) g[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
+    for (int t = 0; t < n; ++t)
+        for (int h = 0; h < H; ++h) yT[(size_t)h * n + t] = y[(size_t)t * H + h];
+    gemv_multi(down, g, n, yT, H, I, 1.0f, 0.0f);
+    for (int t = 0; t < n; ++t)
+        for (int h = 0; h < H; ++h) y[(size_t)t * H + h] = yT[(size_t)h * n + t];
+    free(xT);
+    free(g);
+    free(u);
+    free(yT);
+}
+
 void hfo_permute(const int32_t* ids, int T, int k, int E, int has_shared, int32_t* counts,
                  int32_t* offsets, int32_t* perm) {
     for (int e = 0; e <= E; ++e) counts[e] = 0;
@@ -151,31 +224,57 @@ void hfo_permute(const int32_t* ids, int T, int k, int E, int has_shared, int32_
     free(cur);
 }
 
-/* Router + top-k for every token (glm_forward.cpp:517-541). */
+/* Router + top-k for every token (glm_forward.cpp:517-541). The router
+ * GEMV runs for up to 512 tokens at a time through gemv_multi (per token the
+ * same sums as hfo_router_scores), then sigmoid and topKScores per token. */
 static void route_all(const hfo_dims* d, const uint16_t* router_w, const float* bias,
                       const float* x, int T, int32_t* ids, float* w, float* margins) {
     const int E = d->num_experts, H = d->hidden;
     const int k = d->top_k < E ? d->top_k : E; /* TopKResult::k (moe_router.h:43) */
+    const int CH = 512;
     float* scores = (float*)calloc((size_t)E, sizeof(float));
-    for (int t = 0; t < T; ++t) {
-        hfo_router_scores(router_w, x + (size_t)t * H, E, H, scores);
-        float m;
-        hfo_topk_scores(scores, E, bias, k, d->scale, d->norm_topk, ids + (size_t)t * k,
-                        w + (size_t)t * k, &m);
-        if (margins) margins[t] = m;
+    float* xT = (float*)malloc(sizeof(float) * (size_t)H * CH);
+    float* sT = (float*)malloc(sizeof(float) * (size_t)E * CH);
+    for (int t0 = 0; t0 < T; t0 += CH) {
+        const int n = (T - t0) < CH ? (T - t0) : CH;
+        for (int t = 0; t < n; ++t)
+            for (int j = 0; j < H; ++j) xT[(size_t)j * n + t] = x[(size_t)(t0 + t) * H + j];
+        for (size_t i = 0; i < (size_t)E * n; ++i) sT[i] = 0.0f;
+        gemv_multi(router_w, xT, n, sT, E, H, 1.0f, 0.0f);
+        for (int t = 0; t < n; ++t) {
+            for (int e = 0; e < E; ++e) scores[e] = 1.0f / (1.0f + expf(-sT[(size_t)e * n + t]));
+            float m;
+            hfo_topk_scores(scores, E, bias, k, d->scale, d->norm_topk,
+                            ids + (size_t)(t0 + t) * k, w + (size_t)(t0 + t) * k, &m);
+            if (margins) margins[t0 + t] = m;
+        }
     }
     free(scores);
+    free(xT);
+    free(sT);
 }
 
-/* Expert FFN for every token routed to one expert, into slot_out rows. */
+/* Expert FFN for every token routed to one expert, into slot_out rows
+ * (one batched pass over the expert's weights; per token the same
+ * arithmetic as hfo_expert_ffn). */
 static void run_expert(const hfo_dims* d, const uint16_t* gud, int I, const float* x,
                        int ntok, const int32_t* toks, const int32_t* slots, float* slot_out) {
     const int H = d->hidden;
     const uint16_t* g = gud;
     const uint16_t* u = gud + (size_t)I * H;
     const uint16_t* dn = u + (size_t)I * H;
+    if (ntok <= 0) return;
+    float* xs = (float*)malloc(sizeof(float) * (size_t)ntok * H);
+    float* ys = (float*)malloc(sizeof(float) * (size_t)ntok * H);
+    for (int j = 0; j < ntok; ++j) {
+        memcpy(xs + (size_t)j * H, x + (size_t)toks[j] * H, sizeof(float) * (size_t)H);
+        memcpy(ys + (size_t)j * H, slot_out + (size_t)slots[j] * H, sizeof(float) * (size_t)H);
+    }
+    hfo_expert_ffn_multi(g, u, dn, xs, ys, ntok, H, I);
     for (int j = 0; j < ntok; ++j)
-        hfo_expert_ffn(g, u, dn, x + (size_t)toks[j] * H, slot_out + (size_t)slots[j] * H, H, I);
+        memcpy(slot_out + (size_t)slots[j] * H, ys + (size_t)j * H, sizeof(float) * (size_t)H);
+    free(xs);
+    free(ys);
 }
 
 /* Weighted accumulate in top-k rank order, then + shared

@@ -55,6 +55,13 @@ int hfo_topk_scores(const float* scores, int E, const float* bias, int top_k, fl
 void hfo_expert_ffn(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
                     const float* x, float* y, int H, int I);
 
+/* hfo_expert_ffn for n tokens of one expert in one pass over its weights:
+ * x [n x H] -> y [n x H] (y is read for the beta * y term of the down GEMV,
+ * like hfo_expert_ffn's zero-filled output). Each token's result is
+ * bit-identical to hfo_expert_ffn on that token alone. */
+void hfo_expert_ffn_multi(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                          const float* x, float* y, int n, int H, int I);
+
 /* GLMForward::rmsNorm (model/glm_forward.cpp:185-197) on one row of n:
  * sq = sum x_i^2 (i ascending), rms = 1 / sqrt(sq / n + eps),
  * out_i = x_i * rms * w_i (w BF16; x_i * rms when w is NULL). out may be x. */

@@ -201,6 +201,27 @@ def gen_x_bf16(seed: int, T: int, H: int) -> np.ndarray:
     return gen_bf16_normal(seed, 0, KIND_X, 0, 1.0, T * H).reshape(T, H)
 
 
+def gen_x_bf16_c(seed: int, T: int, H: int) -> np.ndarray:
+    """gen_x_bf16 through the C generator (multi-threaded; same bits)."""
+    out = np.empty(T * H, np.uint16)
+    lib().hfo_gen_bf16_normal(seed, 0, KIND_X, 0, 1.0, T * H, _p(out, _c_u16p))
+    return out.reshape(T, H)
+
+
+def gen_x_rows_bf16(seed: int, rows, H: int) -> np.ndarray:
+    """Rows `rows` of gen_x_bf16(seed, T, H) for any T above them (element
+    t*H + j of the stream), without generating the other rows."""
+    k = key(seed, 0, KIND_X, 0)
+    out = np.empty((len(rows), H), np.uint16)
+    sc = normal_scale(1.0)
+    for i, t in enumerate(rows):
+        b = _bits(k, H, int(t) * H)
+        s = ((b & np.uint64(0xFFFF)) + ((b >> np.uint64(16)) & np.uint64(0xFFFF)) +
+             ((b >> np.uint64(32)) & np.uint64(0xFFFF)) + (b >> np.uint64(48))).astype(np.int64)
+        out[i] = f32_to_bf16((s - 131070).astype(np.float32) * sc)
+    return out
+
+
 # ---------------------------------------------------------------- wrappers
 def gemv_bf16_f32(A_bf16, x, y=None, alpha=1.0, beta=0.0):
     A = np.ascontiguousarray(A_bf16, dtype=np.uint16)

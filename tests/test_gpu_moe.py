@@ -57,6 +57,16 @@ def layer_for(shape, wseed, max_tokens, bias=None, path="gemv"):
     return L
 
 
+def agreeing(ids, ids_ref):
+    """Tokens whose top-k index list equals the oracle's: the outputs of these
+    are compared (the others are near-ties, where either order is right).
+    The mask must cover at least one token and most of the batch."""
+    a = np.all(np.asarray(ids) == np.asarray(ids_ref), axis=1)
+    need = 0.9 if a.size >= 10 else 0.5
+    assert a.sum() >= 1 and a.mean() >= need, f"only {a.sum()}/{a.size} tokens route alike"
+    return a
+
+
 def check_routing(r, ids_ref, margins_ref, E, has_shared=True):
     ids = r["topk_ids"].cpu().numpy()
     ok = margins_ref > MARGIN
@@ -177,8 +187,8 @@ def test_moe_large_T_multiblock_routing(T):
     torch.cuda.synchronize()
     orc = O.moe_layer_synth(d, 31, 0, O.bf16_to_f32(xb).reshape(T, 256))
     ids = check_routing(r, orc["ids"], orc["margins"], 64)
-    if np.array_equal(ids, orc["ids"]):
-        close(out.cpu().numpy(), orc["out"], f"T={T}")
+    a = agreeing(ids, orc["ids"])
+    close(out.cpu().numpy()[a], orc["out"][a], f"T={T}")
     L.close()
 
 
