@@ -20,6 +20,9 @@ Inputs: seeded synthetic tensors (hummingflight_b200/configs.py) generated in
 HBM. The generator is an Irwin-Hall(4) normal, so weights and activations are
 bounded at +-3.46 sigma of the N(0, sigma) the configs name.
 
+`--probe gemv` / `--probe ingest` run the GEMV-twin and checkpoint-ingest
+measurements instead (see probe_gemv / probe_ingest).
+
 `--impl reference` times the reference's own CPU MoE path (compute/cpu_kernels.cpp
 + compute/moe_router.h built unmodified into oracle/_ref, AVX2 build, all host
 threads) on a bounded token sample of the same workload.
@@ -233,6 +236,160 @@ def cpu_baseline(wl, budget_s, ntok):
                       f"time), reference AVX2 build"}
 
 
+# ---------------------------------------------------------------- probes
+# `--probe gemv`: device time of the gemv_bf16_f32 twin (hf_gemv_bf16_f32) on
+# the matrix shapes of its call sites -- the attention projections of
+# glm_forward.cpp:314-408 (q_a, q_b, kv_a, kv_b, o_proj), the DSA indexer, the
+# router and an LM head. Each shape runs 60 times back to back from a CUDA
+# graph (no host launch cost in the time), cycling through enough copies of
+# the weight to pass 512 MB per cycle, so every launch streams its matrix from
+# HBM rather than L2. Prints the mean time per launch, matrix bytes / time and
+# the error against a torch fp32 product (relative to the largest output).
+GEMV_SHAPES = {"q_a": (2048, 6144), "q_b": (16384, 2048), "kv_a": (576, 6144),
+               "kv_b": (28672, 512), "o_proj": (6144, 16384), "idx_wq_b": (4096, 2048),
+               "idx_wk": (128, 6144), "router": (256, 6144), "lm_head": (151552, 6144)}
+
+
+def probe_gemv(launches=60):
+    import torch
+
+    from hummingflight_b200 import moe as M
+    for name, (m, k) in GEMV_SHAPES.items():
+        nb = m * k * 2
+        ncopy = max(1, min(64, (512 << 20) // nb + 1))
+        As = [(torch.randn(m, k, device="cuda") * 0.05).to(torch.bfloat16).view(torch.int16)
+              for _ in range(ncopy)]
+        x = torch.randn(k, device="cuda")
+        y = torch.zeros(m, device="cuda")
+        M.gemv_bf16_f32(As[0], x, y, m, k)
+        ref = As[0].view(torch.bfloat16).float() @ x
+        err = ((y - ref).abs().max() / ref.abs().max()).item()
+        for i in range(5):
+            M.gemv_bf16_f32(As[i % ncopy], x, y, m, k)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=torch.cuda.Stream()):
+            for i in range(launches):
+                M.gemv_bf16_f32(As[i % ncopy], x, y, m, k)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        t_ms = a.elapsed_time(b) / launches
+        print(f"{name:9s} {m:6d} x {k:5d}: {t_ms * 1000:7.1f} us  {nb / t_ms / 1e6:6.0f} GB/s  "
+              f"rel err {err:.1e}  ({ncopy} copies)", flush=True)
+        del g, As
+
+
+# `--probe ingest`: checkpoint ingest throughput, safetensors shards (in the
+# page cache) -> resident HBM weights through hf_moe_load_safetensors. Writes
+# one GLM-shaped MoE layer (`--probe-experts` routed experts of 75.5 MB, the
+# router and the bias) as shards in the checkpoint's tensor names, loads it
+# `--probe-repeat` times and prints one JSON line: the load rate beside the
+# two ceilings of the path -- a pinned host-to-device copy of 1 GiB (the DMA
+# bound) and a pread of the shards with the loader's thread count (the
+# page-cache bound). Every expert holds the same random bytes.
+def _write_shards(d, E, H, I, Is, nshards, layer=0):
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from safetensors_writer import write_file
+    rng = np.random.default_rng(0)
+    blk = {k: rng.integers(0, 1 << 16, (I, H) if k != "down" else (H, I), dtype=np.uint16)
+           for k in ("gate", "up", "down")}
+    pre = f"model.layers.{layer}.mlp."
+    tensors = [(pre + "gate.weight", "BF16", (E, H),
+                rng.integers(0, 1 << 16, (E, H), dtype=np.uint16)),
+               (pre + "gate.e_score_correction_bias", "F32", (E,),
+                rng.uniform(-0.1, 0.1, E).astype(np.float32))]
+    for e in range(E):
+        for k in ("gate", "up", "down"):
+            tensors.append((pre + f"experts.{e}.{k}_proj.weight", "BF16", blk[k].shape, blk[k]))
+    sh = {k: blk[k][:Is] if k != "down" else blk[k][:, :Is] for k in blk}
+    for k in ("gate", "up", "down"):
+        tensors.append((pre + f"shared_experts.{k}_proj.weight", "BF16", sh[k].shape,
+                        np.ascontiguousarray(sh[k])))
+    per = (len(tensors) + nshards - 1) // nshards
+    paths = []
+    for s in range(nshards):
+        p = os.path.join(d, f"model-{s + 1:05d}-of-{nshards:05d}.safetensors")
+        write_file(p, tensors[s * per:(s + 1) * per])
+        paths.append(p)
+    return paths
+
+
+def _pread_rate(paths, threads):
+    import concurrent.futures as cf
+    import time
+    chunk = 16 << 20
+    jobs = []
+    for p in paths:
+        n = os.path.getsize(p)
+        jobs += [(p, o, min(chunk, n - o)) for o in range(0, n, chunk)]
+    bufs = [np.empty(chunk, np.uint8) for _ in range(threads)]
+    fds = {p: os.open(p, os.O_RDONLY) for p in paths}
+
+    def run(tid):
+        for i in range(tid, len(jobs), threads):
+            p, o, n = jobs[i]
+            os.preadv(fds[p], [memoryview(bufs[tid])[:n]], o)
+
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(threads) as ex:
+        list(ex.map(run, range(threads)))
+    dt = time.perf_counter() - t0
+    for fd in fds.values():
+        os.close(fd)
+    return sum(j[2] for j in jobs) / dt / 1e9
+
+
+def _h2d_rate(torch, nbytes=1 << 30, reps=5):
+    src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        dst.copy_(src, non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    return nbytes * reps / (a.elapsed_time(b) / 1e3) / 1e9
+
+
+def probe_ingest(E, nshards, repeat):
+    import shutil
+    import tempfile
+
+    import torch
+
+    from hummingflight_b200 import _lib
+    from hummingflight_b200.configs import LayerShape
+    from hummingflight_b200.moe import MoELayer
+    H, I, Is = 6144, 2048, 2048
+    d = tempfile.mkdtemp(prefix="hf_ingest_")
+    try:
+        paths = _write_shards(d, E, H, I, Is, nshards)
+        L = MoELayer(LayerShape(H, E, min(8, E), I, Is, 2.5, True), 1, 8, 0, "auto")
+        runs = [L.load_safetensors(0, paths, 0) for _ in range(repeat)]
+        best = min(r["seconds"] for r in runs)
+        nbytes = runs[0]["bytes"]
+        threads = max(1, min(8, (os.cpu_count() or 2) // 2))
+        line = {"metric": "checkpoint ingest GB/s (safetensors page cache -> HBM)",
+                "value": nbytes / best / 1e9, "unit": "GB/s", "bytes": nbytes, "experts": E,
+                "tensors": runs[0]["tensors"], "shards": nshards,
+                "seconds": [round(r["seconds"], 4) for r in runs],
+                "ceilings": {"h2d_pinned_gbs": _h2d_rate(torch),
+                             "pread_gbs": _pread_rate(paths, threads),
+                             "reader_threads": threads}}
+        L.close()
+        _lib.lib().hf_ingest_release_staging()
+        print(json.dumps(line))
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
 # ---------------------------------------------------------------- our arm (GPU)
 class Job:
     """One workload resident on this rank: the layers, x and outputs."""
@@ -247,11 +404,35 @@ class Job:
         if T_glob % world or shape.num_experts % world:
             raise SystemExit(f"{wl.name}: tokens and experts must divide by {world} ranks")
         self.T = T = T_glob // world
+        E = shape.num_experts
         self.L = MoELayer(shape, wl.layers, T, local, args.path, args.gemv_max, rank, world, uid)
-        self.bias = zipf_bias(shape.num_experts, wl.weight_seeds[0]) if wl.bias == "zipf" else None
+        self.bias = zipf_bias(E, wl.weight_seeds[0]) if wl.bias == "zipf" else None
         for l, seed in enumerate(wl.weight_seeds):
             self.L.synth_layer(l, seed, 0, self.bias)
         x_all = torch.empty((T_glob, H), dtype=torch.int16, device="cuda")
+        self.orders = [np.arange(E)] * wl.layers
+        self.placement = "contiguous"
+        if world > 1 and args.placement == "balanced":
+            # Expert placement by load: route a calibration batch (the same
+            # size, other tokens: x seed + 1000) through every layer, sum the
+            # per-expert token counts over the ranks, and give each rank E/W
+            # experts of about equal work (tokens + 128 token-equivalents for
+            # an active expert's weight stream), then load the layer again.
+            from hummingflight_b200.moe import balanced_placement
+            synth_bf16_normal(x_all, wl.x_seed + 1000, 0, 0, 0, 1.0)
+            xc = x_all[rank * T:(rank + 1) * T].contiguous().view(torch.bfloat16)
+            self.orders = []
+            for l, seed in enumerate(wl.weight_seeds):
+                ids = self.L.route(l, xc)["topk_ids"]
+                cnt = torch.bincount(ids.reshape(-1).long(), minlength=E)
+                dist.all_reduce(cnt)
+                c = cnt.cpu().numpy().astype(np.int64)
+                order = balanced_placement(c + 128 * (c > 0), world)
+                self.orders.append(order)
+                self.L.set_placement(l, order)
+                self.L.synth_layer(l, seed, 0, self.bias)
+            del xc
+            self.placement = "balanced (calibration batch: x seed + 1000)"
         synth_bf16_normal(x_all, wl.x_seed, 0, 0, 0, 1.0)
         self.x = x_all[rank * T:(rank + 1) * T].contiguous().view(torch.bfloat16)
         del x_all
@@ -259,7 +440,7 @@ class Job:
                      for _ in range(wl.layers)]
         # the routing of every layer (global counts: all ranks' tokens)
         self.counts_glob, self.counts_rank0 = [], []
-        E, el = shape.num_experts, shape.num_experts // world
+        el = E // world
         for l in range(wl.layers):
             _, r = self.L.forward(l, self.x, out=self.outs[l], routing=True)
             ids = r["topk_ids"]
@@ -271,7 +452,7 @@ class Job:
             self.counts_glob.append(glob)
             # rank 0's expert work: its local experts over the whole batch + shared on its tokens
             c0 = np.zeros(E + 1, np.int64)
-            c0[:el] = glob[:el]
+            c0[:el] = glob[self.orders[l][:el]]
             c0[E] = T
             self.counts_rank0.append(c0)
         torch.cuda.synchronize()
@@ -460,6 +641,8 @@ def main():
                     help="tokens of the workload the reference arm runs per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sub", action="store_true", help="skip the config 2 / 0 sub-results")
+    ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="expert placement over the ranks (N > 1)")
     ap.add_argument("--experts", type=int, default=0,
                     help="profiling case: fewer routed experts (same per-expert shape)")
     ap.add_argument("--tokens", type=int, default=0, help="profiling case: override T")
@@ -468,7 +651,19 @@ def main():
                     help="profiling case: override the (routed and shared) intermediate size")
     ap.add_argument("--gemv-max", type=int, default=0,
                     help="AUTO path: segments up to this many tokens use the GEMV (0 = default)")
+    ap.add_argument("--probe", default="", choices=["", "gemv", "ingest"],
+                    help="instead of the layer benchmark: the GEMV twin on the attention "
+                         "shapes, or checkpoint ingest throughput")
+    ap.add_argument("--probe-experts", type=int, default=32)
+    ap.add_argument("--probe-shards", type=int, default=4)
+    ap.add_argument("--probe-repeat", type=int, default=3)
     args = ap.parse_args()
+    if args.probe == "gemv":
+        probe_gemv()
+        return
+    if args.probe == "ingest":
+        probe_ingest(args.probe_experts, args.probe_shards, args.probe_repeat)
+        return
     args.warmup = max(3, args.warmup)
     wl = WORKLOADS[args.config]
     profiling_case = bool(args.experts or args.tokens or args.inter or args.layers)
@@ -505,6 +700,15 @@ def main():
 
     job = Job(wl, args, rank, world, local, dist, uid)
     meas = measure(job, args, world, dist, stream, local, args.steps)
+    ranks_phases = None
+    if world > 1:  # every rank's phase times (second pass) and routed rows
+        el = wl.shape.num_experts // world
+        mine = {"phases": {p: v[0] / args.steps for p, v in meas["prof"].items() if v[0] > 0},
+                "ms_profiled": meas["ms_profiled"],
+                "routed_rows": int(sum(int(c[o[rank * el:(rank + 1) * el]].sum())
+                                       for c, o in zip(job.counts_glob, job.orders)))}
+        ranks_phases = [None] * world
+        dist.all_gather_object(ranks_phases, mine)
     e_steps = max(3, args.steps // 4)
     e2e = e2e_ms(job, world, dist, stream, e_steps)
     shape, T_glob, T = wl.shape, wl.tokens, job.T
@@ -526,6 +730,7 @@ def main():
                        "top_k": shape.top_k, "inter": shape.inter,
                        "shared_inter": shape.shared_inter,
                        "parallelism": f"ep{world}" if world > 1 else "single",
+                       "expert_placement": job.placement,
                        "path": args.path,
                        "active_experts_layer0": int((job.counts_glob[0] > 0).sum()),
                        "profiling_case": profiling_case,
@@ -544,6 +749,16 @@ def main():
             "roofline": rl,
             "clocks": meas["clocks"],
         }
+        if ranks_phases:
+            gemm = [sum(v for p, v in r["phases"].items() if p.startswith("gemm"))
+                    for r in ranks_phases]
+            rows = [r["routed_rows"] for r in ranks_phases]
+            line["ranks"] = {
+                "phases_ms_per_step": [r["phases"] for r in ranks_phases],
+                "routed_rows_per_step": rows,
+                "rows_max_over_mean": max(rows) / (sum(rows) / len(rows)),
+                "gemm_ms_max_over_mean": max(gemm) / (sum(gemm) / len(gemm)),
+                "slowest_rank_by_gemm": int(np.argmax(gemm))}
         if wl.bias == "zipf":
             z = zipf_stats(job.counts_glob[0], wl.weight_seeds[0], shape.top_k)
             z["beta"] = ZIPF_BETA

@@ -16,7 +16,7 @@ c_int, c_float, c_size, c_u64, c_u32, c_vp = (ctypes.c_int, ctypes.c_float, ctyp
                                               ctypes.c_uint64, ctypes.c_uint32, ctypes.c_void_p)
 
 HF_OK, HF_ERR_ARG, HF_ERR_CUDA, HF_ERR_NCCL, HF_ERR_TIMEOUT, HF_ERR_OOM, HF_ERR_STATE, \
-    HF_ERR_UNSUPPORTED = range(8)
+    HF_ERR_UNSUPPORTED, HF_ERR_RANGE = range(9)
 HF_MEM_HOST, HF_MEM_DEVICE = 0, 1
 HF_BF16, HF_F32 = 0, 1
 HF_PATH_AUTO, HF_PATH_GEMV, HF_PATH_GEMM = 0, 1, 2
@@ -80,6 +80,10 @@ SIGNATURES = {
                                      ctypes.POINTER(HfMoeRouting), c_vp]),
     "hf_moe_route": (c_int, [c_vp, c_int, c_vp, c_int, c_int, ctypes.POINTER(HfMoeRouting), c_vp]),
     "hf_ep_unique_id": (c_int, [c_vp]),
+    "hf_moe_ep_transport": (c_int, [c_vp, c_vp]),
+    "hf_moe_ep_resync": (c_int, [c_vp]),
+    "hf_moe_set_placement": (c_int, [c_vp, c_int, c_vp]),
+    "hf_ep_balanced_placement": (c_int, [c_int, c_int, c_vp, c_vp]),
     "hf_ep_plan": (c_int, [c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "hf_moe_route_noalloc": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float,
                                      c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),

@@ -39,6 +39,22 @@ struct LayerBuf {
     CUtensorMap sh_gate{}, sh_up{}, sh_down{};  // shared expert: one view per matrix
     CUtensorMap rt{};            // router rows (the router GEMM's weight operand)
     bool maps = false;
+    // Expert placement (expert parallelism): placed position j holds global
+    // expert order[j], rank r owns positions [r*El, (r+1)*El); inv is the
+    // inverse. The router rows and bias are stored in placed order, so routing
+    // produces placed ids and the exchange sends each rank one contiguous
+    // range; routing outputs are mapped back to global ids. Empty: identity.
+    std::vector<int32_t> order, inv;
+    int32_t* d_order = nullptr;  // [E] device copy of order
+    // Resident format of the down blocks (hf_weights.cu): dfmt[g] = 1 when
+    // group g's block holds FP16 (w * 2^S), 0 for the BF16 layout; down_ready
+    // once a forward has put every block in one format, down_f16 which one.
+    std::vector<uint8_t> dfmt;
+    bool down_ready = false, down_f16 = false;
+    uint16_t** d_blocks = nullptr;  // [G] down block of each group
+    int* d_list = nullptr;          // [G] groups a conversion touches
+    unsigned* d_absmax = nullptr;   // [G] largest |w| (BF16 bits)
+    float* d_scale = nullptr;       // [G] 2^-S
 };
 
 template <typename T>
@@ -112,6 +128,28 @@ struct hf_moe_ctx {
 
 namespace hf {
 
+// Local slot of global expert `eid` on this rank (-1: not owned here), and
+// the global id of local slot l, under the layer's placement.
+inline int local_slot(const hf_moe_ctx* c, const LayerBuf& L, int eid) {
+    if (eid < 0 || eid >= c->E) return -1;
+    const int l = (L.inv.empty() ? eid : L.inv[size_t(eid)]) - c->e_begin;
+    return (l >= 0 && l < c->E_local) ? l : -1;
+}
+inline int slot_expert(const hf_moe_ctx* c, const LayerBuf& L, int l) {
+    const int pos = c->e_begin + l;
+    return L.order.empty() ? pos : L.order[size_t(pos)];
+}
+// Down-block format (hf_weights.cu): before a forward, before handing out a
+// block's address, and after a weight setter wrote group g (-1: all).
+hf_status ensure_down_format(hf_moe_ctx* c, LayerBuf& L, cudaStream_t st);
+hf_status down_to_bf16(hf_moe_ctx* c, LayerBuf& L, int g);
+void down_written(LayerBuf& L, int g);
+// Router rows and bias (written in global order) into the placed order.
+hf_status place_router(hf_moe_ctx* c, LayerBuf& L, cudaStream_t st);
+// Routing outputs of a forward in global expert ids (placed layers only).
+hf_status unplace_routing(hf_moe_ctx* c, const LayerBuf& L, const hf_moe_routing* r, int T,
+                          cudaStream_t st);
+
 // Brackets one phase of a forward with events (when profiling) and counts its
 // kernel launches.
 struct PhaseTimer {
@@ -165,6 +203,13 @@ struct ExpertWork {
     int pair;              // the GEMM tiles run on CTA pairs
     bool maybe_gemm;   // some segment may take the GEMM / the GEMV (else skip the launches)
     bool maybe_gemv;
+    int down_f16 = 0;  // the layer's down blocks are FP16 (GemmArgs::down_f16)
+    // GEMM2 outputs through per-position row pointers and the end-of-kernel
+    // flag release (GemmArgs::yrow / sig_*); GEMM path only
+    float* const* yrow = nullptr;
+    unsigned long long* const* sig_flags = nullptr;
+    int sig_n = 0, sig_slot = 0;
+    unsigned long long sig_seq = 0;
 };
 
 // Routing arguments of a forward on the given (source) plan.
@@ -182,8 +227,9 @@ struct RouterTiles {
 RouterTiles router_tiles(int T, int E, int H, int nsm);
 bool use_tc_router(const hf_moe_ctx* c, const LayerBuf& L, const void* x, hf_dtype xd, int T);
 hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st);
+// slot_pos: the row of y each slot reads (default: the context's slot -> position table)
 hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, const float* resid,
-                      float* slot_out, cudaStream_t st);
+                      float* slot_out, cudaStream_t st, const int32_t* slot_pos = nullptr);
 
 // Allocates a layer's weight buffers and tensor maps on first use (hf_moe.cu).
 hf_status ctx_layer_alloc(hf_moe_ctx* c, int layer);

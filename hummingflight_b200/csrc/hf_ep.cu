@@ -1,24 +1,36 @@
-// hf_ep.cu -- expert parallelism: experts sharded across GPUs, token rows
-// exchanged with NCCL over NVLink.
+// hf_ep.cu -- expert parallelism: experts sharded across the GPUs of one node,
+// token rows exchanged over NVLink.
 //
 // The reference runs on one host with no collective backend (single-process
-// CPU engine); this exchange is new. Rank r owns experts
-// [r*E/W, (r+1)*E/W) and a replica of the shared expert. One forward:
+// CPU engine); this exchange is new. Rank r owns E/W experts -- by default
+// [r*E/W, (r+1)*E/W), or those a placement gives it (hf_moe_set_placement;
+// the router rows are stored in placed order, so the experts of one rank are
+// one contiguous range of placed ids) -- plus a replica of the shared expert.
+// One forward on the default transport, peer memory (CUDA IPC mappings of
+// every rank's slabs, NVLink stores, no host round trip):
 //
-//  1. route the rank's own tokens over ALL experts (the canonical
-//     permutation orders slots by expert, so the slots bound for rank d form
-//     one contiguous range) and gather their activation rows in that order;
-//  2. exchange per-expert counts (W x E/W int32), read them on the host and
-//     size the row exchange (the one host synchronization of a forward);
-//  3. send the rows (grouped ncclSend/ncclRecv), append the local tokens;
-//  4. run the same GEMV / tcgen05 GEMM kernels on the local experts (received
-//     rows, ordered expert-major then source rank) and on the shared expert
-//     (local tokens);
-//  5. send each expert output row (fp32) back to its source, where it lands
-//     at the slot's canonical position;
-//  6. combine at the source in the reference's top-k rank order.
+//  1. route the rank's own tokens over ALL experts; the canonical
+//     permutation orders slots by expert, so the slots bound for rank d are
+//     one contiguous range;
+//  2. the pack kernel stores each routed activation row straight into its
+//     destination's receive slab, then the per-expert counts, then this
+//     forward's sequence number into every rank's arrival flag
+//     (fence.sc.sys + st.release.sys);
+//  3. the receiver's plan kernel waits (bounded) for every source's flag and
+//     builds the plan from the counts on the device;
+//  4. the same GEMV / tcgen05 GEMM kernels run on the local experts (received
+//     rows, expert-major then source) and on the shared expert (local
+//     tokens). On the GEMM path the down GEMM's epilogue stores every output
+//     row straight into its source's output slab, and its last CTA raises
+//     the return flags, so the return overlaps the GEMM tile by tile;
+//  5. the source waits (bounded) for every rank's return flag and combines in
+//     the reference's top-k rank order, reading the rows from its slab.
 // Each slot's expert product and the combine order do not depend on W, so
-// the output equals the single-GPU output bit for bit.
+// the output equals the single-GPU output bit for bit (given the same router
+// logits). Without peer mappings (all ranks agree on the transport at
+// create) the same slabs travel through NCCL for small batches, and large
+// batches use an exchange sized on the host (counts read back, grouped
+// ncclSend/ncclRecv).
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2, which returns the copy
 // the process already uses, e.g. PyTorch's), so the library does not pin an
@@ -45,6 +57,8 @@ struct NcclApi {
     ncclResult_t (*GroupEnd)() = nullptr;
     ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
     std::string error;
     bool ok = false;
@@ -66,9 +80,10 @@ static NcclApi load_nccl() {
     a.GroupEnd = reinterpret_cast<decltype(a.GroupEnd)>(sym("ncclGroupEnd"));
     a.Send = reinterpret_cast<decltype(a.Send)>(sym("ncclSend"));
     a.Recv = reinterpret_cast<decltype(a.Recv)>(sym("ncclRecv"));
+    a.AllReduce = reinterpret_cast<decltype(a.AllReduce)>(sym("ncclAllReduce"));
     a.GetErrorString = reinterpret_cast<decltype(a.GetErrorString)>(sym("ncclGetErrorString"));
     a.ok = a.GetUniqueId && a.CommInitRank && a.CommDestroy && a.GroupStart && a.GroupEnd &&
-           a.Send && a.Recv && a.GetErrorString;
+           a.Send && a.Recv && a.AllReduce && a.GetErrorString;
     if (!a.ok) a.error = "libnccl.so.2 lacks a required symbol";
     return a;
 }
@@ -240,12 +255,16 @@ __device__ __forceinline__ void ep_last_block(int* done, F tail) {
 
 // Rows into the destinations' slabs (at this rank's slab) in peer memory;
 // then counts, then flags[d][rank] = seq on every rank.
+// With rowmap set, also records where each slot's output will be read back:
+// routed slot -> row d * cap + r of this rank's output slab, the shared slot
+// of local token t (slot n + t) -> row W * cap + t.
 __global__ void __launch_bounds__(256) k_ep_pack_p2p(const int32_t* perm, const int32_t* ids,
                                                      const int32_t* offsets, const uint4* x,
                                                      int row_vec, int n, int k, int El, int cap,
                                                      int rank, int W, const int32_t* cnt_src,
                                                      PeerPtrs pp, int* done,
-                                                     unsigned long long seq) {
+                                                     unsigned long long seq, int32_t* rowmap,
+                                                     int n_shared) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int nw = (gridDim.x * blockDim.x) >> 5;
     for (int p = warp; p < n; p += nw) {
@@ -255,7 +274,11 @@ __global__ void __launch_bounds__(256) k_ep_pack_p2p(const int32_t* perm, const 
         const uint4* src = x + size_t(slot / k) * row_vec;
         uint4* dst = reinterpret_cast<uint4*>(pp.x[d]) + (size_t(rank) * cap + r) * row_vec;
         for (int c = lane; c < row_vec; c += 32) dst[c] = ld_nc_u4(src + c);
+        if (rowmap && lane == 0) rowmap[slot] = d * cap + r;
     }
+    if (rowmap)
+        for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_shared; t += gridDim.x * blockDim.x)
+            rowmap[n + t] = W * cap + t;
     ep_last_block(done, [&] {
         for (int i = threadIdx.x; i < W * El; i += blockDim.x)
             pp.cnt[i / El][rank * El + i % El] = cnt_src[i];
@@ -306,6 +329,13 @@ struct EpState {
     unsigned long long seq = 0;           // forwards exchanged so far
     PeerPtrs peers{};
     std::vector<void*> opened;            // IPC mappings to close
+    // outputs returned from the down GEMM's epilogue (peer memory, GEMM path):
+    // per-position output rows, the ranks' output slabs and flag arrays as
+    // device tables, and slot -> row of this rank's output slab
+    float** yrow = nullptr;                       // [R_cap + T_max]
+    float** d_peer_y = nullptr;                   // [W]
+    unsigned long long** d_peer_flags = nullptr;  // [W]
+    int32_t* rowmap = nullptr;                    // [T_max * k + T_max]
     void* xsend = nullptr;     // [T_max*k x H] activation rows in canonical order
     void* xall = nullptr;      // [(R_cap + T_max) x H] received rows, then local tokens
     float* ysend = nullptr;    // [R_cap x H] expert outputs in arrival order
@@ -325,28 +355,70 @@ size_t ep_recv_cap(const hf_moe_ctx* c) {
     return size_t(c->world) * T * size_t(std::min(c->k, c->E_local));
 }
 
+// One value agreed by every rank: the minimum (or maximum) over the ranks of
+// `v`, through the communicator on a private stream.
+static hf_status allreduce_u64(EpState& e, unsigned long long* v, bool take_max) {
+    NcclApi& n = nccl();
+    unsigned long long* dv = nullptr;
+    HF_TRY(dalloc(&dv, 1));
+    cudaStream_t st = nullptr;
+    hf_status s = HF_OK;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMemcpy(dv, v, sizeof(*v), cudaMemcpyHostToDevice) != cudaSuccess) {
+        s = fail(HF_ERR_CUDA, "expert-parallel agreement: staging failed");
+    } else {
+        const ncclResult_t r =
+            n.AllReduce(dv, dv, 1, ncclUint64, take_max ? ncclMax : ncclMin, e.comm, st);
+        if (r != ncclSuccess) s = nccl_fail(r, "ncclAllReduce");
+        else if (cudaStreamSynchronize(st) != cudaSuccess ||
+                 cudaMemcpy(v, dv, sizeof(*v), cudaMemcpyDeviceToHost) != cudaSuccess)
+            s = fail(HF_ERR_CUDA, "expert-parallel agreement: read-back failed");
+    }
+    if (st) cudaStreamDestroy(st);
+    cudaFree(dv);
+    return s;
+}
+
 // Maps every rank's slab receive buffers, counts and flags into this process
-// (CUDA IPC handles gathered over the communicator). Any failure leaves the
-// NCCL slab exchange in place.
+// (CUDA IPC handles gathered over the communicator). The ranks agree on the
+// outcome: peer memory is used only when every rank mapped every peer, else
+// every rank closes its mappings and all fall back to the NCCL exchanges
+// together (a rank alone on NCCL would wait forever for sends its peers never
+// make). Every rank therefore takes part in both exchanges below whatever
+// fails locally. Test hook: HF_EP_FAIL_P2P_ON_RANK=r makes rank r report a
+// failed mapping after it has opened its peers' handles.
+struct HandleBlob {
+    cudaIpcMemHandle_t h[4];
+    int ok;
+    int pad[3];
+};
+
 static hf_status setup_p2p(hf_moe_ctx* c) {
     EpState& e = *c->ep;
     NcclApi& n = nccl();
     const int W = c->world, me = c->rank;
     if (W > kEpMaxRanks) return fail(HF_ERR_ARG, "peer-memory exchange: too many ranks");
-    HF_TRY(dalloc(&e.flags, size_t(2) * W));
-    HF_CUDA(cudaMemset(e.flags, 0, sizeof(unsigned long long) * 2 * W));
     constexpr int kBufs = 4;
+    HandleBlob mine{};
+    mine.ok = 1;
+    if (dalloc(&e.flags, size_t(2) * W) != HF_OK ||
+        cudaMemset(e.flags, 0, sizeof(unsigned long long) * 2 * W) != cudaSuccess)
+        mine.ok = 0;
     void* mine_ptr[kBufs] = {e.xslab_recv, e.yslab_recv, e.cnt_recv, e.flags};
-    cudaIpcMemHandle_t mine[kBufs];
-    for (int i = 0; i < kBufs; ++i) HF_CUDA(cudaIpcGetMemHandle(&mine[i], mine_ptr[i]));
-    const size_t hb = sizeof(mine);
+    for (int i = 0; i < kBufs && mine.ok; ++i)
+        if (cudaIpcGetMemHandle(&mine.h[i], mine_ptr[i]) != cudaSuccess) mine.ok = 0;
+    if (!mine.ok) {
+        cudaGetLastError();
+        std::memset(mine.h, 0, sizeof(mine.h));
+    }
+    const size_t hb = sizeof(HandleBlob);
     char* dev = nullptr;
     HF_TRY(dalloc(&dev, size_t(W) * hb));
     cudaStream_t st = nullptr;
     hf_status s = HF_OK;
-    std::vector<cudaIpcMemHandle_t> all(size_t(W) * kBufs);
+    std::vector<HandleBlob> all(static_cast<size_t>(W));
     if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMemcpy(dev + size_t(me) * hb, mine, hb, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaMemcpy(dev + size_t(me) * hb, &mine, hb, cudaMemcpyHostToDevice) != cudaSuccess) {
         s = fail(HF_ERR_CUDA, "peer-memory exchange: handle staging failed");
     } else {
         n.GroupStart();
@@ -362,18 +434,36 @@ static hf_status setup_p2p(hf_moe_ctx* c) {
     if (st) cudaStreamDestroy(st);
     cudaFree(dev);
     HF_TRY(s);
-    for (int d = 0; d < W; ++d) {
-        void* p[kBufs] = {mine_ptr[0], mine_ptr[1], mine_ptr[2], mine_ptr[3]};
-        if (d != me)
-            for (int i = 0; i < kBufs; ++i) {
-                HF_CUDA(cudaIpcOpenMemHandle(&p[i], all[size_t(d) * kBufs + i],
-                                             cudaIpcMemLazyEnablePeerAccess));
-                e.opened.push_back(p[i]);
-            }
-        e.peers.x[d] = static_cast<char*>(p[0]);
-        e.peers.y[d] = static_cast<float*>(p[1]);
-        e.peers.cnt[d] = static_cast<int32_t*>(p[2]);
-        e.peers.flags[d] = static_cast<unsigned long long*>(p[3]);
+    bool every_handle = true;
+    for (int d = 0; d < W; ++d) every_handle = every_handle && all[size_t(d)].ok;
+    unsigned long long mapped = every_handle ? 1 : 0;
+    if (every_handle) {
+        for (int d = 0; d < W && mapped; ++d) {
+            void* p[kBufs] = {mine_ptr[0], mine_ptr[1], mine_ptr[2], mine_ptr[3]};
+            if (d != me)
+                for (int i = 0; i < kBufs; ++i) {
+                    if (cudaIpcOpenMemHandle(&p[i], all[size_t(d)].h[i],
+                                             cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                        cudaGetLastError();
+                        mapped = 0;
+                        break;
+                    }
+                    e.opened.push_back(p[i]);
+                }
+            e.peers.x[d] = static_cast<char*>(p[0]);
+            e.peers.y[d] = static_cast<float*>(p[1]);
+            e.peers.cnt[d] = static_cast<int32_t*>(p[2]);
+            e.peers.flags[d] = static_cast<unsigned long long*>(p[3]);
+        }
+        const char* hook = std::getenv("HF_EP_FAIL_P2P_ON_RANK");
+        if (hook && std::atoi(hook) == me) mapped = 0;
+    }
+    HF_TRY(allreduce_u64(e, &mapped, false));  // every rank, every time
+    if (!mapped) {
+        for (void* p : e.opened) cudaIpcCloseMemHandle(p);
+        e.opened.clear();
+        e.peers = PeerPtrs{};
+        return fail(HF_ERR_CUDA, "peer-memory exchange unavailable on some rank");
     }
     e.p2p = true;
     return HF_OK;
@@ -406,7 +496,8 @@ hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
                          slab_bytes <= kEpP2PSlabBytes;
     if (try_p2p || slab_bytes <= kEpSlabBytes) {
         HF_TRY(dalloc(&e->xslab_recv, (size_t(W) * cap + T) * row4));
-        HF_TRY(dalloc(&e->yslab_recv, size_t(W) * cap * c->H));
+        // output slab: rows from every rank, then this rank's own shared-expert rows
+        HF_TRY(dalloc(&e->yslab_recv, (size_t(W) * cap + T) * c->H));
         HF_TRY(dalloc(&e->recv_tot, size_t(W)));
     }
     if (try_p2p && setup_p2p(c) != HF_OK) {
@@ -417,6 +508,13 @@ hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
     }
     if (e->p2p) {
         e->cap = int(cap);
+        HF_TRY(dalloc(&e->yrow, e->R_cap + T));
+        HF_TRY(dalloc(&e->d_peer_y, size_t(W)));
+        HF_TRY(dalloc(&e->d_peer_flags, size_t(W)));
+        HF_TRY(dalloc(&e->rowmap, T * c->k + T));
+        HF_CUDA(cudaMemcpy(e->d_peer_y, e->peers.y, sizeof(float*) * W, cudaMemcpyHostToDevice));
+        HF_CUDA(cudaMemcpy(e->d_peer_flags, e->peers.flags, sizeof(unsigned long long*) * W,
+                           cudaMemcpyHostToDevice));
     } else if (slab_bytes <= kEpSlabBytes) {
         e->cap = int(cap);
         HF_TRY(dalloc(&e->xslab_send, size_t(W) * cap * row4));
@@ -448,7 +546,8 @@ void ep_destroy(hf_moe_ctx* c) {
     if (e->comm) nccl().CommDestroy(e->comm);
     void* d[] = {e->xsend,      e->xall,       e->ysend,      e->yrecv,     e->cnt_recv,
                  e->loc_counts, e->row_pos,    e->xslab_send, e->xslab_recv, e->yslab_send,
-                 e->yslab_recv, e->recv_tot, e->flags};
+                 e->yslab_recv, e->recv_tot,   e->flags,      e->yrow,      e->d_peer_y,
+                 e->d_peer_flags, e->rowmap};
     for (void* p : d) cudaFree(p);
     void* h[] = {e->h_src, e->h_recv, e->h_perm, e->h_rowpos, e->h_loc};
     for (void* p : h)
@@ -476,6 +575,21 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
 
     // 1. route the local tokens over all experts; rows into per-destination slabs
     const RouteArgs ra = route_args(c, L, x, xd, T);
+    // Expert paths of the receiver. Tiles and the GEMV threshold follow the
+    // whole job's batch (T x W tokens): each local expert sees about as many
+    // rows as it would on one GPU. On peer memory with every segment on the
+    // tensor-core GEMM, the down GEMM's epilogue stores each output row
+    // straight into its source's output slab and its last CTA raises the
+    // return flags, so the return overlaps the GEMM and no copy kernel runs.
+    RouteArgs rl = ra;
+    rl.plan = c->plan;
+    rl.pl = c->pl;
+    set_gemm_tiles(c->gemm_bn, T * W, rl);
+    rl.gemv_max = gemv_threshold(c, T * W);
+    const bool maybe_gemm = rl.gemm_ok && (c->cfg.path == HF_PATH_GEMM || rows + T > rl.gemv_max);
+    const bool maybe_gemv = !rl.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
+                            (c->cfg.path == HF_PATH_AUTO && rl.gemv_max > 0);
+    const bool fused = e.p2p && e.yrow && maybe_gemm && !maybe_gemv;
     if (T > 0) {
         HF_TRY(run_route(c, L, ra, st));
     } else {
@@ -488,7 +602,8 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         PhaseTimer px(c, st, 7);
         k_ep_pack_p2p<<<copy_grid(c->nsm, std::max(1, T * k)), 256, 0, st>>>(
             c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, static_cast<const uint4*>(x),
-            int(rowb / 16), T * k, k, El, cap, c->rank, W, cnt_src, e.peers, c->sched + 6, seq);
+            int(rowb / 16), T * k, k, El, cap, c->rank, W, cnt_src, e.peers, c->sched + 6, seq,
+            fused ? e.rowmap : nullptr, has_shared ? T : 0);
         HF_CUDA(cudaGetLastError());
         px.done(1);
     } else {
@@ -519,21 +634,16 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         HF_CUDA(cudaMemcpyAsync(e.xslab_recv + size_t(rows) * rowb, x, size_t(T) * rowb,
                                 cudaMemcpyDeviceToDevice, st));
 
-    // 3. receiver plan on the device, then the local experts. Tiles and the
-    // GEMV threshold follow the whole job's batch (T x W tokens): each local
-    // expert sees about as many rows as it would on one GPU.
-    RouteArgs rl = ra;
-    rl.plan = c->plan;
-    rl.pl = c->pl;
-    set_gemm_tiles(c->gemm_bn, T * W, rl);
-    rl.gemv_max = gemv_threshold(c, T * W);
+    // 3. receiver plan on the device, then the local experts
     {
         PhaseTimer pp(c, st, 1);
+        const EpRowOut ro{fused ? e.yrow : nullptr, e.d_peer_y, c->rank, H};
         HF_TRY(launch_ep_plan(rl, e.cnt_recv, W, El, cap, T, c->perm, e.row_pos, e.recv_tot,
-                              e.p2p ? e.flags : nullptr, seq, c->timeout_ns, err, st));
+                              e.p2p ? e.flags : nullptr, seq, c->timeout_ns, err, ro, st));
         pp.done(1);
     }
     ExpertWork w{};
+    w.down_f16 = L.down_f16;
     w.plan = c->plan;
     w.pl = c->pl;
     w.perm = c->perm;
@@ -547,10 +657,29 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     w.m1 = rl.gemm_m1;
     w.m2 = rl.gemm_m2;
     w.pair = rl.gemm_pair;
-    w.maybe_gemm = rl.gemm_ok && (c->cfg.path == HF_PATH_GEMM || rows + T > rl.gemv_max);
-    w.maybe_gemv = !rl.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
-                   (c->cfg.path == HF_PATH_AUTO && rl.gemv_max > 0);
+    w.maybe_gemm = maybe_gemm;
+    w.maybe_gemv = maybe_gemv;
+    if (fused) {
+        w.yrow = e.yrow;
+        w.sig_flags = e.d_peer_flags;
+        w.sig_n = W;
+        w.sig_slot = W + c->rank;
+        w.sig_seq = seq;
+    }
     HF_TRY(run_experts(c, L, w, st));
+
+    if (fused) {
+        // 4. every rank's outputs for this rank's tokens are in its output slab
+        // once every return flag shows this forward; 5. combine from there
+        PhaseTimer py(c, st, 8);
+        k_ep_wait<<<1, 32, 0, st>>>(e.flags + W, W, seq, c->timeout_ns, err);
+        HF_CUDA(cudaGetLastError());
+        py.done(1);
+        if (T > 0)
+            HF_TRY(run_combine(c, e.yslab_recv, T, out, resid, r ? r->slot_out : nullptr, st,
+                               e.rowmap));
+        return HF_OK;
+    }
 
     // 4. outputs back to their sources in arrival order, then to canonical positions
     const int row4 = H / 4;
@@ -674,6 +803,7 @@ static hf_status ep_forward_sized(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         pp.done(1);
     }
     ExpertWork w{};
+    w.down_f16 = L.down_f16;
     w.plan = c->plan;
     w.pl = c->pl;
     w.perm = c->perm;
@@ -721,9 +851,193 @@ hf_status ep_forward(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int
     return ep_forward_sized(c, L, x, xd, T, out, resid, r, st);
 }
 
+// ------------------------------------------------------------------ expert placement
+// Router rows and bias of a placed layer: written in global expert order by
+// the weight setters, then gathered into placed order (row j <- order[j]).
+hf_status place_router(hf_moe_ctx* c, LayerBuf& L, cudaStream_t st) {
+    if (L.order.empty()) return HF_OK;
+    const size_t rows = size_t(c->E), rb = size_t(c->H) * 2;
+    uint16_t* tmp = nullptr;
+    HF_TRY(dalloc(&tmp, rows * c->H));
+    hf_status s = launch_gather_rows(tmp, L.router, rb, int(rows), L.d_order, 1, st);
+    if (s == HF_OK &&
+        cudaMemcpyAsync(L.router, tmp, rows * rb, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        s = fail(HF_ERR_CUDA, "router placement copy failed");
+    std::vector<float> b(rows), pb(rows);
+    if (s == HF_OK &&
+        (cudaMemcpyAsync(b.data(), L.bias, sizeof(float) * rows, cudaMemcpyDeviceToHost, st) !=
+             cudaSuccess ||
+         cudaStreamSynchronize(st) != cudaSuccess))
+        s = fail(HF_ERR_CUDA, "bias placement read failed");
+    if (s == HF_OK) {
+        for (size_t j = 0; j < rows; ++j) pb[j] = b[size_t(L.order[j])];
+        if (cudaMemcpy(L.bias, pb.data(), sizeof(float) * rows, cudaMemcpyHostToDevice) !=
+            cudaSuccess)
+            s = fail(HF_ERR_CUDA, "bias placement write failed");
+    }
+    cudaStreamSynchronize(st);
+    cudaFree(tmp);
+    return s;
+}
+
+// Routing outputs in global expert ids from the placed ones: ids through
+// order[], counts to their experts, offsets rescanned, and each expert's
+// segment of the permutation moved to its global offset (the order inside a
+// segment, token then slot, does not depend on the labels). One block.
+__global__ void __launch_bounds__(1024) k_unplace(const int32_t* order, int E, int T, int k,
+                                                  const int32_t* ids_p, const int32_t* cnt_p,
+                                                  const int32_t* off_p, const int32_t* perm_p,
+                                                  int32_t* ids_o, int32_t* cnt_o, int32_t* off_o,
+                                                  int32_t* perm_o) {
+    extern __shared__ int32_t sm_u[];
+    const int G = E + 1;
+    int32_t* s_cnt = sm_u;          // [G] global order
+    int32_t* s_off = s_cnt + G;     // [G + 1] global order
+    int32_t* s_offp = s_off + G + 1;  // [G + 1] placed order
+    for (int j = threadIdx.x; j < G; j += blockDim.x) {
+        const int e = j < E ? order[j] : E;
+        s_cnt[e] = cnt_p[j];
+    }
+    for (int j = threadIdx.x; j <= G; j += blockDim.x) s_offp[j] = off_p[j];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int e = 0; e < G; ++e) {
+            s_off[e] = acc;
+            acc += s_cnt[e];
+        }
+        s_off[G] = acc;
+    }
+    __syncthreads();
+    if (cnt_o)
+        for (int e = threadIdx.x; e < G; e += blockDim.x) cnt_o[e] = s_cnt[e];
+    if (off_o)
+        for (int e = threadIdx.x; e <= G; e += blockDim.x) off_o[e] = s_off[e];
+    if (ids_o)
+        for (int i = threadIdx.x; i < T * k; i += blockDim.x) ids_o[i] = order[ids_p[i]];
+    if (perm_o) {
+        const int n = s_offp[G];
+        for (int p = threadIdx.x; p < n; p += blockDim.x) {
+            int lo = 0, hi = G - 1;  // group j of placed position p: s_offp[j] <= p < s_offp[j+1]
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (s_offp[mid] <= p) lo = mid;
+                else hi = mid - 1;
+            }
+            const int e = lo < E ? order[lo] : E;
+            perm_o[s_off[e] + (p - s_offp[lo])] = perm_p[p];
+        }
+    }
+}
+
+hf_status unplace_routing(hf_moe_ctx* c, const LayerBuf& L, const hf_moe_routing* r, int T,
+                          cudaStream_t st) {
+    const int G = c->E + 1;
+    const size_t smem = sizeof(int32_t) * size_t(3 * G + 2);
+    HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_unplace), int(smem)));
+    k_unplace<<<1, 1024, smem, st>>>(L.d_order, c->E, T, c->k, c->ids, c->plan_src + c->pl_src.counts,
+                                     c->plan_src + c->pl_src.offsets, c->perm_src, r->topk_ids,
+                                     r->counts, r->offsets, r->perm);
+    HF_CUDA(cudaGetLastError());
+    return HF_OK;
+}
+
+int ep_transport(const hf_moe_ctx* c) {
+    if (!c->ep) return 0;
+    if (c->ep->p2p) return 1;
+    return c->ep->cap > 0 ? 2 : 3;
+}
+
+// Every rank: wait for this rank's work, clear the error word, and adopt the
+// largest forward sequence number of any rank, so that the next forward waits
+// for flags that only that forward's stores can raise (flags left by a
+// forward that ran on fewer than all ranks are below it).
+hf_status ep_resync(hf_moe_ctx* c) {
+    EpState& e = *c->ep;
+    HF_CUDA(cudaDeviceSynchronize());
+    HF_CUDA(cudaMemset(c->plan + c->pl.stats + 3, 0, sizeof(int)));
+    unsigned long long s = e.seq;
+    HF_TRY(allreduce_u64(e, &s, true));
+    e.seq = s;
+    return HF_OK;
+}
+
 }  // namespace hf
 
 using namespace hf;
+
+extern "C" hf_status hf_moe_set_placement(hf_moe_ctx* ctx, int layer, const int32_t* order) {
+    if (!ctx) return fail(HF_ERR_ARG, "hf_moe_set_placement: null context");
+    if (layer < 0 || layer >= int(ctx->layers.size()))
+        return fail(HF_ERR_ARG, "hf_moe_set_placement: layer out of range");
+    const int E = ctx->E;
+    std::vector<int32_t> ord(static_cast<size_t>(E)), inv(static_cast<size_t>(E), -1);
+    bool identity = true;
+    for (int j = 0; j < E; ++j) {
+        const int e = order ? order[j] : j;
+        if (e < 0 || e >= E || inv[size_t(e)] >= 0)
+            return fail(HF_ERR_ARG, "hf_moe_set_placement: order is not a permutation of 0..E-1");
+        ord[size_t(j)] = e;
+        inv[size_t(e)] = j;
+        identity = identity && e == j;
+    }
+    DeviceGuard dg(ctx->cfg.device);
+    HF_TRY(ctx_layer_alloc(ctx, layer));
+    LayerBuf& L = ctx->layers[layer];
+    const bool same = identity ? L.order.empty() : L.order == ord;
+    if (same) return HF_OK;
+    if (identity) {
+        L.order.clear();
+        L.inv.clear();
+    } else {
+        if (!L.d_order) HF_TRY(dalloc(&L.d_order, size_t(E)));
+        HF_CUDA(cudaMemcpy(L.d_order, ord.data(), sizeof(int32_t) * E, cudaMemcpyHostToDevice));
+        L.order = std::move(ord);
+        L.inv = std::move(inv);
+    }
+    L.loaded = false;  // the rank's experts changed: the weights are set again
+    return HF_OK;
+}
+
+extern "C" hf_status hf_ep_balanced_placement(int E, int world, const long long* load,
+                                              int32_t* order) {
+    if (E <= 0 || world <= 0 || E % world || !load || !order)
+        return fail(HF_ERR_ARG, "hf_ep_balanced_placement: bad arguments (E must divide by world)");
+    const int El = E / world;
+    std::vector<int> idx(static_cast<size_t>(E));
+    std::iota(idx.begin(), idx.end(), 0);
+    // heaviest first (ties: lower id), each to the least-loaded rank with room
+    std::stable_sort(idx.begin(), idx.end(),
+                     [&](int a, int b) { return load[a] > load[b]; });
+    std::vector<long long> sum(static_cast<size_t>(world), 0);
+    std::vector<std::vector<int>> own(static_cast<size_t>(world));
+    for (int e : idx) {
+        int best = -1;
+        for (int r = 0; r < world; ++r)
+            if (int(own[size_t(r)].size()) < El && (best < 0 || sum[size_t(r)] < sum[size_t(best)]))
+                best = r;
+        own[size_t(best)].push_back(e);
+        sum[size_t(best)] += load[e];
+    }
+    for (int r = 0; r < world; ++r) {
+        std::sort(own[size_t(r)].begin(), own[size_t(r)].end());
+        for (int l = 0; l < El; ++l) order[size_t(r) * El + l] = own[size_t(r)][size_t(l)];
+    }
+    return HF_OK;
+}
+
+extern "C" hf_status hf_moe_ep_transport(hf_moe_ctx* ctx, int* transport) {
+    if (!ctx || !transport) return fail(HF_ERR_ARG, "hf_moe_ep_transport: null argument");
+    *transport = ep_transport(ctx);
+    return HF_OK;
+}
+
+extern "C" hf_status hf_moe_ep_resync(hf_moe_ctx* ctx) {
+    if (!ctx) return fail(HF_ERR_ARG, "hf_moe_ep_resync: null context");
+    if (!ctx->ep) return HF_OK;
+    DeviceGuard dg(ctx->cfg.device);
+    return ep_resync(ctx);
+}
 
 extern "C" hf_status hf_ep_unique_id(unsigned char* out) {
     if (!out) return fail(HF_ERR_ARG, "hf_ep_unique_id: null output");

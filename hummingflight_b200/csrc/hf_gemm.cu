@@ -29,6 +29,7 @@
 #include <mutex>
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "hf_internal.cuh"
 #include "hf_sm100.cuh"
@@ -75,6 +76,7 @@ struct GemmCfg {
 };
 
 struct TileInfo {
+    int g;             // group (expert) of the tile
     int seg, n0, n, m0, mvalid;
     int kb0, kb1;      // K blocks [kb0, kb1) of this tile (split-K runs)
     int rowA0, rowA1;
@@ -106,6 +108,7 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, const PlanView& p
     const int nt = (c + a.bn - 1) / a.bn;
     const int local = u - p.pref[g];
     const int mi = local / nt, ni = local % nt;
+    t.g = g;
     t.shared = (g == G - 1);
     const int Ig = t.shared ? a.Is : a.I;
     t.seg = p.off[g];
@@ -361,7 +364,9 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             }
             tc_fence_after();
             const uint32_t nmma = PAIR ? uint32_t((t.n + 31) & ~31) : uint32_t((t.n + 15) & ~15);
-            const uint32_t idesc = PAIR ? idesc_bf16_m256(nmma) : idesc_bf16_m128(nmma);
+            const bool f16 = a.down_f16 && a.which == 2;  // FP16 down rows x FP16 mid
+            const uint32_t idesc = PAIR ? (f16 ? idesc_f16_m256(nmma) : idesc_bf16_m256(nmma))
+                                        : (f16 ? idesc_f16_m128(nmma) : idesc_bf16_m128(nmma));
             const uint32_t d0 = tmem_base + acc * C::kAccCols;
             for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
                 const uint32_t s = it % S, ph = (it / S) & 1;
@@ -448,8 +453,24 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                     if constexpr (NUM_A == 2) tmem_ld32(ta + BN + c0, v1);
                 }
                 tmem_ld_wait();
-                if (NUM_A == 2 && a.which == 1) {  // gate/up pair -> SwiGLU -> hi/lo planes
-                    if (rv) {
+                if (NUM_A == 2 && a.which == 1) {  // gate/up pair -> SwiGLU -> mid planes
+                    if (rv && a.down_f16) {
+                        // one FP16 plane: mid * 2^-kMidF16Shift (exact scaling, one rounding)
+                        const size_t o0 = size_t(t.seg + t.n0 + c0) * a.Imax + t.m0 + rr;
+                        __half* ph = reinterpret_cast<__half*>(a.mid_hi) + o0;
+                        bool over = false;
+#pragma unroll
+                        for (int j = 0; j < CW; ++j) {
+                            if (c0 + j < t.n) {
+                                const float m = __fmul_rn(
+                                    swiglu_fast(__uint_as_float(v0[j]), __uint_as_float(v1[j])),
+                                    1.0f / float(1 << kMidF16Shift));
+                                over = over || !(fabsf(m) <= 65504.0f);
+                                ph[size_t(j) * a.Imax] = __float2half_rn(m);
+                            }
+                        }
+                        if (over) atomicOr(a.err, 8);  // beyond the FP16 range: HF_ERR_RANGE
+                    } else if (rv) {
                         // column c0 of this row in both planes; one row of mid per column
                         const size_t o0 = size_t(t.seg + t.n0 + c0) * a.Imax + t.m0 + rr;
                         __nv_bfloat16* ph = reinterpret_cast<__nv_bfloat16*>(a.mid_hi) + o0;
@@ -467,14 +488,19 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                         }
                     }
                 } else if (!a.resid) {  // down rows m0 + r (and m0 + 128 + r) -> fp32 outputs
+                    // FP16 pass: the product carries 2^S (weights) and 2^-6 (mid); both
+                    // powers of two, so undoing them is exact
+                    const float sc = (a.which == 2 && a.down_f16)
+                                         ? a.groups[t.g].down_scale * float(1 << kMidF16Shift)
+                                         : 1.0f;
 #pragma unroll
                     for (int j = 0; j < CW; ++j) {
                         const int col = c0 + j;
                         if (col < t.n) {
                             const size_t pos = size_t(t.seg + t.n0 + col);
-                            float* yr = a.y + t.yoff + pos * a.H + t.m0 + rr;
-                            if (rv) yr[0] = __uint_as_float(v0[j]);
-                            if (NUM_A == 2 && rv1) yr[kRow1] = __uint_as_float(v1[j]);
+                            float* yr = (a.yrow ? a.yrow[pos] : a.y + t.yoff + pos * a.H) + t.m0 + rr;
+                            if (rv) yr[0] = __fmul_rn(__uint_as_float(v0[j]), sc);
+                            if (NUM_A == 2 && rv1) yr[kRow1] = __fmul_rn(__uint_as_float(v1[j]), sc);
                         }
                     }
                 } else {  // residual block (dense MLP): y = resid + down row; the thread
@@ -511,6 +537,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
         }
     }
     __syncwarp();  // reconverge warps 0 and 1 (one lane of each ran a role loop)
+    if (a.sig_flags) __threadfence_system();  // this thread's output stores, system-wide
     tc_fence_before();
     __syncthreads();
     if constexpr (PAIR) cluster_sync();  // no remote arrive or TMEM write targets a finished CTA
@@ -528,6 +555,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             a.sched[0] = 0;
             a.sched[1] = 0;
             __threadfence();
+            if (a.sig_flags) {  // every CTA's outputs are out: tell their owners
+                __threadfence_system();
+                for (int d = 0; d < a.sig_n; ++d) st_release_sys(a.sig_flags[d] + a.sig_slot, a.sig_seq);
+            }
         }
     }
 }
@@ -643,10 +674,16 @@ static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cuda
 }
 
 hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid, cudaStream_t st) {
-    if (a.pair && a.which == 2 && a.mrows == 512 && num_b == 2) {
-        // prefill down: 512-row tiles on CTA pairs (two 256-row MMA blocks)
-        if (a.bn == 128) return launch_one<2, 2, 128, true>(m, a, grid, st);
-        if (a.bn == 256) return launch_one<2, 2, 256, true>(m, a, grid, st);
+    if (a.pair && a.which == 2 && a.mrows == 512) {
+        // prefill down: 512-row tiles on CTA pairs (two 256-row MMA blocks);
+        // one mid plane on the FP16 pass, hi + lo on the BF16 one
+        if (num_b == 2) {
+            if (a.bn == 128) return launch_one<2, 2, 128, true>(m, a, grid, st);
+            if (a.bn == 256) return launch_one<2, 2, 256, true>(m, a, grid, st);
+        } else {
+            if (a.bn == 128) return launch_one<2, 1, 128, true>(m, a, grid, st);
+            if (a.bn == 256) return launch_one<2, 1, 256, true>(m, a, grid, st);
+        }
     }
     if (a.pair && a.which == 1) {  // prefill gate/up: 256-row tiles on CTA pairs
         if (a.bn == 128 && a.mrows == 256)
@@ -664,12 +701,14 @@ hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid,
                                           : launch_one<2, 2, 64>(m, a, grid, st);
         if (a.bn == 128) return num_b == 1 ? launch_one<2, 1, 128>(m, a, grid, st)
                                            : launch_one<2, 2, 128>(m, a, grid, st);
-    } else if (num_b == 1) {  // single-plane B (router logits): bf16 activations
+    } else if (num_b == 1) {  // single-plane B: router logits (bf16) or the FP16 down pass
         if (a.mrows == 256) {
+            if (a.bn == 16) return launch_one<2, 1, 16>(m, a, grid, st);
             if (a.bn == 32) return launch_one<2, 1, 32>(m, a, grid, st);
             if (a.bn == 64) return launch_one<2, 1, 64>(m, a, grid, st);
             if (a.bn == 128) return launch_one<2, 1, 128>(m, a, grid, st);
         } else if (a.mrows == 128) {
+            if (a.bn == 16) return launch_one<1, 1, 16>(m, a, grid, st);
             if (a.bn == 32) return launch_one<1, 1, 32>(m, a, grid, st);
             if (a.bn == 64) return launch_one<1, 1, 64>(m, a, grid, st);
             if (a.bn == 128) return launch_one<1, 1, 128>(m, a, grid, st);

@@ -22,6 +22,8 @@
 #include <mutex>
 #include <tuple>
 
+#include <cuda_fp16.h>
+
 #include "hf_internal.cuh"
 
 namespace hf {
@@ -174,7 +176,21 @@ __global__ void __launch_bounds__(256) k_gemv1(GemvArgs a) {
 }
 
 // Four down rows (h0..h0+3) against NT mid vectors (fp32, shared memory).
-template <int NT>
+// Eight FP16 weights (a down block in the FP16 resident format, w * 2^S).
+__device__ __forceinline__ void unpack8_f16(const uint4& v, float (&o)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[q]));
+        o[2 * q] = f.x;
+        o[2 * q + 1] = f.y;
+    }
+}
+
+// F16: the down block holds FP16 w * 2^S; the sums carry 2^S exactly and
+// are multiplied by W.down_scale = 2^-S at the end (the same bits as the
+// BF16 block would give).
+template <int NT, bool F16>
 __device__ __forceinline__ void gemv2_rows(const GroupW& W, int H, int h0, const float* ms,
                                            int lane, float* y, int p0, const float* resid) {
     const int I = W.inter;
@@ -199,7 +215,10 @@ __device__ __forceinline__ void gemv2_rows(const GroupW& W, int H, int h0, const
         for (int q = 0; q < kUnroll; ++q) {
             float wf[4][8];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) unpack8(wv[q][r], wf[r]);
+            for (int r = 0; r < 4; ++r) {
+                if constexpr (F16) unpack8_f16(wv[q][r], wf[r]);
+                else unpack8(wv[q][r], wf[r]);
+            }
 #pragma unroll
             for (int j = 0; j < NT; ++j) {
                 float xf[8];
@@ -217,7 +236,10 @@ __device__ __forceinline__ void gemv2_rows(const GroupW& W, int H, int h0, const
         for (int r = 0; r < 4; ++r) wv[r] = ld_stream_u4(pr[r] + size_t(c) * 8);
         float wf[4][8];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) unpack8(wv[r], wf[r]);
+        for (int r = 0; r < 4; ++r) {
+            if constexpr (F16) unpack8_f16(wv[r], wf[r]);
+            else unpack8(wv[r], wf[r]);
+        }
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
             float xf[8];
@@ -231,7 +253,10 @@ __device__ __forceinline__ void gemv2_rows(const GroupW& W, int H, int h0, const
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int j = 0; j < NT; ++j) acc[r][j] = warp_sum(acc[r][j]);
+        for (int j = 0; j < NT; ++j) {
+            acc[r][j] = warp_sum(acc[r][j]);
+            if constexpr (F16) acc[r][j] = __fmul_rn(acc[r][j], W.down_scale);
+        }
 #pragma unroll
     for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -278,11 +303,20 @@ __global__ void __launch_bounds__(256) k_gemv2(GemvArgs a) {
         }
         __syncthreads();
         const int h0 = rb * kGemv2Rows + warp * 4;
-        switch (te) {
-            case 1: gemv2_rows<1>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
-            case 2: gemv2_rows<2>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
-            case 3: gemv2_rows<3>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
-            default: gemv2_rows<4>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+        if (W.down_f16) {
+            switch (te) {
+                case 1: gemv2_rows<1, true>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+                case 2: gemv2_rows<2, true>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+                case 3: gemv2_rows<3, true>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+                default: gemv2_rows<4, true>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+            }
+        } else {
+            switch (te) {
+                case 1: gemv2_rows<1, false>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+                case 2: gemv2_rows<2, false>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+                case 3: gemv2_rows<3, false>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+                default: gemv2_rows<4, false>(W, H, h0, ms, lane, a.y, p0, a.resid); break;
+            }
         }
         if (a.prefetch_shared && g == G - 1 && ch == nch - 1 && h0 < H) {
             // last use of these shared down rows: back to normal L2 priority

@@ -754,11 +754,12 @@ hf_status hf_moe_load_safetensors(hf_moe_ctx* ctx, int layer, int model_layer,
     int experts = 0, skipped = 0;
     for (int e = 0; e < E; ++e) {
         const std::string x = "experts." + std::to_string(e) + ".";
-        if (e < ctx->e_begin || e >= ctx->e_begin + ctx->E_local) {
+        const int l = local_slot(ctx, L, e);
+        if (l < 0) {
             skipped += where.count(pre + x + "gate_proj.weight") ? 1 : 0;
             continue;
         }
-        uint16_t* b = L.experts + size_t(e - ctx->e_begin) * ctx->expert_elems;
+        uint16_t* b = L.experts + size_t(l) * ctx->expert_elems;
         HF_TRY(need(x + "gate_proj.weight", "BF16", {I, H}, b, false));
         HF_TRY(need(x + "up_proj.weight", "BF16", {I, H}, b + size_t(I) * H, false));
         HF_TRY(need(x + "down_proj.weight", "BF16", {H, I}, b + size_t(2) * I * H, false));
@@ -773,6 +774,8 @@ hf_status hf_moe_load_safetensors(hf_moe_ctx* ctx, int layer, int model_layer,
     if (!has_bias) HF_CUDA(cudaMemset(L.bias, 0, sizeof(float) * size_t(E)));
     HF_CUDA(cudaDeviceSynchronize());  // the layer's buffers exist before other streams write
     HF_TRY(upload(ctx->cfg.device, copies));
+    HF_TRY(place_router(ctx, L, nullptr));  // the router rows in the layer's expert placement
+    down_written(L, -1);
     L.has_bias = has_bias;
     L.loaded = true;
     if (stats) {

@@ -50,8 +50,10 @@ constexpr int kGemvAutoMax = 1;
 struct GroupW {
     const uint16_t* gate;  // [inter x H]
     const uint16_t* up;    // [inter x H]
-    const uint16_t* down;  // [H x inter]
+    const uint16_t* down;  // [H x inter]: BF16, or FP16 holding w * 2^S when down_f16
     int inter;
+    int down_f16;          // the down block is stored as FP16 (see down_scale)
+    float down_scale;      // 2^-S: multiplies products with the FP16 down block
     int pad;
 };
 
@@ -258,10 +260,18 @@ hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cud
 // Expert-parallel receiver plan from device counts (fixed-capacity slabs of
 // `cap` rows per source); see k_ep_plan. With `flags` it first waits (bounded)
 // for every source's arrival flag to reach `seq` (peer-memory exchange).
+// Output rows of an expert-parallel receiver's positions (yrow == nullptr:
+// none written): peer_y[s] is rank s's output slab as mapped here.
+struct EpRowOut {
+    float** yrow;            // [positions] device
+    float* const* peer_y;    // [W] device
+    int rank, H;
+};
 hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, int W, int El, int cap, int T_loc,
                          int32_t* perm, int32_t* row_pos, int32_t* recv_tot,
                          const unsigned long long* flags, unsigned long long seq,
-                         unsigned long long timeout_ns, int* err, cudaStream_t st);
+                         unsigned long long timeout_ns, int* err, const EpRowOut& ro,
+                         cudaStream_t st);
 // Dense MLP pass: one group of all T tokens in order; writes groups[0] = w.
 hf_status launch_dense_plan(const RouteArgs& a, const GroupW& w, GroupW* groups, int32_t* perm,
                             int* sched, cudaStream_t st);
@@ -328,7 +338,26 @@ struct GemmArgs {
     // tile scheduler: [0] next tile id, [1] CTAs done; zero before a launch,
     // left zero by it (device memory owned by the caller, one pair per stream)
     int* sched;
+    // optional (GEMM2, nsplit == 1, no resid): output row of position p at
+    // yrow[p] instead of y + p * H -- a row in another GPU's memory (a peer
+    // mapping) when an expert-parallel receiver returns outputs from the
+    // epilogue. With sig_flags set, every thread fences its stores system-wide
+    // and the last CTA out stores sig_seq (release, system scope) to
+    // sig_flags[d][sig_slot] for d < sig_n.
+    float* const* yrow;
+    unsigned long long* const* sig_flags;
+    int sig_n, sig_slot;
+    unsigned long long sig_seq;
+    // FP16 down pass: GEMM1 writes mid as one FP16 plane holding mid * 2^-kMidF16Shift
+    // (mid_hi), GEMM2 multiplies FP16 down rows (w * 2^S) by it and scales its
+    // accumulator by 2^kMidF16Shift * groups[g].down_scale
+    int down_f16;
+    const GroupW* groups;
 };
+// mid is stored as FP16 times 2^-6: finite up to 65504 * 64 ~ 4.2e6, full
+// 11-bit precision from 2^-8 up; smaller values keep an absolute error
+// below 2^-19
+constexpr int kMidF16Shift = 6;
 struct GemmMaps {
     CUtensorMap A, A_sh;       // weights: routed view; shared expert gate (GEMM1) or down rows
     CUtensorMap A_sh2;         // shared expert up rows (GEMM1)

@@ -298,6 +298,8 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.timeout_ns = c->timeout_ns;
         gm.test_stall = c->stall;
         gm.sched = c->sched;
+        gm.down_f16 = w.down_f16;
+        gm.groups = L.groups;
         GemmMaps m1 = c->maps1;
         m1.A = L.gu;
         m1.A_sh = L.sh_gate;
@@ -315,23 +317,28 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.which = 2;
         gm.bn = w.bn2;
         gm.mrows = w.m2;
+        gm.yrow = w.yrow;
+        gm.sig_flags = w.sig_flags;
+        gm.sig_n = w.sig_n;
+        gm.sig_slot = w.sig_slot;
+        gm.sig_seq = w.sig_seq;
         GemmMaps m2 = c->maps2;
         m2.A = L.dn;
         m2.A_sh = L.sh_down;
         m2.A_sh2 = L.sh_down;
         PhaseTimer p5(c, st, 5);
-        HF_TRY(launch_gemm(m2, gm, 2, c->nsm, st));
+        HF_TRY(launch_gemm(m2, gm, w.down_f16 ? 1 : 2, c->nsm, st));
         p5.done(1);
     }
     return HF_OK;
 }
 
 hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, const float* resid,
-                      float* slot_out, cudaStream_t st) {
+                      float* slot_out, cudaStream_t st, const int32_t* slot_pos) {
     CombineArgs ca{};
     ca.resid = resid;
     ca.y = y;
-    ca.slot_pos = c->slot_pos;
+    ca.slot_pos = slot_pos ? slot_pos : c->slot_pos;
     ca.w = c->w;
     ca.T = T;
     ca.H = c->H;
@@ -363,6 +370,7 @@ const char* hf_status_string(hf_status s) {
         case HF_ERR_OOM: return "HF_ERR_OOM";
         case HF_ERR_STATE: return "HF_ERR_STATE";
         case HF_ERR_UNSUPPORTED: return "HF_ERR_UNSUPPORTED";
+        case HF_ERR_RANGE: return "HF_ERR_RANGE";
     }
     return "HF_ERR_UNKNOWN";
 }
@@ -377,6 +385,11 @@ static void free_ctx(hf_moe_ctx* c) {
         cudaFree(L.experts);
         cudaFree(L.shared);
         cudaFree(L.groups);
+        cudaFree(L.d_order);
+        cudaFree(L.d_blocks);
+        cudaFree(L.d_list);
+        cudaFree(L.d_absmax);
+        cudaFree(L.d_scale);
     }
     for (auto& m : c->marks) {
         cudaEventDestroy(m.a);
@@ -397,6 +410,10 @@ static void free_ctx(hf_moe_ctx* c) {
 static hf_status take_error_word(hf_moe_ctx* c, int word) {
     if (word == 0) return HF_OK;
     HF_CUDA(cudaMemset(c->plan + c->pl.stats + 3, 0, sizeof(int)));
+    if (word == 8)
+        return fail(HF_ERR_RANGE,
+                    "a SwiGLU intermediate exceeded the FP16 down pass's range (|mid| > 4.2e6); "
+                    "outputs of that forward are invalid (HF_DOWN_F16=0 keeps the BF16 hi + lo pass)");
     return fail(HF_ERR_TIMEOUT,
                 "a bounded device wait in the tcgen05 GEMM gave up; the kernel drained and "
                 "returned, outputs of that forward are invalid");
@@ -591,6 +608,8 @@ static hf_status layer_alloc(hf_moe_ctx* c, int layer) {
             w.gate = w.up = w.down = nullptr;
             w.inter = 0;
         }
+        w.down_f16 = 0;
+        w.down_scale = 1.0f;
         w.pad = 0;
     }
     HF_CUDA(cudaMemcpy(L.groups, tab.data(), sizeof(GroupW) * c->G, cudaMemcpyHostToDevice));
@@ -635,6 +654,7 @@ hf_status hf_moe_set_router(hf_moe_ctx* ctx, int layer, const uint16_t* router_b
     HF_CUDA(cudaMemcpy(L.router, router_bf16, sizeof(uint16_t) * ctx->E * ctx->H, kind_of(kind)));
     if (bias) HF_CUDA(cudaMemcpy(L.bias, bias, sizeof(float) * ctx->E, kind_of(kind)));
     else HF_CUDA(cudaMemset(L.bias, 0, sizeof(float) * ctx->E));
+    HF_TRY(place_router(ctx, L, nullptr));
     L.has_bias = bias != nullptr;
     L.loaded = true;
     return HF_OK;
@@ -644,13 +664,14 @@ hf_status hf_moe_set_expert(hf_moe_ctx* ctx, int layer, int eid, const uint16_t*
                             hf_mem_kind kind) {
     HF_TRY(check_layer(ctx, layer, "hf_moe_set_expert"));
     if (!gud) return fail(HF_ERR_ARG, "hf_moe_set_expert: null weights");
-    if (eid < ctx->e_begin || eid >= ctx->e_begin + ctx->E_local)
-        return fail(HF_ERR_ARG, "hf_moe_set_expert: expert id not owned by this context");
+    const int l = local_slot(ctx, ctx->layers[layer], eid);
+    if (l < 0) return fail(HF_ERR_ARG, "hf_moe_set_expert: expert id not owned by this context");
     DeviceGuard dg(ctx->cfg.device);
     HF_TRY(layer_alloc(ctx, layer));
     LayerBuf& L = ctx->layers[layer];
-    HF_CUDA(cudaMemcpy(L.experts + size_t(eid - ctx->e_begin) * ctx->expert_elems, gud,
+    HF_CUDA(cudaMemcpy(L.experts + size_t(l) * ctx->expert_elems, gud,
                        sizeof(uint16_t) * ctx->expert_elems, kind_of(kind)));
+    down_written(L, l);
     return HF_OK;
 }
 
@@ -658,16 +679,18 @@ hf_status hf_moe_set_expert_parts(hf_moe_ctx* ctx, int layer, int eid, const uin
                                   const uint16_t* up, const uint16_t* down, hf_mem_kind kind) {
     HF_TRY(check_layer(ctx, layer, "hf_moe_set_expert_parts"));
     if (!gate || !up || !down) return fail(HF_ERR_ARG, "hf_moe_set_expert_parts: null projection");
-    if (eid < ctx->e_begin || eid >= ctx->e_begin + ctx->E_local)
+    const int l = local_slot(ctx, ctx->layers[layer], eid);
+    if (l < 0)
         return fail(HF_ERR_ARG, "hf_moe_set_expert_parts: expert id not owned by this context");
     DeviceGuard dg(ctx->cfg.device);
     HF_TRY(layer_alloc(ctx, layer));
     LayerBuf& L = ctx->layers[layer];
-    uint16_t* b = L.experts + size_t(eid - ctx->e_begin) * ctx->expert_elems;
+    uint16_t* b = L.experts + size_t(l) * ctx->expert_elems;
     const size_t n = size_t(ctx->I) * ctx->H;
     HF_CUDA(cudaMemcpy(b, gate, sizeof(uint16_t) * n, kind_of(kind)));
     HF_CUDA(cudaMemcpy(b + n, up, sizeof(uint16_t) * n, kind_of(kind)));
     HF_CUDA(cudaMemcpy(b + 2 * n, down, sizeof(uint16_t) * n, kind_of(kind)));
+    down_written(L, l);
     return HF_OK;
 }
 
@@ -683,6 +706,7 @@ hf_status hf_moe_set_shared(hf_moe_ctx* ctx, int layer, const uint16_t* gate, co
     HF_CUDA(cudaMemcpy(L.shared, gate, sizeof(uint16_t) * n, kind_of(kind)));
     HF_CUDA(cudaMemcpy(L.shared + n, up, sizeof(uint16_t) * n, kind_of(kind)));
     HF_CUDA(cudaMemcpy(L.shared + 2 * n, down, sizeof(uint16_t) * n, kind_of(kind)));
+    down_written(L, ctx->G - 1);
     return HF_OK;
 }
 
@@ -694,12 +718,15 @@ hf_status hf_moe_expert_device_ptr(hf_moe_ctx* ctx, int layer, int eid, uint16_t
     LayerBuf& L = ctx->layers[layer];
     if (eid == ctx->E) {
         if (!L.shared) return fail(HF_ERR_STATE, "no shared expert in this config");
+        HF_TRY(down_to_bf16(ctx, L, ctx->G - 1));  // the BF16 layout while the caller holds it
         *dev_ptr = L.shared;
         return HF_OK;
     }
-    if (eid < ctx->e_begin || eid >= ctx->e_begin + ctx->E_local)
+    const int l = local_slot(ctx, L, eid);
+    if (l < 0)
         return fail(HF_ERR_ARG, "hf_moe_expert_device_ptr: expert id not owned by this context");
-    *dev_ptr = L.experts + size_t(eid - ctx->e_begin) * ctx->expert_elems;
+    HF_TRY(down_to_bf16(ctx, L, l));
+    *dev_ptr = L.experts + size_t(l) * ctx->expert_elems;
     return HF_OK;
 }
 
@@ -718,13 +745,28 @@ hf_status hf_moe_mark_loaded(hf_moe_ctx* ctx, int layer) {
     HF_TRY(check_layer(ctx, layer, "hf_moe_mark_loaded"));
     if (!ctx->layers[layer].router) return fail(HF_ERR_STATE, "layer has no weights");
     ctx->layers[layer].loaded = true;
+    ctx->layers[layer].down_ready = false;  // the next forward checks the down blocks again
     return HF_OK;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-static hf_status copy_routing(hf_moe_ctx* c, const hf_moe_routing* r, int T, cudaStream_t st) {
+static hf_status copy_routing(hf_moe_ctx* c, const LayerBuf& L, const hf_moe_routing* r, int T,
+                              cudaStream_t st) {
     if (!r) return HF_OK;
+    if (T == 0) {  // an empty batch routes nothing: zero counts and offsets
+        if (r->counts) HF_CUDA(cudaMemsetAsync(r->counts, 0, sizeof(int32_t) * c->G_src, st));
+        if (r->offsets)
+            HF_CUDA(cudaMemsetAsync(r->offsets, 0, sizeof(int32_t) * (c->G_src + 1), st));
+        return HF_OK;
+    }
+    if (!L.order.empty()) {  // placed expert ids: outputs in global ids
+        const cudaMemcpyKind d2d = cudaMemcpyDeviceToDevice;
+        if (r->topk_weights)
+            HF_CUDA(cudaMemcpyAsync(r->topk_weights, c->w, sizeof(float) * T * c->k, d2d, st));
+        if (r->margins) HF_CUDA(cudaMemcpyAsync(r->margins, c->margins, sizeof(float) * T, d2d, st));
+        return unplace_routing(c, L, r, T, st);
+    }
     const int k = c->k, G = c->G_src;
     const size_t nslots = size_t(T) * k + (c->Is > 0 ? T : 0);
     const cudaMemcpyKind d2d = cudaMemcpyDeviceToDevice;
@@ -753,20 +795,17 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
     c->last_stream = st;
     if (c->world > 1 && !route_only) {
         // every rank takes part in the exchanges, even with no tokens of its own
+        HF_TRY(ensure_down_format(c, L, st));
         HF_TRY(ep_forward(c, L, x, xd, T, out, resid, r, st));
-        return copy_routing(c, r, T, st);
+        return copy_routing(c, L, r, T, st);
     }
-    if (T == 0) {  // an empty batch routes nothing: report zero counts and offsets
-        if (r && r->counts)
-            HF_CUDA(cudaMemsetAsync(r->counts, 0, sizeof(int32_t) * c->G_src, st));
-        if (r && r->offsets)
-            HF_CUDA(cudaMemsetAsync(r->offsets, 0, sizeof(int32_t) * (c->G_src + 1), st));
-        return HF_OK;
-    }
+    if (T == 0) return copy_routing(c, L, r, T, st);  // zero counts and offsets
+    if (!route_only) HF_TRY(ensure_down_format(c, L, st));
     const RouteArgs ra = route_args(c, L, x, xd, T);
     HF_TRY(run_route(c, L, ra, st));
     if (!route_only) {
         ExpertWork w{};
+        w.down_f16 = L.down_f16;
         w.plan = c->plan;
         w.pl = c->pl;
         w.perm = c->perm;
@@ -787,7 +826,7 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
         HF_TRY(run_experts(c, L, w, st));
         HF_TRY(run_combine(c, c->y, T, out, resid, r ? r->slot_out : nullptr, st));
     }
-    return copy_routing(c, r, T, st);
+    return copy_routing(c, L, r, T, st);
 }
 
 hf_status hf_moe_forward(hf_moe_ctx* ctx, int layer, const void* x, hf_dtype x_dtype, int T,
@@ -959,10 +998,11 @@ hf_status hf_moe_synth_layer(hf_moe_ctx* ctx, int layer, uint64_t seed, uint32_t
         HF_TRY(synth_f32u(L.bias, size_t(ctx->E), synth_key(seed, gen_layer, HF_SYNTH_BIAS, 0),
                           -0.1f, 0.1f, st));
     L.has_bias = true;
+    HF_TRY(place_router(ctx, L, st));
     const size_t n = size_t(ctx->I) * ctx->H;
     for (int e = 0; e < ctx->E_local; ++e) {
         uint16_t* b = L.experts + size_t(e) * ctx->expert_elems;
-        const uint32_t eid = uint32_t(ctx->e_begin + e);
+        const uint32_t eid = uint32_t(slot_expert(ctx, L, e));
         HF_TRY(synth_bf16(b, n, synth_key(seed, gen_layer, HF_SYNTH_GATE, eid), sc, st));
         HF_TRY(synth_bf16(b + n, n, synth_key(seed, gen_layer, HF_SYNTH_UP, eid), sc, st));
         HF_TRY(synth_bf16(b + 2 * n, n, synth_key(seed, gen_layer, HF_SYNTH_DOWN, eid), sc, st));
@@ -975,6 +1015,7 @@ hf_status hf_moe_synth_layer(hf_moe_ctx* ctx, int layer, uint64_t seed, uint32_t
         HF_TRY(synth_bf16(L.shared + 2 * ns, ns, synth_key(seed, gen_layer, HF_SYNTH_DOWN, eid), sc, st));
     }
     if (bias_override) HF_CUDA(cudaStreamSynchronize(st));  // host array may go away
+    down_written(L, -1);
     L.loaded = true;
     return HF_OK;
 }

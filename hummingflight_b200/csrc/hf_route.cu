@@ -568,12 +568,17 @@ hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cud
 // arrival -- the order the host plan of the large-batch exchange uses -- and
 // the shared expert's T_loc local tokens come last (rows W * cap + t). Also
 // writes row_pos (slab row -> local position) and recv_tot[s] (rows from s).
+// With yrow set it also writes each position's output row: received row i
+// from source s goes back to row rank * cap + i of s's output slab
+// (peer_y[s], mapped here), a local token t to row W * cap + t of this rank's
+// own slab (peer_y[rank]).
 __global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cnt, int W, int El,
                                                   int cap, int T_loc, int32_t* perm,
                                                   int32_t* row_pos, int32_t* recv_tot,
                                                   const unsigned long long* flags,
                                                   unsigned long long seq,
-                                                  unsigned long long timeout_ns, int* err) {
+                                                  unsigned long long timeout_ns, int* err,
+                                                  EpRowOut ro) {
     extern __shared__ __align__(16) uint32_t sm[];
     // peer-memory exchange: counts and rows are in place once every source's
     // flag shows this forward's sequence number
@@ -611,26 +616,32 @@ __global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cn
         const int n = cnt[sj];
         const int pos0 = s_off[sj % El] + s_pos[sj];
         const int row0 = (sj / El) * cap + s_src[sj];
+        const int s = sj / El;
+        float* yb = ro.yrow ? ro.peer_y[s] + (size_t(ro.rank) * cap + s_src[sj]) * ro.H : nullptr;
         for (int i = 0; i < n; ++i) {
             perm[pos0 + i] = row0 + i;  // slot id = row of [slabs | local tokens] (k = 1)
             row_pos[row0 + i] = pos0 + i;
+            if (yb) ro.yrow[pos0 + i] = yb + size_t(i) * ro.H;
         }
     }
     if (a.has_shared)  // slot ids past all rows name the local tokens (token_of_slot)
-        for (int t = threadIdx.x; t < T_loc; t += blockDim.x)
+        for (int t = threadIdx.x; t < T_loc; t += blockDim.x) {
             perm[s_off[El] + t] = (rows + T_loc) + (rows + t);
+            if (ro.yrow) ro.yrow[s_off[El] + t] = ro.peer_y[ro.rank] + size_t(rows + t) * ro.H;
+        }
 }
 
 hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, int W, int El, int cap, int T_loc,
                          int32_t* perm, int32_t* row_pos, int32_t* recv_tot,
                          const unsigned long long* flags, unsigned long long seq,
-                         unsigned long long timeout_ns, int* err, cudaStream_t st) {
+                         unsigned long long timeout_ns, int* err, const EpRowOut& ro,
+                         cudaStream_t st) {
     const int G = a.pl.G;
     if (G != El + 1 || G > 2 * 1024) return fail(HF_ERR_ARG, "expert-parallel plan: bad group count");
     const size_t smem = sizeof(int) * (G + G + 1 + kPlanScratch + 2 * W * El);
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_ep_plan), int(smem)));
     k_ep_plan<<<1, 1024, smem, st>>>(a, cnt, W, El, cap, T_loc, perm, row_pos, recv_tot, flags, seq,
-                                     timeout_ns, err);
+                                     timeout_ns, err, ro);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }

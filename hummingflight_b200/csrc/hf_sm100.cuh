@@ -171,6 +171,9 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t smem_addr) {
 __device__ __forceinline__ uint32_t idesc_bf16_m128(uint32_t n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
 }
+__device__ __forceinline__ uint32_t idesc_f16_m128(uint32_t n) {
+    return (1u << 4) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+}
 
 // ------------------------------------------------------------------ CTA pairs (cta_group::2)
 // A cluster of two CTAs on two SMs computes one M = 256 tile: CTA r holds A
@@ -278,6 +281,11 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
 // Instruction descriptor of a pair MMA: M = 256 across the two CTAs.
 __device__ __forceinline__ uint32_t idesc_bf16_m256(uint32_t n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((256u >> 4) << 24);
+}
+// The same with FP16 A and B (format fields 0): both operands of one
+// kind::f16 MMA are always of one type.
+__device__ __forceinline__ uint32_t idesc_f16_m256(uint32_t n) {
+    return (1u << 4) | ((n >> 3) << 17) | ((256u >> 4) << 24);
 }
 
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {

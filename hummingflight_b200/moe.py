@@ -242,6 +242,24 @@ class MoELayer:
         bounded device wait gave up in one of the forwards since the last check."""
         call("hf_moe_synchronize", self._h)
 
+    def set_placement(self, layer: int, order):
+        """Expert placement of a layer (hf_moe_set_placement): rank r owns the
+        experts order[r*E/W:(r+1)*E/W]. Set the layer's weights afterwards."""
+        o = None if order is None else np.ascontiguousarray(order, np.int32)
+        call("hf_moe_set_placement", self._h, layer, _ptr(o))
+
+    EP_TRANSPORTS = {0: "none", 1: "peer", 2: "nccl_slabs", 3: "nccl_sized"}
+
+    def ep_transport(self) -> str:
+        """The exchange the ranks agreed on at create (hf_moe_ep_transport)."""
+        v = ctypes.c_int()
+        call("hf_moe_ep_transport", self._h, ctypes.byref(v))
+        return self.EP_TRANSPORTS[v.value]
+
+    def ep_resync(self):
+        """Every rank, between forwards, after a forward some rank skipped."""
+        call("hf_moe_ep_resync", self._h)
+
     def set_wait_timeout(self, ns: int):
         call("hf_moe_set_wait_timeout", self._h, ns)
 
@@ -277,6 +295,15 @@ class MoELayer:
             self.close()
         except Exception:
             pass
+
+
+def balanced_placement(load, world: int) -> np.ndarray:
+    """hf_ep_balanced_placement: an expert order for set_placement that
+    balances `load` [E] (e.g. calibration token counts) over `world` ranks."""
+    ld = np.ascontiguousarray(load, np.int64)
+    order = np.empty(ld.size, np.int32)
+    call("hf_ep_balanced_placement", int(ld.size), int(world), _ptr(ld), _ptr(order))
+    return order
 
 
 def gemv_bf16_f32(A, x, y, M: int, K: int, alpha: float = 1.0, beta: float = 0.0, stream=None):
@@ -375,7 +402,7 @@ def synth_f32_uniform(dst, seed: int, layer: int, kind: int, expert: int, lo: fl
     return dst
 
 
-__all__ = ["MoELayer", "gemv_bf16_f32", "top_k_scores", "dense_mlp_forward",
+__all__ = ["MoELayer", "balanced_placement", "gemv_bf16_f32", "top_k_scores", "dense_mlp_forward",
            "dense_mlp_workspace_size", "dense_mlp_status", "dense_block_forward", "rmsnorm",
            "synth_bf16_normal",
            "synth_f32_uniform", "HfError", "HF_BF16", "HF_F32"]

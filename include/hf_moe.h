@@ -48,7 +48,9 @@ typedef enum hf_status {
     HF_ERR_TIMEOUT = 4,     /* a bounded device wait gave up (error word set)   */
     HF_ERR_OOM = 5,         /* device allocation failed                         */
     HF_ERR_STATE = 6,       /* call out of order (e.g. weights not set)         */
-    HF_ERR_UNSUPPORTED = 7  /* no device / wrong architecture                   */
+    HF_ERR_UNSUPPORTED = 7, /* no device / wrong architecture                   */
+    HF_ERR_RANGE = 8        /* a SwiGLU intermediate beyond the FP16 down pass's
+                               range (|silu(g) * u| > 4.2e6): outputs invalid    */
 } hf_status;
 
 typedef enum hf_mem_kind { HF_MEM_HOST = 0, HF_MEM_DEVICE = 1 } hf_mem_kind;
@@ -183,19 +185,58 @@ HF_API hf_status hf_moe_set_wait_timeout(hf_moe_ctx* ctx, uint64_t ns);
 HF_API hf_status hf_moe_debug_stall(hf_moe_ctx* ctx, int enable);
 
 /* Expert parallelism (no reference counterpart: the reference is a single
- * process on one host). With ep_world = W > 1 each rank's context holds the
- * experts [rank*E/W, (rank+1)*E/W) plus the shared expert, and
- * hf_moe_forward routes the rank's own T tokens, exchanges token rows and
- * expert outputs with the other ranks over NCCL (one host synchronization per
- * forward, after the per-expert counts arrive) and combines at the source in
- * the reference's rank order, so outputs equal the single-GPU outputs. Every
- * rank must call the same forwards in the same order (T may differ, even 0).
+ * process on one host). With ep_world = W > 1 each rank's context holds E/W
+ * experts (by default [rank*E/W, (rank+1)*E/W); see hf_moe_set_placement)
+ * plus the shared expert, and hf_moe_forward routes the rank's own T tokens,
+ * exchanges token rows and expert outputs with the other ranks and combines
+ * at the source in the reference's rank order, so outputs equal the
+ * single-GPU outputs. The exchange is peer memory over NVLink when every rank
+ * can map every other (stores into the other ranks' buffers, arrival flags
+ * with bounded waits, no host synchronization; the down GEMM returns its
+ * outputs from its epilogue), else NCCL (hf_moe_ep_transport). Every rank
+ * must call the same forwards in the same order (T may differ, even 0).
  * NCCL is loaded at run time (libnccl.so.2). */
 /* A fresh NCCL unique id (128 bytes) for hf_moe_config.ep_unique_id; rank 0
  * makes it and the caller broadcasts it to the other ranks. An id serves one
  * set of contexts (one communicator): make a new one for every hf_moe_create
  * round. */
 HF_API hf_status hf_ep_unique_id(unsigned char* out128);
+
+/* Expert placement of one layer (expert parallelism). order [E] lists global
+ * expert ids; rank r owns the experts order[r*E/W .. (r+1)*E/W - 1] (the
+ * default is order[j] = j, contiguous ranges). All ranks pass the same order.
+ * Call before the layer's weights: the rank keeps only its own experts, so a
+ * new placement marks the layer unloaded until its router (hf_moe_set_router,
+ * hf_moe_synth_layer or hf_moe_load_safetensors) and experts are set again.
+ * Ids everywhere in the API stay global (set_expert, routing outputs); with
+ * a placement, write the router through hf_moe_set_router, not through the
+ * pointer of hf_moe_router_device_ptr. No reference counterpart: the
+ * reference keeps every expert on one host (its LRU/placement tiers decide
+ * only which tier holds a weight, engine/scheduler.cpp). */
+HF_API hf_status hf_moe_set_placement(hf_moe_ctx* ctx, int layer, const int32_t* order);
+
+/* A placement that balances expected work: experts sorted by load (e.g.
+ * routed token counts from a calibration batch, plus a constant for the
+ * weight stream of an active expert), heaviest first, each to the least
+ * loaded rank that still has room for E/world experts; each rank's experts
+ * in ascending id. Writes order [E] for hf_moe_set_placement. */
+HF_API hf_status hf_ep_balanced_placement(int E, int world, const long long* load, int32_t* order);
+
+/* The exchange an expert-parallel context uses, agreed by all its ranks at
+ * hf_moe_create: 0 none (one GPU), 1 peer memory over NVLink (CUDA IPC
+ * mappings of the other ranks' slabs), 2 fixed slabs over NCCL, 3 NCCL with
+ * counts read on the host. No reference counterpart (the reference runs on
+ * one host process with no collective backend). */
+HF_API hf_status hf_moe_ep_transport(hf_moe_ctx* ctx, int* transport);
+
+/* Recovery after a forward that did not run on every rank (a rank skipped it,
+ * so the others' bounded waits ran out and reported HF_ERR_TIMEOUT). Every
+ * rank calls it, between forwards: it waits for the rank's own work, clears
+ * the error, and agrees on the forward sequence numbers (one all-reduce), so
+ * the next forward on all ranks is valid again. The counterpart of the
+ * reference's bounded waits that give up and continue
+ * (engine/scheduler.cpp:696-722). */
+HF_API hf_status hf_moe_ep_resync(hf_moe_ctx* ctx);
 /* The host-side order of one exchange, as the forward builds it (for tests
  * and external transports): send_counts / recv_counts [W x E_local] are the
  * rows this rank sends to / receives from each rank per local expert;

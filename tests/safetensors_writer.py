@@ -2,7 +2,7 @@
 bytes after the JSON header: 8-byte little-endian header length, the header
 padded with spaces to a multiple of 8, tensor data 8-byte aligned -- the layout
 the checkpoint loader's strict options require (model/safetensors.h:32-48).
-Used to build checkpoints for the ingest benchmark and for tests.
+Used to build checkpoints for the tests and for `bench.py --probe ingest`.
 """
 from __future__ import annotations
 

@@ -83,8 +83,8 @@ def test_open_missing_file_fails():
 
 
 def test_package_writer_round_trip(tmp_path):
-    """hummingflight_b200.safetensors_writer output passes the strict checks."""
-    from hummingflight_b200.safetensors_writer import write_file
+    """tests/safetensors_writer.py output passes the strict checks."""
+    from safetensors_writer import write_file
     S = st()
     rng = np.random.default_rng(11)
     a = rng.integers(0, 1 << 16, (5, 7), dtype=np.uint16)      # 70 bytes: the next start pads
