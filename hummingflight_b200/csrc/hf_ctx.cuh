@@ -204,6 +204,7 @@ struct ExpertWork {
     bool maybe_gemm;   // some segment may take the GEMM / the GEMV (else skip the launches)
     bool maybe_gemv;
     int down_f16 = 0;  // the layer's down blocks are FP16 (GemmArgs::down_f16)
+    int groups_base = 0;  // the plan's group g is the layer's group groups_base + g
     // GEMM2 outputs through per-position row pointers and the end-of-kernel
     // flag release (GemmArgs::yrow / sig_*); GEMM path only
     float* const* yrow = nullptr;

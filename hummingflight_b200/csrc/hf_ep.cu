@@ -336,6 +336,11 @@ struct EpState {
     float** d_peer_y = nullptr;                   // [W]
     unsigned long long** d_peer_flags = nullptr;  // [W]
     int32_t* rowmap = nullptr;                    // [T_max * k + T_max]
+    // the shared expert on the local tokens while the dispatch is in flight:
+    // the dispatch runs on `side`, ordered by the two events
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_routed = nullptr, ev_packed = nullptr;
+    GroupW* shared_group = nullptr;               // [1] the plan kernel's group slot
     void* xsend = nullptr;     // [T_max*k x H] activation rows in canonical order
     void* xall = nullptr;      // [(R_cap + T_max) x H] received rows, then local tokens
     float* ysend = nullptr;    // [R_cap x H] expert outputs in arrival order
@@ -515,6 +520,10 @@ hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
         HF_CUDA(cudaMemcpy(e->d_peer_y, e->peers.y, sizeof(float*) * W, cudaMemcpyHostToDevice));
         HF_CUDA(cudaMemcpy(e->d_peer_flags, e->peers.flags, sizeof(unsigned long long*) * W,
                            cudaMemcpyHostToDevice));
+        HF_CUDA(cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking));
+        HF_CUDA(cudaEventCreateWithFlags(&e->ev_routed, cudaEventDisableTiming));
+        HF_CUDA(cudaEventCreateWithFlags(&e->ev_packed, cudaEventDisableTiming));
+        HF_TRY(dalloc(&e->shared_group, size_t(1)));
     } else if (slab_bytes <= kEpSlabBytes) {
         e->cap = int(cap);
         HF_TRY(dalloc(&e->xslab_send, size_t(W) * cap * row4));
@@ -542,8 +551,13 @@ hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
 void ep_destroy(hf_moe_ctx* c) {
     EpState* e = c->ep;
     if (!e) return;
+    if (e->side) cudaStreamSynchronize(e->side);
     for (void* p : e->opened) cudaIpcCloseMemHandle(p);
     if (e->comm) nccl().CommDestroy(e->comm);
+    if (e->side) cudaStreamDestroy(e->side);
+    if (e->ev_routed) cudaEventDestroy(e->ev_routed);
+    if (e->ev_packed) cudaEventDestroy(e->ev_packed);
+    cudaFree(e->shared_group);
     void* d[] = {e->xsend,      e->xall,       e->ysend,      e->yrecv,     e->cnt_recv,
                  e->loc_counts, e->row_pos,    e->xslab_send, e->xslab_recv, e->yslab_send,
                  e->yslab_recv, e->recv_tot,   e->flags,      e->yrow,      e->d_peer_y,
@@ -557,6 +571,60 @@ void ep_destroy(hf_moe_ctx* c) {
 }
 
 // ------------------------------------------------------------------ forward
+// The shared expert over this rank's own T tokens as a pass of its own (a
+// one-group plan, the tensor-core GEMMs), its outputs into rows W*cap + t of
+// this rank's output slab, where the combine reads them. It needs nothing
+// from the other ranks, so it runs while the dispatch is in flight.
+static hf_status ep_shared_pass(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T,
+                                cudaStream_t st) {
+    EpState& e = *c->ep;
+    RouteArgs ra{};
+    ra.T = T;
+    ra.H = c->H;
+    ra.plan = c->plan;  // rebuilt by the receiver plan right after this pass (same stream)
+    ra.pl = PlanLayout::make(1);
+    ra.has_shared = 1;
+    ra.shared_inter = c->Is;
+    ra.inter = c->Is;
+    ra.path = HF_PATH_GEMM;
+    ra.gemm_ok = 1;
+    set_gemm_tiles(c->gemm_bn, T, ra);
+    const size_t n = size_t(c->Is) * c->H;
+    GroupW w{L.shared, L.shared + n, L.shared + 2 * n, c->Is, 0, 1.0f, 0};  // GEMV fields: unused
+    {
+        PhaseTimer pp(c, st, 1);
+        HF_TRY(launch_dense_plan(ra, w, e.shared_group, c->perm, c->sched, st));
+        pp.done(1);
+    }
+    ExpertWork ws{};
+    ws.down_f16 = L.down_f16;
+    ws.plan = c->plan;
+    ws.pl = ra.pl;
+    ws.perm = c->perm;  // identity: slot t = token t (k = 0)
+    ws.x = x;
+    ws.x_f32 = xd == HF_F32;
+    ws.T = T;
+    ws.k = 0;
+    ws.y = e.yslab_recv + size_t(c->world) * e.cap * c->H;
+    ws.bn1 = ra.gemm_bn1;
+    ws.bn2 = ra.gemm_bn2;
+    ws.m1 = ra.gemm_m1;
+    ws.m2 = ra.gemm_m2;
+    ws.pair = ra.gemm_pair;
+    ws.maybe_gemm = true;
+    ws.maybe_gemv = false;
+    ws.groups_base = c->G - 1;  // the GEMM's group 0 is the layer's shared expert
+    return run_experts(c, L, ws, st);
+}
+
+static bool ep_shared_early() {
+    static const bool on = [] {
+        const char* v = std::getenv("HF_EP_SHARED_EARLY");  // tuning knob: 0 = one grouped pass
+        return !(v && std::atoi(v) == 0);
+    }();
+    return on;
+}
+
 // Slab exchange (peer memory at any size, NCCL for small batches): fixed
 // per-source regions, counts and plan stay on the device.
 static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T,
@@ -590,6 +658,8 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     const bool maybe_gemv = !rl.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
                             (c->cfg.path == HF_PATH_AUTO && rl.gemv_max > 0);
     const bool fused = e.p2p && e.yrow && maybe_gemm && !maybe_gemv;
+    // the shared expert runs as its own pass beside the dispatch (fused path)
+    const bool early = fused && has_shared && T > 0 && e.side && ep_shared_early();
     if (T > 0) {
         HF_TRY(run_route(c, L, ra, st));
     } else {
@@ -598,14 +668,26 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     const int32_t* cnt_src = c->plan_src + c->pl_src.counts;
     if (e.p2p) {
         // 2. rows straight into the destinations' slabs over NVLink, then the
-        // counts and this rank's arrival flag on every rank (even with T = 0)
-        PhaseTimer px(c, st, 7);
-        k_ep_pack_p2p<<<copy_grid(c->nsm, std::max(1, T * k)), 256, 0, st>>>(
+        // counts and this rank's arrival flag on every rank (even with T = 0);
+        // with `early`, on the side stream while the shared expert computes
+        cudaStream_t sp = st;
+        if (early) {
+            HF_CUDA(cudaEventRecord(e.ev_routed, st));
+            HF_CUDA(cudaStreamWaitEvent(e.side, e.ev_routed, 0));
+            sp = e.side;
+        }
+        PhaseTimer px(c, sp, 7);
+        k_ep_pack_p2p<<<copy_grid(c->nsm, std::max(1, T * k)), 256, 0, sp>>>(
             c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, static_cast<const uint4*>(x),
             int(rowb / 16), T * k, k, El, cap, c->rank, W, cnt_src, e.peers, c->sched + 6, seq,
             fused ? e.rowmap : nullptr, has_shared ? T : 0);
         HF_CUDA(cudaGetLastError());
         px.done(1);
+        if (early) {
+            HF_CUDA(cudaEventRecord(e.ev_packed, e.side));
+            HF_TRY(ep_shared_pass(c, L, x, xd, T, st));
+            HF_CUDA(cudaStreamWaitEvent(st, e.ev_packed, 0));
+        }
     } else {
         if (T > 0) {
             PhaseTimer p1(c, st, 1);
@@ -629,12 +711,14 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         HF_NCCL(n.GroupEnd());
         px.done(0);
     }
-    // local tokens after the slabs
-    if (T > 0)
+    // local tokens after the slabs (the shared expert's rows of the grouped pass)
+    if (T > 0 && !early)
         HF_CUDA(cudaMemcpyAsync(e.xslab_recv + size_t(rows) * rowb, x, size_t(T) * rowb,
                                 cudaMemcpyDeviceToDevice, st));
 
-    // 3. receiver plan on the device, then the local experts
+    // 3. receiver plan on the device (without the shared expert when it ran
+    // early), then the local experts
+    if (early) rl.has_shared = 0;
     {
         PhaseTimer pp(c, st, 1);
         const EpRowOut ro{fused ? e.yrow : nullptr, e.d_peer_y, c->rank, H};

@@ -8,22 +8,27 @@
 // N = the segment's tokens (up to BN per tile, rounded up to 16 at run time),
 // K = hidden (gate/up) or intermediate (down). Both operands are K-major, so
 // the reference's [gate | up | down] row-major weights feed the tensor cores
-// unchanged: one TMA box of 64 bf16 x 128 rows per weight matrix and k-block,
-// and boxes of 64 x 16 token rows for the activations.
+// unchanged: one TMA box of 64 elements x 128 rows per weight matrix and
+// k-block, and boxes of 64 x 16 token rows for the activations.
 //
-//   GEMM1  acc_g = Wg x^T, acc_u = Wu x^T (two TMEM accumulators); epilogue
-//          mid = g / (1 + exp(-g)) * u in fp32, stored as a BF16 hi + lo pair
-//          (hi = bf16(mid), lo = bf16(mid - hi)) so the next GEMM sees ~16
-//          mantissa bits instead of 8.
-//   GEMM2  acc = Wd mid_hi^T + Wd mid_lo^T; epilogue stores fp32 expert
-//          outputs y[position][h] for the deterministic combine.
+//   GEMM1  acc_g = Wg x^T, acc_u = Wu x^T (two TMEM accumulators, BF16 x
+//          BF16); epilogue mid = g / (1 + exp(-g)) * u in fp32, stored as one
+//          FP16 plane holding mid * 2^-6 when the layer's down blocks are FP16
+//          (hf_weights.cu), else as a BF16 hi + lo pair (hi = bf16(mid),
+//          lo = bf16(mid - hi)), so the next GEMM sees 11 or ~16 mantissa
+//          bits instead of BF16's 8.
+//   GEMM2  acc = Wd mid^T: one FP16 x FP16 pass (the accumulator scaled back
+//          by the powers of two), or Wd mid_hi^T + Wd mid_lo^T with BF16;
+//          epilogue stores fp32 expert outputs y[position][h] for the
+//          deterministic combine (or, for an expert-parallel receiver, into
+//          the row of its source's output slab).
 //
-// CTA = 6 warps, one CTA per SM, persistent over a static tile list:
-// warp 0 issues TMA loads into a STAGES-deep shared-memory ring, warp 1 owns
-// TMEM and issues tcgen05.mma from one thread, warps 2-5 drain the double-
-// buffered TMEM accumulators. Every wait is bounded (see hf_sm100.cuh): on
-// timeout the CTA drains its TMA loads and MMAs, frees TMEM and reports
-// HF_ERR_TIMEOUT through the error word instead of hanging.
+// CTA = 10 warps, one CTA (or one CTA of a pair) per SM, persistent over the
+// tile list: warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
+// warp 1 owns TMEM and issues tcgen05.mma from one thread, warps 2-9 drain the
+// TMEM accumulators (two warps per lane quadrant). Every wait is bounded (see
+// hf_sm100.cuh): on timeout the CTA drains its TMA loads and MMAs, frees TMEM
+// and reports HF_ERR_TIMEOUT through the error word instead of hanging.
 #include <algorithm>
 #include <map>
 #include <mutex>
@@ -439,20 +444,12 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             // 512-row tile) the second 256-row MMA block, this CTA's half of it
             constexpr int kRow1 = PAIR ? 256 : 128;
             const bool rv1 = rr + kRow1 < t.mvalid;
-            // columns per TMEM load: 32, or 16 for 16-token tiles (an x32 load
-            // would reach past the allocated columns)
-            constexpr int CW = BN < 32 ? BN : 32;
-            // the two warps of a quadrant take alternate column chunks
-            for (int c0 = ((warp - 2) / 4) * CW; c0 < t.n; c0 += 2 * CW) {
-                uint32_t v0[CW], v1[CW];
-                if constexpr (CW == 16) {
-                    tmem_ld16(ta + c0, v0);
-                    if constexpr (NUM_A == 2) tmem_ld16(ta + BN + c0, v1);
-                } else {
-                    tmem_ld32(ta + c0, v0);
-                    if constexpr (NUM_A == 2) tmem_ld32(ta + BN + c0, v1);
-                }
-                tmem_ld_wait();
+            // TMEM is read 16 columns at a time, one load in flight while the
+            // previous one is processed (a load's latency, not its bandwidth,
+            // bounds a drain that waits for each load before using it); the two
+            // warps of a quadrant take alternate 16-column chunks
+            constexpr int CW = 16;
+            auto process = [&](int c0, const uint32_t (&v0)[CW], const uint32_t (&v1)[CW]) {
                 if (NUM_A == 2 && a.which == 1) {  // gate/up pair -> SwiGLU -> mid planes
                     if (rv && a.down_f16) {
                         // one FP16 plane: mid * 2^-kMidF16Shift (exact scaling, one rounding)
@@ -527,6 +524,33 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                         }
                     }
                 }
+            };
+            uint32_t a0[CW], a1[CW], b0[CW], b1[CW];
+#pragma unroll
+            for (int j = 0; j < CW; ++j) a1[j] = b1[j] = 0u;  // untouched when NUM_A == 1
+            int c0 = ((warp - 2) / 4) * CW;
+            if (c0 < t.n) {
+                tmem_ld16(ta + c0, a0);
+                if constexpr (NUM_A == 2) tmem_ld16(ta + BN + c0, a1);
+            }
+            tmem_ld_wait_regs(a0, a1);
+            while (c0 < t.n) {
+                const int c1 = c0 + 2 * CW;
+                if (c1 < t.n) {
+                    tmem_ld16(ta + c1, b0);
+                    if constexpr (NUM_A == 2) tmem_ld16(ta + BN + c1, b1);
+                }
+                process(c0, a0, a1);
+                tmem_ld_wait_regs(b0, b1);
+                if (c1 >= t.n) break;
+                const int c2 = c1 + 2 * CW;
+                if (c2 < t.n) {
+                    tmem_ld16(ta + c2, a0);
+                    if constexpr (NUM_A == 2) tmem_ld16(ta + BN + c2, a1);
+                }
+                process(c1, b0, b1);
+                tmem_ld_wait_regs(a0, a1);
+                c0 = c2;
             }
             tc_fence_before();
             __syncwarp();

@@ -206,10 +206,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 __device__ __forceinline__ float swiglu(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
-// The same with the fast exponential and a rounded reciprocal (a few ulp from
-// swiglu): the tensor-core epilogue evaluates it for every element of a tile.
+// The same with the fast exponential and the fast division (a few ulp from
+// swiglu, far below the rounding of mid to FP16 or to a BF16 hi + lo pair):
+// the tensor-core epilogue evaluates it for every element of a tile. For
+// g < -88 the exponential overflows and the quotient is -0, as in swiglu.
 __device__ __forceinline__ float swiglu_fast(float g, float u) {
-    return __fmul_rn(__fmul_rn(g, __frcp_rn(__fadd_rn(1.0f, __expf(-g)))), u);
+    return __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), u);
 }
 
 __device__ __forceinline__ int token_of_slot(int slot, int T, int k) {

@@ -299,7 +299,7 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.test_stall = c->stall;
         gm.sched = c->sched;
         gm.down_f16 = w.down_f16;
-        gm.groups = L.groups;
+        gm.groups = L.groups + w.groups_base;
         GemmMaps m1 = c->maps1;
         m1.A = L.gu;
         m1.A_sh = L.sh_gate;
