@@ -134,7 +134,10 @@ def phase_bytes(shape, counts, T, k, path, gemv_max):
         w_gu = int((2 * inter[sel] * H * 2).sum())
         w_d = int((H * inter[sel] * 2).sum())
         slots = int(c[sel].sum())
-        mid_b = int((c[sel] * inter[sel]).sum()) * 4  # fp32 (GEMV) or BF16 hi + lo (GEMM)
+        # mid per element: fp32 on the GEMV, one FP16 plane on the GEMM's FP16
+        # down pass (a BF16 hi + lo pair with HF_DOWN_F16=0)
+        mid_e = 4 if name == "gemv" or os.environ.get("HF_DOWN_F16") == "0" else 2
+        mid_b = int((c[sel] * inter[sel]).sum()) * mid_e
         out[f"{name}_gate_up"] = w_gu + slots * H * 2 + mid_b
         out[f"{name}_down"] = w_d + mid_b + slots * H * 4
         out[f"{name}_gate_up_flops"] = int((2 * 2 * c[sel] * inter[sel] * H).sum())
@@ -569,11 +572,19 @@ def roofline(job, meas, args, pk, steps):
         achieved = flops / (per_launch_ms / 1e3) / 1e12
     else:
         achieved = alg / (per_launch_ms / 1e3) / 1e9 if alg else None
+    # DRAM bytes per launch from ncu: measured on this workload, or -- where the
+    # full workload is too large to capture -- the ratio of DRAM traffic to
+    # algorithmic bytes measured on a small case of the same kernel, scaled to
+    # this launch's algorithmic bytes
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
-            traffic = json.load(f).get(f"{wl.name}:{dom}")
+            t = json.load(f).get(f"{wl.name}:{dom}")
+        if isinstance(t, dict) and alg:
+            traffic = t["traffic_over_algorithmic"] * alg
+        elif isinstance(t, (int, float)):
+            traffic = t
     peak = tfl if tensor_bound else hbm
     return pb, {"bound": "tensor" if tensor_bound else "hbm", "kernel": dom,
                 "achieved": achieved, "peak": peak,

@@ -273,7 +273,16 @@ __global__ void __launch_bounds__(256) k_ep_pack_p2p(const int32_t* perm, const 
         const int r = p - offsets[d * El];
         const uint4* src = x + size_t(slot / k) * row_vec;
         uint4* dst = reinterpret_cast<uint4*>(pp.x[d]) + (size_t(rank) * cap + r) * row_vec;
-        for (int c = lane; c < row_vec; c += 32) dst[c] = ld_nc_u4(src + c);
+        // eight 16-byte loads in flight per lane before their stores cross NVLink
+        for (int c0 = lane; c0 < row_vec; c0 += 32 * 8) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c0 + 32 * u < row_vec) v[u] = ld_nc_u4(src + c0 + 32 * u);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c0 + 32 * u < row_vec) dst[c0 + 32 * u] = v[u];
+        }
         if (rowmap && lane == 0) rowmap[slot] = d * cap + r;
     }
     if (rowmap)
@@ -677,7 +686,12 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
             sp = e.side;
         }
         PhaseTimer px(c, sp, 7);
-        k_ep_pack_p2p<<<copy_grid(c->nsm, std::max(1, T * k)), 256, 0, sp>>>(
+        // beside the shared expert's kernels the pack takes one block per SM,
+        // which fits next to a GEMM CTA (a full grid would hold every SM until
+        // it drained and the two would run one after the other)
+        const int pack_grid = early ? std::min(c->nsm, copy_grid(c->nsm, std::max(1, T * k)))
+                                    : copy_grid(c->nsm, std::max(1, T * k));
+        k_ep_pack_p2p<<<pack_grid, 256, 0, sp>>>(
             c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, static_cast<const uint4*>(x),
             int(rowb / 16), T * k, k, El, cap, c->rank, W, cnt_src, e.peers, c->sched + 6, seq,
             fused ? e.rowmap : nullptr, has_shared ? T : 0);

@@ -651,6 +651,46 @@ __global__ void __launch_bounds__(256) k_gather_x(GatherArgs a) {
     }
 }
 
+// Token-major form of the bf16 gather: a warp reads token t's row once and
+// writes it to the positions of all of the token's slots (its k routed slots
+// and its shared-expert slot) that belong to GEMM segments. Each row is read
+// once instead of k + 1 times.
+__global__ void __launch_bounds__(256) k_gather_tokens(GatherArgs a) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    const int G = a.pl.G;
+    const int32_t* offs = a.plan + a.pl.offsets;
+    const int32_t* g1 = a.plan + a.pl.g1;
+    const int ns = a.k + (a.has_shared ? 1 : 0);  // <= 9
+    const int row_vec = a.H / 8;
+    for (int t = warp; t < a.T; t += nw) {
+        // lane i < ns: the position of slot i of token t, or -1 (GEMV segment)
+        int pos = -1;
+        if (lane < ns) {
+            const int slot = lane < a.k ? t * a.k + lane : a.T * a.k + t;
+            const int p = a.slot_pos[slot];
+            const int g = find_group(offs, G, p);
+            pos = g1[g + 1] != g1[g] ? p : -1;
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) +
+                                                          size_t(t) * a.H);
+        for (int c0 = lane; c0 < row_vec; c0 += 32 * 8) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c0 + 32 * u < row_vec) v[u] = ld_nc_u4(src + c0 + 32 * u);
+            for (int i = 0; i < ns; ++i) {
+                const int p = __shfl_sync(0xffffffffu, pos, i);
+                if (p < 0) continue;
+                uint4* dst = reinterpret_cast<uint4*>(a.xp_hi + size_t(p) * a.H);
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (c0 + 32 * u < row_vec) dst[c0 + 32 * u] = v[u];
+            }
+        }
+    }
+}
+
 // ============================================================ host launchers
 // Grid of a pair kernel: two CTAs per cluster that can be resident at once
 // (an odd SM left in a GPC cannot host a pair), at most `want`.
@@ -752,6 +792,7 @@ hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid,
 hf_status launch_gather(const GatherArgs& a, int x_f32, cudaStream_t st) {
     const int grid = num_sms(a.device) * 4;
     if (x_f32) k_gather_x<true><<<grid, 256, 0, st>>>(a);
+    else if (a.slot_pos && a.k > 1 && a.k <= kMaxTopK) k_gather_tokens<<<grid, 256, 0, st>>>(a);
     else k_gather_x<false><<<grid, 256, 0, st>>>(a);
     HF_CUDA(cudaGetLastError());
     return HF_OK;

@@ -374,6 +374,10 @@ struct GatherArgs {
     int T, k, H, device;
     uint16_t* xp_hi;
     uint16_t* xp_lo;
+    // optional (bf16 x, k > 1): slot -> position, so each token's row is read
+    // once and written to all of its positions (token-major gather)
+    const int32_t* slot_pos;
+    int has_shared;
 };
 hf_status launch_gemm(const GemmMaps& m, const GemmArgs& a, int num_b, int grid, cudaStream_t st);
 hf_status launch_gather(const GatherArgs& a, int x_f32, cudaStream_t st);

@@ -247,6 +247,9 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gx.device = c->cfg.device;
         gx.xp_hi = c->xp_hi;
         gx.xp_lo = c->xp_lo;
+        // single device: slot -> position of the routing (token-major gather)
+        gx.slot_pos = w.k > 1 && w.perm == c->perm_src ? c->slot_pos : nullptr;
+        gx.has_shared = c->Is > 0;
         PhaseTimer p1(c, st, 1);
         HF_TRY(launch_gather(gx, w.x_f32, st));
         p1.done(1);
