@@ -130,6 +130,10 @@ def phase_bytes(shape, counts, T, k, path, gemv_max):
     else:
         on_gemv = live & (c <= gemv_max)
     out = {"active": int((c[:E] > 0).sum())}
+    # expert outputs: one FP16 plane when no segment can take the GEMV (the
+    # library's rule; HF_Y_F16=0 keeps fp32), else fp32
+    no_gemv = path == "gemm" or (path == "auto" and gemv_max == 0)
+    y_e = 2 if no_gemv and os.environ.get("HF_Y_F16") != "0" else 4
     for name, sel in (("gemv", on_gemv), ("gemm", live & ~on_gemv)):
         w_gu = int((2 * inter[sel] * H * 2).sum())
         w_d = int((H * inter[sel] * 2).sum())
@@ -139,13 +143,13 @@ def phase_bytes(shape, counts, T, k, path, gemv_max):
         mid_e = 4 if name == "gemv" or os.environ.get("HF_DOWN_F16") == "0" else 2
         mid_b = int((c[sel] * inter[sel]).sum()) * mid_e
         out[f"{name}_gate_up"] = w_gu + slots * H * 2 + mid_b
-        out[f"{name}_down"] = w_d + mid_b + slots * H * 4
+        out[f"{name}_down"] = w_d + mid_b + slots * H * y_e
         out[f"{name}_gate_up_flops"] = int((2 * 2 * c[sel] * inter[sel] * H).sum())
         out[f"{name}_down_flops"] = int((2 * c[sel] * inter[sel] * H).sum())
     n_slots = int(c.sum())
     out["router"] = E * H * 2 + T * H * 2 + T * E * 4
     out["router_flops"] = 2 * T * E * H
-    out["combine"] = n_slots * H * 4 + T * H * 4 + T * k * 8
+    out["combine"] = n_slots * H * y_e + T * H * 4 + T * k * 8
     out["total_weights"] = E * H * 2 + int((3 * inter[live] * H * 2).sum())
     return out
 

@@ -204,6 +204,7 @@ struct ExpertWork {
     bool maybe_gemm;   // some segment may take the GEMM / the GEMV (else skip the launches)
     bool maybe_gemv;
     int down_f16 = 0;  // the layer's down blocks are FP16 (GemmArgs::down_f16)
+    int y16 = 0;       // outputs as the FP16 plane (GemmArgs::y16); GEMM-only passes
     int groups_base = 0;  // the plan's group g is the layer's group groups_base + g
     // GEMM2 outputs through per-position row pointers and the end-of-kernel
     // flag release (GemmArgs::yrow / sig_*); GEMM path only
@@ -228,9 +229,14 @@ struct RouterTiles {
 RouterTiles router_tiles(int T, int E, int H, int nsm);
 bool use_tc_router(const hf_moe_ctx* c, const LayerBuf& L, const void* x, hf_dtype xd, int T);
 hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st);
-// slot_pos: the row of y each slot reads (default: the context's slot -> position table)
-hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, const float* resid,
-                      float* slot_out, cudaStream_t st, const int32_t* slot_pos = nullptr);
+// slot_pos: the row of y each slot reads (default: the context's slot -> position table);
+// y16: y holds the FP16 plane (GemmArgs::y16)
+hf_status run_combine(hf_moe_ctx* c, const float* y, int y16, int T, float* out,
+                      const float* resid, float* slot_out, cudaStream_t st,
+                      const int32_t* slot_pos = nullptr);
+// Expert outputs of a forward whose every segment takes the GEMM go through
+// the FP16 plane (HF_Y_F16=0 keeps fp32); the same answer on every rank.
+bool y16_wanted(const hf_moe_ctx* c, bool maybe_gemv);
 
 // Allocates a layer's weight buffers and tensor maps on first use (hf_moe.cu).
 hf_status ctx_layer_alloc(hf_moe_ctx* c, int layer);

@@ -585,7 +585,7 @@ void ep_destroy(hf_moe_ctx* c) {
 // this rank's output slab, where the combine reads them. It needs nothing
 // from the other ranks, so it runs while the dispatch is in flight.
 static hf_status ep_shared_pass(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dtype xd, int T,
-                                cudaStream_t st) {
+                                bool y16, cudaStream_t st) {
     EpState& e = *c->ep;
     RouteArgs ra{};
     ra.T = T;
@@ -614,7 +614,11 @@ static hf_status ep_shared_pass(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dt
     ws.x_f32 = xd == HF_F32;
     ws.T = T;
     ws.k = 0;
-    ws.y = e.yslab_recv + size_t(c->world) * e.cap * c->H;
+    // rows W * cap.. of the output slab, in the slab's element type
+    const size_t yoff = size_t(c->world) * e.cap * c->H;
+    ws.y = y16 ? reinterpret_cast<float*>(reinterpret_cast<__half*>(e.yslab_recv) + yoff)
+               : e.yslab_recv + yoff;
+    ws.y16 = y16;
     ws.bn1 = ra.gemm_bn1;
     ws.bn2 = ra.gemm_bn2;
     ws.m1 = ra.gemm_m1;
@@ -626,12 +630,16 @@ static hf_status ep_shared_pass(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_dt
     return run_experts(c, L, ws, st);
 }
 
-static bool ep_shared_early() {
-    static const bool on = [] {
-        const char* v = std::getenv("HF_EP_SHARED_EARLY");  // tuning knob: 0 = one grouped pass
-        return !(v && std::atoi(v) == 0);
+// The shared expert beside the dispatch pays at two ranks (config 3: the
+// dispatch moves 403 MB a layer and the shared pass hides under it) and costs
+// at eight (its three smaller launches lose more than the overlap gains:
+// 18.3 -> 19.0 ms a step), so by default it runs early at W = 2 only.
+static bool ep_shared_early(int world) {
+    static const int knob = [] {
+        const char* v = std::getenv("HF_EP_SHARED_EARLY");  // tuning knob: 0 never, 1 always
+        return v ? std::atoi(v) : -1;
     }();
-    return on;
+    return knob < 0 ? world == 2 : knob != 0;
 }
 
 // Slab exchange (peer memory at any size, NCCL for small batches): fixed
@@ -667,8 +675,13 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     const bool maybe_gemv = !rl.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
                             (c->cfg.path == HF_PATH_AUTO && rl.gemv_max > 0);
     const bool fused = e.p2p && e.yrow && maybe_gemm && !maybe_gemv;
+    // expert outputs as the FP16 plane (every rank decides the same: the
+    // GEMV possibility depends on the configuration only at W > 1)
+    const bool y16 = y16_wanted(c, maybe_gemv);
+    const size_t esz = y16 ? 2 : 4;
+    const int yvec = int(size_t(H) * esz / 16);  // 16-byte vectors per output row
     // the shared expert runs as its own pass beside the dispatch (fused path)
-    const bool early = fused && has_shared && T > 0 && e.side && ep_shared_early();
+    const bool early = fused && has_shared && T > 0 && e.side && ep_shared_early(W);
     if (T > 0) {
         HF_TRY(run_route(c, L, ra, st));
     } else {
@@ -699,7 +712,7 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         px.done(1);
         if (early) {
             HF_CUDA(cudaEventRecord(e.ev_packed, e.side));
-            HF_TRY(ep_shared_pass(c, L, x, xd, T, st));
+            HF_TRY(ep_shared_pass(c, L, x, xd, T, y16, st));
             HF_CUDA(cudaStreamWaitEvent(st, e.ev_packed, 0));
         }
     } else {
@@ -735,7 +748,7 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     if (early) rl.has_shared = 0;
     {
         PhaseTimer pp(c, st, 1);
-        const EpRowOut ro{fused ? e.yrow : nullptr, e.d_peer_y, c->rank, H};
+        const EpRowOut ro{fused ? e.yrow : nullptr, e.d_peer_y, c->rank, H, int(esz)};
         HF_TRY(launch_ep_plan(rl, e.cnt_recv, W, El, cap, T, c->perm, e.row_pos, e.recv_tot,
                               e.p2p ? e.flags : nullptr, seq, c->timeout_ns, err, ro, st));
         pp.done(1);
@@ -750,6 +763,7 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     w.T = rows + T;
     w.k = 1;
     w.y = c->y;
+    w.y16 = y16;
     w.bn1 = rl.gemm_bn1;
     w.bn2 = rl.gemm_bn2;
     w.m1 = rl.gemm_m1;
@@ -774,18 +788,18 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         HF_CUDA(cudaGetLastError());
         py.done(1);
         if (T > 0)
-            HF_TRY(run_combine(c, e.yslab_recv, T, out, resid, r ? r->slot_out : nullptr, st,
+            HF_TRY(run_combine(c, e.yslab_recv, y16, T, out, resid, r ? r->slot_out : nullptr, st,
                                e.rowmap));
         return HF_OK;
     }
 
     // 4. outputs back to their sources in arrival order, then to canonical positions
-    const int row4 = H / 4;
     const int n_shared = has_shared ? T : 0;
+    const size_t yslab = size_t(cap) * H * esz;  // bytes of one source's output slab
     PhaseTimer py(c, st, 8);
     if (e.p2p) {
         k_ep_unpack_p2p<<<copy_grid(c->nsm, rows), 256, 0, st>>>(
-            reinterpret_cast<const float4*>(c->y), e.row_pos, e.recv_tot, W, cap, row4, c->rank,
+            reinterpret_cast<const float4*>(c->y), e.row_pos, e.recv_tot, W, cap, yvec, c->rank,
             e.peers, c->sched + 7, seq);
         HF_CUDA(cudaGetLastError());
         if (T == 0) {  // no outputs to collect, but every rank waits for every rank
@@ -794,15 +808,15 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         }
     } else {
         k_ep_unpack<<<copy_grid(c->nsm, rows), 256, 0, st>>>(
-            reinterpret_cast<const float4*>(c->y), e.row_pos, e.recv_tot, W, cap, row4,
+            reinterpret_cast<const float4*>(c->y), e.row_pos, e.recv_tot, W, cap, yvec,
             reinterpret_cast<float4*>(e.yslab_send));
         HF_CUDA(cudaGetLastError());
+        char* ys = reinterpret_cast<char*>(e.yslab_send);
+        char* yr = reinterpret_cast<char*>(e.yslab_recv);
         HF_NCCL(n.GroupStart());
         for (int d = 0; d < W; ++d) {
-            HF_NCCL(n.Send(e.yslab_send + size_t(d) * cap * H, size_t(cap) * H, ncclFloat32, d,
-                           e.comm, st));
-            HF_NCCL(n.Recv(e.yslab_recv + size_t(d) * cap * H, size_t(cap) * H, ncclFloat32, d,
-                           e.comm, st));
+            HF_NCCL(n.Send(ys + size_t(d) * yslab, yslab, ncclChar, d, e.comm, st));
+            HF_NCCL(n.Recv(yr + size_t(d) * yslab, yslab, ncclChar, d, e.comm, st));
         }
         HF_NCCL(n.GroupEnd());
     }
@@ -810,13 +824,13 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         k_ep_return<<<copy_grid(c->nsm, T * k + n_shared), 256, 0, st>>>(
             c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, T * k, k, El, cap,
             reinterpret_cast<const float4*>(e.yslab_recv), reinterpret_cast<const float4*>(c->y),
-            c->plan + c->pl.offsets + El, n_shared, row4, reinterpret_cast<float4*>(e.yrecv),
+            c->plan + c->pl.offsets + El, n_shared, yvec, reinterpret_cast<float4*>(e.yrecv),
             e.p2p ? e.flags + W : nullptr, W, seq, c->timeout_ns, err);
         HF_CUDA(cudaGetLastError());
     }
     py.done(T > 0 ? 2 : 1);
     // 5. combine in the reference order at the source
-    if (T > 0) HF_TRY(run_combine(c, e.yrecv, T, out, resid, r ? r->slot_out : nullptr, st));
+    if (T > 0) HF_TRY(run_combine(c, e.yrecv, y16, T, out, resid, r ? r->slot_out : nullptr, st));
     return HF_OK;
 }
 
@@ -918,12 +932,15 @@ static hf_status ep_forward_sized(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     w.maybe_gemm = rl.gemm_ok && (c->cfg.path == HF_PATH_GEMM || maxseg > rl.gemv_max);
     w.maybe_gemv = !rl.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
                    (c->cfg.path == HF_PATH_AUTO && rl.gemv_max > 0);
+    // the same on every rank: maybe_gemv depends on the configuration only
+    const bool y16 = y16_wanted(c, w.maybe_gemv);
+    w.y16 = y16;
     if (npos > 0) HF_TRY(run_experts(c, L, w, st));
 
     // 5. outputs back to their sources, at canonical slot positions
     PhaseTimer py(c, st, 8);
-    if (R > 0) HF_TRY(launch_gather_rows(e.ysend, c->y, size_t(H) * 4, R, e.row_pos, 1, st));
-    const size_t yrow = size_t(H) * 4;
+    const size_t yrow = size_t(H) * (y16 ? 2 : 4);  // bytes of one output row
+    if (R > 0) HF_TRY(launch_gather_rows(e.ysend, c->y, yrow, R, e.row_pos, 1, st));
     char* ys = reinterpret_cast<char*>(e.ysend);
     char* yr = reinterpret_cast<char*>(e.yrecv);
     HF_NCCL(n.GroupStart());
@@ -935,11 +952,12 @@ static hf_status ep_forward_sized(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     }
     HF_NCCL(n.GroupEnd());
     if (T > 0 && has_shared)
-        HF_CUDA(cudaMemcpyAsync(yr + size_t(T) * k * yrow, c->y + size_t(R) * H, size_t(T) * yrow,
-                                cudaMemcpyDeviceToDevice, st));
+        HF_CUDA(cudaMemcpyAsync(yr + size_t(T) * k * yrow,
+                                reinterpret_cast<const char*>(c->y) + size_t(R) * yrow,
+                                size_t(T) * yrow, cudaMemcpyDeviceToDevice, st));
     py.done(R > 0 ? 1 : 0);
     // 6. combine in the reference order at the source
-    if (T > 0) HF_TRY(run_combine(c, e.yrecv, T, out, resid, r ? r->slot_out : nullptr, st));
+    if (T > 0) HF_TRY(run_combine(c, e.yrecv, y16, T, out, resid, r ? r->slot_out : nullptr, st));
     return HF_OK;
 }
 

@@ -452,21 +452,32 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             auto process = [&](int c0, const uint32_t (&v0)[CW], const uint32_t (&v1)[CW]) {
                 if (NUM_A == 2 && a.which == 1) {  // gate/up pair -> SwiGLU -> mid planes
                     if (rv && a.down_f16) {
-                        // one FP16 plane: mid * 2^-kMidF16Shift (exact scaling, one rounding)
+                        // one FP16 plane: mid * 2^-kMidF16Shift (exact scaling, one
+                        // rounding); columns j and j + 1 share one packed conversion
+                        // (a conversion per value bounded the epilogue)
                         const size_t o0 = size_t(t.seg + t.n0 + c0) * a.Imax + t.m0 + rr;
                         __half* ph = reinterpret_cast<__half*>(a.mid_hi) + o0;
-                        bool over = false;
+                        constexpr float kDown = 1.0f / float(1 << kMidF16Shift);
+                        float mx = 0.0f;
 #pragma unroll
-                        for (int j = 0; j < CW; ++j) {
+                        for (int j = 0; j < CW; j += 2) {
                             if (c0 + j < t.n) {
-                                const float m = __fmul_rn(
-                                    swiglu_fast(__uint_as_float(v0[j]), __uint_as_float(v1[j])),
-                                    1.0f / float(1 << kMidF16Shift));
-                                over = over || !(fabsf(m) <= 65504.0f);
-                                ph[size_t(j) * a.Imax] = __float2half_rn(m);
+                                const bool two = c0 + j + 1 < t.n;
+                                const float m0 = __fmul_rn(
+                                    swiglu_fast(__uint_as_float(v0[j]), __uint_as_float(v1[j])), kDown);
+                                const float m1 =
+                                    two ? __fmul_rn(swiglu_fast(__uint_as_float(v0[j + 1]),
+                                                                __uint_as_float(v1[j + 1])),
+                                                    kDown)
+                                        : 0.0f;
+                                mx = fmaxf(mx, fmaxf(fabsf(m0), fabsf(m1)));
+                                const __half2 h = __floats2half2_rn(m0, m1);
+                                ph[size_t(j) * a.Imax] = __low2half(h);
+                                if (two) ph[size_t(j + 1) * a.Imax] = __high2half(h);
                             }
                         }
-                        if (over) atomicOr(a.err, 8);  // beyond the FP16 range: HF_ERR_RANGE
+                        // beyond the FP16 range (Inf included): HF_ERR_RANGE
+                        if (mx > 65504.0f) atomicOr(a.err, 8);
                     } else if (rv) {
                         // column c0 of this row in both planes; one row of mid per column
                         const size_t o0 = size_t(t.seg + t.n0 + c0) * a.Imax + t.m0 + rr;
@@ -490,14 +501,54 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                     const float sc = (a.which == 2 && a.down_f16)
                                          ? a.groups[t.g].down_scale * float(1 << kMidF16Shift)
                                          : 1.0f;
-#pragma unroll
-                    for (int j = 0; j < CW; ++j) {
-                        const int col = c0 + j;
-                        if (col < t.n) {
+                    if (a.y16) {
+                        // one FP16 plane: y * 2^-kYF16Shift (folded into the exact
+                        // power-of-two scale, so one rounding). Columns j and j + 1
+                        // convert together (one packed conversion for two values);
+                        // an output beyond the plane's range is HF_ERR_RANGE
+                        const float sc16 = sc * (1.0f / float(1 << kYF16Shift));
+                        float mx = 0.0f;
+                        auto row = [&](int col) {
                             const size_t pos = size_t(t.seg + t.n0 + col);
-                            float* yr = (a.yrow ? a.yrow[pos] : a.y + t.yoff + pos * a.H) + t.m0 + rr;
-                            if (rv) yr[0] = __fmul_rn(__uint_as_float(v0[j]), sc);
-                            if (NUM_A == 2 && rv1) yr[kRow1] = __fmul_rn(__uint_as_float(v1[j]), sc);
+                            return (a.yrow ? reinterpret_cast<__half*>(a.yrow[pos])
+                                           : reinterpret_cast<__half*>(a.y) + t.yoff + pos * a.H) +
+                                   t.m0 + rr;
+                        };
+#pragma unroll
+                        for (int j = 0; j < CW; j += 2) {
+                            const int col = c0 + j;
+                            if (col < t.n) {
+                                const bool two = col + 1 < t.n;
+                                __half* y0 = row(col);
+                                __half* y1 = two ? row(col + 1) : y0;
+#pragma unroll
+                                for (int b = 0; b < NUM_A; ++b) {
+                                    if (b == 0 ? !rv : !rv1) continue;
+                                    const uint32_t(&v)[CW] = b == 0 ? v0 : v1;
+                                    const float m0 = __fmul_rn(__uint_as_float(v[j]), sc16);
+                                    const float m1 =
+                                        two ? __fmul_rn(__uint_as_float(v[j + 1]), sc16) : 0.0f;
+                                    mx = fmaxf(mx, fmaxf(fabsf(m0), fabsf(m1)));
+                                    const __half2 h = __floats2half2_rn(m0, m1);
+                                    const int ro = b == 0 ? 0 : kRow1;
+                                    y0[ro] = __low2half(h);
+                                    if (two) y1[ro] = __high2half(h);
+                                }
+                            }
+                        }
+                        if (mx > 65504.0f) atomicOr(a.err, 8);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < CW; ++j) {
+                            const int col = c0 + j;
+                            if (col < t.n) {
+                                const size_t pos = size_t(t.seg + t.n0 + col);
+                                float* yr =
+                                    (a.yrow ? a.yrow[pos] : a.y + t.yoff + pos * a.H) + t.m0 + rr;
+                                if (rv) yr[0] = __fmul_rn(__uint_as_float(v0[j]), sc);
+                                if (NUM_A == 2 && rv1)
+                                    yr[kRow1] = __fmul_rn(__uint_as_float(v1[j]), sc);
+                            }
                         }
                     }
                 } else {  // residual block (dense MLP): y = resid + down row; the thread

@@ -387,16 +387,55 @@ int gemv_grid(int device, bool first, bool xf32, int H, int inter_max, int G, in
 // With a residual (the MLP block, glm_forward.cpp:795-796): output = residual +
 // (moeOut + sharedOut); each thread reads its residual elements before it
 // writes the same elements, so the residual may be the output buffer.
+// A thread owns V consecutive elements of one token: 4 of fp32 outputs, 8 of
+// the FP16 plane -- one 16-byte load a slot either way. The loads of all
+// slots are issued first, as raw 16-byte vectors; FP16 values are widened
+// (times 2^kYF16Shift, exact) only where the accumulation uses them.
+template <bool Y16>
+struct CombineVec {
+    static constexpr int V = Y16 ? 8 : 4;
+    uint4 q;
+    __device__ __forceinline__ void load(const float* y, size_t row, int H, int h) {
+        q = Y16 ? *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(y) + row * H + h)
+                : *reinterpret_cast<const uint4*>(y + row * H + h);
+    }
+    __device__ __forceinline__ void zero() { q = make_uint4(0u, 0u, 0u, 0u); }
+    __device__ __forceinline__ void get(float (&v)[V]) const {
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        if constexpr (Y16) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                v[2 * i] = __fmul_rn(f.x, float(1 << kYF16Shift));
+                v[2 * i + 1] = __fmul_rn(f.y, float(1 << kYF16Shift));
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(w[i]);
+        }
+    }
+};
+
+template <int V>
+__device__ __forceinline__ void store_f32(float* p, const float (&v)[V]) {
+#pragma unroll
+    for (int i = 0; i < V; i += 4)
+        *reinterpret_cast<float4*>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+}
+
+template <bool Y16>
 __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
     griddep_wait();  // expert outputs of the previous kernel
-    const int H4 = a.H >> 2;
+    using Vec = CombineVec<Y16>;
+    constexpr int V = Vec::V;
+    const int HV = a.H / V;
     const size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= size_t(a.T) * H4) return;
-    const int t = int(idx / H4), h = int(idx % H4) * 4;
+    if (idx >= size_t(a.T) * HV) return;
+    const int t = int(idx / HV), h = int(idx % HV) * V;
     // all loads first (independent), then the accumulation in rank order
     int pos[kMaxTopK];
     float wt[kMaxTopK];
-    float4 yv[kMaxTopK];
+    Vec yv[kMaxTopK];
 #pragma unroll
     for (int i = 0; i < kMaxTopK; ++i)
         if (i < a.k) {
@@ -405,44 +444,52 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
         }
 #pragma unroll
     for (int i = 0; i < kMaxTopK; ++i)
-        if (i < a.k) yv[i] = *reinterpret_cast<const float4*>(a.y + size_t(pos[i]) * a.H + h);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < a.k) yv[i].load(a.y, size_t(pos[i]), a.H, h);
+    Vec sv;
+    sv.zero();
+    const int sslot = a.T * a.k + t;
+    if (a.has_shared) sv.load(a.y, size_t(a.slot_pos[sslot]), a.H, h);
+    float acc[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc[e] = 0.f;
 #pragma unroll
     for (int i = 0; i < kMaxTopK; ++i) {
         if (i >= a.k) break;
         const float wi = wt[i];
-        const float4 y = yv[i];
-        acc.x = __fadd_rn(acc.x, __fmul_rn(wi, y.x));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(wi, y.y));
-        acc.z = __fadd_rn(acc.z, __fmul_rn(wi, y.z));
-        acc.w = __fadd_rn(acc.w, __fmul_rn(wi, y.w));
-        if (a.slot_out)
-            *reinterpret_cast<float4*>(a.slot_out + size_t(t * a.k + i) * a.H + h) = y;
+        float y[V];
+        yv[i].get(y);
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = __fadd_rn(acc[e], __fmul_rn(wi, y[e]));
+        if (a.slot_out) store_f32<V>(a.slot_out + size_t(t * a.k + i) * a.H + h, y);
     }
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (a.has_shared) {
-        const int slot = a.T * a.k + t;
-        s = *reinterpret_cast<const float4*>(a.y + size_t(a.slot_pos[slot]) * a.H + h);
-        if (a.slot_out) *reinterpret_cast<float4*>(a.slot_out + size_t(slot) * a.H + h) = s;
+    {
+        float s[V];
+        sv.get(s);
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = __fadd_rn(acc[e], s[e]);
+        if (a.has_shared && a.slot_out) store_f32<V>(a.slot_out + size_t(sslot) * a.H + h, s);
     }
-    acc.x = __fadd_rn(acc.x, s.x);
-    acc.y = __fadd_rn(acc.y, s.y);
-    acc.z = __fadd_rn(acc.z, s.z);
-    acc.w = __fadd_rn(acc.w, s.w);
     if (a.resid) {
-        const float4 rs = *reinterpret_cast<const float4*>(a.resid + size_t(t) * a.H + h);
-        acc.x = __fadd_rn(rs.x, acc.x);
-        acc.y = __fadd_rn(rs.y, acc.y);
-        acc.z = __fadd_rn(rs.z, acc.z);
-        acc.w = __fadd_rn(rs.w, acc.w);
+#pragma unroll
+        for (int e = 0; e < V; e += 4) {
+            const float4 rs = *reinterpret_cast<const float4*>(a.resid + size_t(t) * a.H + h + e);
+            acc[e] = __fadd_rn(rs.x, acc[e]);
+            acc[e + 1] = __fadd_rn(rs.y, acc[e + 1]);
+            acc[e + 2] = __fadd_rn(rs.z, acc[e + 2]);
+            acc[e + 3] = __fadd_rn(rs.w, acc[e + 3]);
+        }
     }
-    *reinterpret_cast<float4*>(a.out + size_t(t) * a.H + h) = acc;
+    store_f32<V>(a.out + size_t(t) * a.H + h, acc);
 }
 
 hf_status launch_combine(const CombineArgs& a, cudaStream_t st) {
-    const size_t n = size_t(a.T) * (a.H >> 2);
+    if (a.y16 && a.H % 8) return fail(HF_ERR_ARG, "combine: FP16 outputs need H % 8 == 0");
+    const size_t n = size_t(a.T) * (a.H / (a.y16 ? 8 : 4));
     if (n == 0) return HF_OK;
-    HF_CUDA(launch_pdl(k_combine, dim3(unsigned((n + 255) / 256)), dim3(256), 0, st, a));
+    if (a.y16)
+        HF_CUDA(launch_pdl(k_combine<true>, dim3(unsigned((n + 255) / 256)), dim3(256), 0, st, a));
+    else
+        HF_CUDA(launch_pdl(k_combine<false>, dim3(unsigned((n + 255) / 256)), dim3(256), 0, st, a));
     return HF_OK;
 }
 

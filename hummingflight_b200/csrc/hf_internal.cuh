@@ -268,6 +268,7 @@ struct EpRowOut {
     float** yrow;            // [positions] device
     float* const* peer_y;    // [W] device
     int rank, H;
+    int esz;                 // bytes per output element: 4 (fp32) or 2 (FP16 plane)
 };
 hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, int W, int El, int cap, int T_loc,
                          int32_t* perm, int32_t* row_pos, int32_t* recv_tot,
@@ -355,11 +356,18 @@ struct GemmArgs {
     // accumulator by 2^kMidF16Shift * groups[g].down_scale
     int down_f16;
     const GroupW* groups;
+    // GEMM2 (no resid, nsplit == 1): outputs as one FP16 plane holding
+    // y * 2^-kYF16Shift (y and yrow[] then address __half elements)
+    int y16;
 };
 // mid is stored as FP16 times 2^-6: finite up to 65504 * 64 ~ 4.2e6, full
 // 11-bit precision from 2^-8 up; smaller values keep an absolute error
 // below 2^-19
 constexpr int kMidF16Shift = 6;
+// Expert outputs of an all-GEMM forward are stored as FP16 times 2^-4:
+// finite up to 65504 * 16 ~ 1.05e6 (beyond: HF_ERR_RANGE), full 11-bit
+// precision from 2^-10 up; smaller values keep an absolute error below 2^-21
+constexpr int kYF16Shift = 4;
 struct GemmMaps {
     CUtensorMap A, A_sh;       // weights: routed view; shared expert gate (GEMM1) or down rows
     CUtensorMap A_sh2;         // shared expert up rows (GEMM1)
@@ -391,7 +399,8 @@ uint64_t synth_key(uint64_t seed, uint32_t layer, uint32_t kind, uint32_t expert
 float synth_normal_scale(double sigma);
 
 struct CombineArgs {
-    const float* y;        // [(T*k+T) x H]
+    const float* y;        // [(T*k+T) x H]; FP16 elements (y * 2^-kYF16Shift) when y16
+    int y16;
     const int32_t* slot_pos;
     const float* w;        // [T x k]
     int T, H, k, has_shared;

@@ -325,6 +325,7 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.sig_n = w.sig_n;
         gm.sig_slot = w.sig_slot;
         gm.sig_seq = w.sig_seq;
+        gm.y16 = w.y16;
         GemmMaps m2 = c->maps2;
         m2.A = L.dn;
         m2.A_sh = L.sh_down;
@@ -336,11 +337,21 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
     return HF_OK;
 }
 
-hf_status run_combine(hf_moe_ctx* c, const float* y, int T, float* out, const float* resid,
-                      float* slot_out, cudaStream_t st, const int32_t* slot_pos) {
+bool y16_wanted(const hf_moe_ctx* c, bool maybe_gemv) {
+    static const bool on = [] {
+        const char* e = std::getenv("HF_Y_F16");  // tuning knob: 0 keeps fp32 expert outputs
+        return !(e && std::atoi(e) == 0);
+    }();
+    return on && c->gemm_ok && !maybe_gemv && c->H % 8 == 0;
+}
+
+hf_status run_combine(hf_moe_ctx* c, const float* y, int y16, int T, float* out,
+                      const float* resid, float* slot_out, cudaStream_t st,
+                      const int32_t* slot_pos) {
     CombineArgs ca{};
     ca.resid = resid;
     ca.y = y;
+    ca.y16 = y16;
     ca.slot_pos = slot_pos ? slot_pos : c->slot_pos;
     ca.w = c->w;
     ca.T = T;
@@ -826,8 +837,9 @@ static hf_status run_forward(hf_moe_ctx* c, int layer, const void* x, hf_dtype x
         w.maybe_gemm = ra.gemm_ok && (c->cfg.path == HF_PATH_GEMM || T > ra.gemv_max);
         w.maybe_gemv = !ra.gemm_ok || c->cfg.path == HF_PATH_GEMV ||
                        (c->cfg.path == HF_PATH_AUTO && ra.gemv_max > 0);
+        w.y16 = y16_wanted(c, w.maybe_gemv);
         HF_TRY(run_experts(c, L, w, st));
-        HF_TRY(run_combine(c, c->y, T, out, resid, r ? r->slot_out : nullptr, st));
+        HF_TRY(run_combine(c, c->y, w.y16, T, out, resid, r ? r->slot_out : nullptr, st));
     }
     return copy_routing(c, L, r, T, st);
 }

@@ -568,8 +568,9 @@ hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cud
 // arrival -- the order the host plan of the large-batch exchange uses -- and
 // the shared expert's T_loc local tokens come last (rows W * cap + t). Also
 // writes row_pos (slab row -> local position) and recv_tot[s] (rows from s).
-// With yrow set it also writes each position's output row: received row i
-// from source s goes back to row rank * cap + i of s's output slab
+// With yrow set it also writes each position's output row (rows of ro.esz * H
+// bytes): received row i from source s goes back to row rank * cap + i of s's
+// output slab
 // (peer_y[s], mapped here), a local token t to row W * cap + t of this rank's
 // own slab (peer_y[rank]).
 __global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cnt, int W, int El,
@@ -617,17 +618,24 @@ __global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cn
         const int pos0 = s_off[sj % El] + s_pos[sj];
         const int row0 = (sj / El) * cap + s_src[sj];
         const int s = sj / El;
-        float* yb = ro.yrow ? ro.peer_y[s] + (size_t(ro.rank) * cap + s_src[sj]) * ro.H : nullptr;
+        // output rows are ro.esz * H bytes (fp32 or the FP16 plane)
+        const size_t rowb = size_t(ro.esz) * ro.H;
+        char* yb = ro.yrow ? reinterpret_cast<char*>(ro.peer_y[s]) +
+                                 (size_t(ro.rank) * cap + s_src[sj]) * rowb
+                           : nullptr;
         for (int i = 0; i < n; ++i) {
             perm[pos0 + i] = row0 + i;  // slot id = row of [slabs | local tokens] (k = 1)
             row_pos[row0 + i] = pos0 + i;
-            if (yb) ro.yrow[pos0 + i] = yb + size_t(i) * ro.H;
+            if (yb) ro.yrow[pos0 + i] = reinterpret_cast<float*>(yb + size_t(i) * rowb);
         }
     }
     if (a.has_shared)  // slot ids past all rows name the local tokens (token_of_slot)
         for (int t = threadIdx.x; t < T_loc; t += blockDim.x) {
             perm[s_off[El] + t] = (rows + T_loc) + (rows + t);
-            if (ro.yrow) ro.yrow[s_off[El] + t] = ro.peer_y[ro.rank] + size_t(rows + t) * ro.H;
+            if (ro.yrow)
+                ro.yrow[s_off[El] + t] = reinterpret_cast<float*>(
+                    reinterpret_cast<char*>(ro.peer_y[ro.rank]) +
+                    size_t(rows + t) * ro.esz * ro.H);
         }
 }
 

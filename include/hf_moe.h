@@ -49,8 +49,10 @@ typedef enum hf_status {
     HF_ERR_OOM = 5,         /* device allocation failed                         */
     HF_ERR_STATE = 6,       /* call out of order (e.g. weights not set)         */
     HF_ERR_UNSUPPORTED = 7, /* no device / wrong architecture                   */
-    HF_ERR_RANGE = 8        /* a SwiGLU intermediate beyond the FP16 down pass's
-                               range (|silu(g) * u| > 4.2e6): outputs invalid    */
+    HF_ERR_RANGE = 8        /* a value beyond an FP16 plane of the tensor-core
+                               path: a SwiGLU intermediate |silu(g) * u| > 4.2e6
+                               or an expert output |y| > 1.05e6 (Inf included;
+                               NaN propagates as in fp32): outputs invalid      */
 } hf_status;
 
 typedef enum hf_mem_kind { HF_MEM_HOST = 0, HF_MEM_DEVICE = 1 } hf_mem_kind;
