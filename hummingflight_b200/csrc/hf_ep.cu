@@ -232,7 +232,7 @@ constexpr int kEpMaxRanks = 16;
 struct PeerPtrs {                              // rank d's buffers, as mapped here
     char* x[kEpMaxRanks];                      // xslab_recv
     float* y[kEpMaxRanks];                     // yslab_recv
-    int32_t* cnt[kEpMaxRanks];                 // cnt_recv
+    int32_t* cnt[kEpMaxRanks];                 // cnt_recv (counts, then the slot -> row maps)
     unsigned long long* flags[kEpMaxRanks];    // [2W]: rows from s arrived / outputs from s
 };
 
@@ -255,10 +255,16 @@ __device__ __forceinline__ void ep_last_block(int* done, F tail) {
 
 // Rows into the destinations' slabs (at this rank's slab) in peer memory;
 // then counts, then flags[d][rank] = seq on every rank.
+// A token routed to several experts of one destination rank crosses NVLink
+// once: only its slot with the smallest expert id there stores the row (at
+// that slot's arrival row); every slot writes the row it reads into the
+// destination's slot -> row map (after the counts: cnt[d][W * El + rank *
+// cap + r]). Top-8 over 32-expert ranks sends ~5.3 rows a token at W = 8.
 // With rowmap set, also records where each slot's output will be read back:
 // routed slot -> row d * cap + r of this rank's output slab, the shared slot
 // of local token t (slot n + t) -> row W * cap + t.
 __global__ void __launch_bounds__(256) k_ep_pack_p2p(const int32_t* perm, const int32_t* ids,
+                                                     const int32_t* slot_pos,
                                                      const int32_t* offsets, const uint4* x,
                                                      int row_vec, int n, int k, int El, int cap,
                                                      int rank, int W, const int32_t* cnt_src,
@@ -270,20 +276,36 @@ __global__ void __launch_bounds__(256) k_ep_pack_p2p(const int32_t* perm, const 
     for (int p = warp; p < n; p += nw) {
         const int slot = perm[p];
         const int d = ids[slot] / El;
-        const int r = p - offsets[d * El];
-        const uint4* src = x + size_t(slot / k) * row_vec;
-        uint4* dst = reinterpret_cast<uint4*>(pp.x[d]) + (size_t(rank) * cap + r) * row_vec;
-        // eight 16-byte loads in flight per lane before their stores cross NVLink
-        for (int c0 = lane; c0 < row_vec; c0 += 32 * 8) {
-            uint4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (c0 + 32 * u < row_vec) v[u] = ld_nc_u4(src + c0 + 32 * u);
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (c0 + 32 * u < row_vec) dst[c0 + 32 * u] = v[u];
+        const int off = offsets[d * El];
+        const int r = p - off;
+        const int t = slot / k;
+        // the token's first slot on rank d: smallest expert id there (ids of
+        // one token are distinct), lane = top-k rank
+        unsigned key = 0xffffffffu;
+        if (lane < k) {
+            const int e = ids[t * k + lane];
+            if (e / El == d) key = (unsigned(e) << 5) | unsigned(lane);
         }
-        if (rowmap && lane == 0) rowmap[slot] = d * cap + r;
+        key = __reduce_min_sync(0xffffffffu, key);
+        const int first = t * k + int(key & 31u);
+        if (first == slot) {
+            const uint4* src = x + size_t(t) * row_vec;
+            uint4* dst = reinterpret_cast<uint4*>(pp.x[d]) + (size_t(rank) * cap + r) * row_vec;
+            // eight 16-byte loads in flight per lane before their stores cross NVLink
+            for (int c0 = lane; c0 < row_vec; c0 += 32 * 8) {
+                uint4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (c0 + 32 * u < row_vec) v[u] = ld_nc_u4(src + c0 + 32 * u);
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (c0 + 32 * u < row_vec) dst[c0 + 32 * u] = v[u];
+            }
+        }
+        if (lane == 0) {
+            pp.cnt[d][W * El + rank * cap + r] = first == slot ? r : slot_pos[first] - off;
+            if (rowmap) rowmap[slot] = d * cap + r;
+        }
     }
     if (rowmap)
         for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_shared; t += gridDim.x * blockDim.x)
@@ -354,7 +376,7 @@ struct EpState {
     void* xall = nullptr;      // [(R_cap + T_max) x H] received rows, then local tokens
     float* ysend = nullptr;    // [R_cap x H] expert outputs in arrival order
     float* yrecv = nullptr;    // [(T_max*k + T_max) x H] outputs at canonical positions
-    int32_t* cnt_recv = nullptr;   // [W x El]
+    int32_t* cnt_recv = nullptr;   // [W x El] counts, then [W x cap] slot -> row maps
     int32_t* loc_counts = nullptr; // [El + 1]
     int32_t* row_pos = nullptr;    // [R_cap]
     int32_t* h_src = nullptr;      // pinned [E + 1]
@@ -492,7 +514,8 @@ hf_status ep_create(hf_moe_ctx* c, const unsigned char* unique_id) {
     e->R_cap = ep_recv_cap(c);
     const int W = c->world, El = c->E_local;
     HF_TRY(dalloc(&e->yrecv, (T * c->k + T) * c->H));
-    HF_TRY(dalloc(&e->cnt_recv, size_t(W) * El));
+    // counts [W x El], then (peer memory) the slot -> row maps [W x cap]
+    HF_TRY(dalloc(&e->cnt_recv, size_t(W) * El + size_t(W) * T * std::min(c->k, El)));
     HF_TRY(dalloc(&e->row_pos, e->R_cap));
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof(id));
@@ -705,7 +728,8 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         const int pack_grid = early ? std::min(c->nsm, copy_grid(c->nsm, std::max(1, T * k)))
                                     : copy_grid(c->nsm, std::max(1, T * k));
         k_ep_pack_p2p<<<pack_grid, 256, 0, sp>>>(
-            c->perm_src, c->ids, c->plan_src + c->pl_src.offsets, static_cast<const uint4*>(x),
+            c->perm_src, c->ids, c->slot_pos, c->plan_src + c->pl_src.offsets,
+            static_cast<const uint4*>(x),
             int(rowb / 16), T * k, k, El, cap, c->rank, W, cnt_src, e.peers, c->sched + 6, seq,
             fused ? e.rowmap : nullptr, has_shared ? T : 0);
         HF_CUDA(cudaGetLastError());
@@ -749,7 +773,8 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
     {
         PhaseTimer pp(c, st, 1);
         const EpRowOut ro{fused ? e.yrow : nullptr, e.d_peer_y, c->rank, H, int(esz)};
-        HF_TRY(launch_ep_plan(rl, e.cnt_recv, W, El, cap, T, c->perm, e.row_pos, e.recv_tot,
+        HF_TRY(launch_ep_plan(rl, e.cnt_recv, e.p2p ? e.cnt_recv + W * El : nullptr, W, El, cap,
+                              T, c->perm, e.row_pos, e.recv_tot,
                               e.p2p ? e.flags : nullptr, seq, c->timeout_ns, err, ro, st));
         pp.done(1);
     }

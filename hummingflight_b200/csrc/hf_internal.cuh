@@ -270,7 +270,11 @@ struct EpRowOut {
     int rank, H;
     int esz;                 // bytes per output element: 4 (fp32) or 2 (FP16 plane)
 };
-hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, int W, int El, int cap, int T_loc,
+// rmap (optional, [W x cap]): the slab row each received slot reads --
+// sources send a token's row once per destination rank, however many of
+// its experts live there (nullptr: row = arrival index).
+hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, const int32_t* rmap, int W,
+                         int El, int cap, int T_loc,
                          int32_t* perm, int32_t* row_pos, int32_t* recv_tot,
                          const unsigned long long* flags, unsigned long long seq,
                          unsigned long long timeout_ns, int* err, const EpRowOut& ro,

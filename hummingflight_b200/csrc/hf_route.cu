@@ -573,7 +573,8 @@ hf_status launch_plan_from_counts(const RouteArgs& a, const int32_t* counts, cud
 // output slab
 // (peer_y[s], mapped here), a local token t to row W * cap + t of this rank's
 // own slab (peer_y[rank]).
-__global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cnt, int W, int El,
+__global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cnt,
+                                                  const int32_t* rmap, int W, int El,
                                                   int cap, int T_loc, int32_t* perm,
                                                   int32_t* row_pos, int32_t* recv_tot,
                                                   const unsigned long long* flags,
@@ -623,8 +624,11 @@ __global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cn
         char* yb = ro.yrow ? reinterpret_cast<char*>(ro.peer_y[s]) +
                                  (size_t(ro.rank) * cap + s_src[sj]) * rowb
                            : nullptr;
+        const int32_t* rm = rmap ? rmap + row0 : nullptr;
         for (int i = 0; i < n; ++i) {
-            perm[pos0 + i] = row0 + i;  // slot id = row of [slabs | local tokens] (k = 1)
+            // slot id = row of [slabs | local tokens] (k = 1): the arrival row,
+            // or the row the source stored the token's activations in
+            perm[pos0 + i] = rm ? (sj / El) * cap + rm[i] : row0 + i;
             row_pos[row0 + i] = pos0 + i;
             if (yb) ro.yrow[pos0 + i] = reinterpret_cast<float*>(yb + size_t(i) * rowb);
         }
@@ -639,8 +643,9 @@ __global__ void __launch_bounds__(1024) k_ep_plan(RouteArgs a, const int32_t* cn
         }
 }
 
-hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, int W, int El, int cap, int T_loc,
-                         int32_t* perm, int32_t* row_pos, int32_t* recv_tot,
+hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, const int32_t* rmap, int W,
+                         int El, int cap, int T_loc, int32_t* perm, int32_t* row_pos,
+                         int32_t* recv_tot,
                          const unsigned long long* flags, unsigned long long seq,
                          unsigned long long timeout_ns, int* err, const EpRowOut& ro,
                          cudaStream_t st) {
@@ -648,8 +653,8 @@ hf_status launch_ep_plan(const RouteArgs& a, const int32_t* cnt, int W, int El, 
     if (G != El + 1 || G > 2 * 1024) return fail(HF_ERR_ARG, "expert-parallel plan: bad group count");
     const size_t smem = sizeof(int) * (G + G + 1 + kPlanScratch + 2 * W * El);
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_ep_plan), int(smem)));
-    k_ep_plan<<<1, 1024, smem, st>>>(a, cnt, W, El, cap, T_loc, perm, row_pos, recv_tot, flags, seq,
-                                     timeout_ns, err, ro);
+    k_ep_plan<<<1, 1024, smem, st>>>(a, cnt, rmap, W, El, cap, T_loc, perm, row_pos, recv_tot,
+                                     flags, seq, timeout_ns, err, ro);
     HF_CUDA(cudaGetLastError());
     return HF_OK;
 }
