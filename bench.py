@@ -36,6 +36,7 @@ import statistics
 import subprocess
 import sys
 import threading
+import time
 
 import numpy as np
 
@@ -87,6 +88,16 @@ class ClockSampler:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) == 3:
                 self.rows.append(parts)
+
+    def ready(self, timeout_s: float = 10.0):
+        """Wait (bounded) until nvidia-smi delivers samples, then drop them:
+        it takes longer to start than a short timed region lasts."""
+        if self.p is None:
+            return
+        t0 = time.time()
+        while not self.rows and time.time() - t0 < timeout_s and self.p.poll() is None:
+            time.sleep(0.02)
+        self.rows.clear()
 
     def stop(self):
         if self.p is None:
@@ -509,6 +520,9 @@ def measure(job, args, world, dist, stream, local, steps):
     torch.cuda.synchronize()
     L.profile_read()  # drop warm-up launch counts
     clk = ClockSampler(local)
+    clk.ready()
+    if world > 1:
+        dist.barrier()
     ms = timed(job, steps, world, dist, stream)
     launches = int(sum(v[1] for v in L.profile_read().values()))
     L.profile(True)
