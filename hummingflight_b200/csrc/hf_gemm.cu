@@ -19,9 +19,10 @@
 //          bits instead of BF16's 8.
 //   GEMM2  acc = Wd mid^T: one FP16 x FP16 pass (the accumulator scaled back
 //          by the powers of two), or Wd mid_hi^T + Wd mid_lo^T with BF16;
-//          epilogue stores fp32 expert outputs y[position][h] for the
-//          deterministic combine (or, for an expert-parallel receiver, into
-//          the row of its source's output slab).
+//          epilogue stores the expert outputs y[position][h] -- one FP16
+//          plane holding y * 2^-4 on a forward with no GEMV segment, else
+//          fp32 -- for the deterministic combine (or, for an expert-parallel
+//          receiver, into the row of its source's output slab).
 //
 // CTA = 10 warps, one CTA (or one CTA of a pair) per SM, persistent over the
 // tile list: warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
