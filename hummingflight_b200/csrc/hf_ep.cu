@@ -12,17 +12,20 @@
 //  1. route the rank's own tokens over ALL experts; the canonical
 //     permutation orders slots by expert, so the slots bound for rank d are
 //     one contiguous range;
-//  2. the pack kernel stores each routed activation row straight into its
-//     destination's receive slab, then the per-expert counts, then this
-//     forward's sequence number into every rank's arrival flag
+//  2. the pack kernel stores each token's activation row straight into its
+//     destination's receive slab, once per destination rank however many of
+//     its experts live there (with a slot -> row map beside the counts),
+//     walking the destinations interleaved; then the per-expert counts, then
+//     this forward's sequence number into every rank's arrival flag
 //     (fence.sc.sys + st.release.sys);
 //  3. the receiver's plan kernel waits (bounded) for every source's flag and
-//     builds the plan from the counts on the device;
+//     builds the plan from the counts and row maps on the device;
 //  4. the same GEMV / tcgen05 GEMM kernels run on the local experts (received
 //     rows, expert-major then source) and on the shared expert (local
 //     tokens). On the GEMM path the down GEMM's epilogue stores every output
-//     row straight into its source's output slab, and its last CTA raises
-//     the return flags, so the return overlaps the GEMM tile by tile;
+//     row (the FP16 plane, half the bytes of fp32) straight into its source's
+//     output slab, and its last CTA raises the return flags, so the return
+//     overlaps the GEMM tile by tile;
 //  5. the source waits (bounded) for every rank's return flag and combines in
 //     the reference's top-k rank order, reading the rows from its slab.
 // Each slot's expert product and the combine order do not depend on W, so
