@@ -351,96 +351,6 @@ __global__ void __launch_bounds__(256) k_ep_pack_p2p(const int32_t* perm, const 
     });
 }
 
-// The same dispatch with the row copies on the bulk-copy (TMA) engine: each
-// warp's lane 0 loads a row into one of its two shared-memory buffers
-// (completion on the warp's mbarrier) and stores it to the destination's
-// slab with one bulk store, the next row's load overlapping that store. One
-// block per SM (the buffers take most of shared memory). Waits are bounded;
-// a load that does not land in time sets the timeout bit of the error word.
-constexpr int kPackBulkWarps = 8;
-__global__ void __launch_bounds__(kPackBulkWarps * 32) k_ep_pack_bulk(
-    const int32_t* perm, const int32_t* ids, const int32_t* slot_pos, const int32_t* offsets,
-    const char* x, int rowb, int n, int k, int El, int cap, int rank, int W,
-    const int32_t* cnt_src, PeerPtrs pp, int* done, unsigned long long seq, int32_t* rowmap,
-    int n_shared, unsigned long long timeout_ns, int* err) {
-    extern __shared__ __align__(128) unsigned char pack_buf[];
-    __shared__ __align__(8) uint64_t bar[kPackBulkWarps];
-    const int wi = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int warp = blockIdx.x * (blockDim.x >> 5) + wi;
-    const int nw = gridDim.x * (blockDim.x >> 5);
-    unsigned char* buf = pack_buf + size_t(wi) * 2 * rowb;
-    if (lane == 0) {
-        sm100::mbar_init(&bar[wi], 1);
-        sm100::fence_mbar_init();
-    }
-    __syncwarp();
-    auto landed = [&](uint32_t parity) {
-        const uint64_t dl = sm100::globaltimer() + timeout_ns;
-        uint32_t spins = 0;
-        while (!sm100::mbar_try_wait(&bar[wi], parity))
-            if ((++spins & 255u) == 0 && sm100::globaltimer() > dl) return false;
-        return true;
-    };
-    uint32_t phase = 0;
-    int nb = 0;
-    bool ok = true;
-    const DispatchOrder order(offsets, W, El, rank);
-    for (int i = warp; i < order.tasks(); i += nw) {
-        const int p = order.position(i);  // the same for every lane
-        if (p < 0) continue;
-        const int slot = perm[p];
-        const int d = ids[slot] / El;
-        const int off = offsets[d * El];
-        const int r = p - off;
-        const int t = slot / k;
-        const int first = first_slot_on(ids, t, k, El, d, lane);
-        if (lane == 0) {
-            if (first == slot && ok) {
-                unsigned char* b = buf + size_t(nb) * rowb;
-                sm100::bulk_wait_read<1>();  // the store two rows back has read this buffer
-                sm100::mbar_arrive_expect_tx(&bar[wi], uint32_t(rowb));
-                sm100::bulk_load(b, x + size_t(t) * rowb, uint32_t(rowb), &bar[wi]);
-                if (!landed(phase)) {
-                    atomicOr(err, 2);
-                    ok = false;
-                    landed(phase);  // the load in flight still writes the buffer
-                }
-                phase ^= 1u;
-                if (ok) {
-                    sm100::bulk_store(pp.x[d] + (size_t(rank) * cap + r) * rowb, b, uint32_t(rowb));
-                    sm100::bulk_commit();
-                }
-                nb ^= 1;
-            }
-            pp.cnt[d][W * El + rank * cap + r] = first == slot ? r : slot_pos[first] - off;
-            if (rowmap) rowmap[slot] = d * cap + r;
-        }
-        __syncwarp();
-    }
-    if (lane == 0) {
-        sm100::bulk_wait<0>();  // every store of this warp performed
-        sm100::fence_proxy_async();
-    }
-    if (rowmap)
-        for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n_shared; t += gridDim.x * blockDim.x)
-            rowmap[n + t] = W * cap + t;
-    ep_last_block(done, [&] {
-        for (int i = threadIdx.x; i < W * El; i += blockDim.x)
-            pp.cnt[i / El][rank * El + i % El] = cnt_src[i];
-        __threadfence_system();
-        __syncthreads();
-        if (threadIdx.x < W) sm100::st_release_sys(pp.flags[threadIdx.x] + rank, seq);
-    });
-}
-
-static bool ep_pack_bulk() {
-    static const bool on = [] {
-        const char* v = std::getenv("HF_EP_PACK_BULK");  // tuning knob: 1 = bulk-copy dispatch
-        return v && std::atoi(v) == 1;
-    }();
-    return on;
-}
-
 // Receiver: outputs back into each source's slab (at this rank's slab) in
 // peer memory; then flags[s][W + rank] = seq.
 __global__ void __launch_bounds__(256) k_ep_unpack_p2p(const float4* y, const int32_t* row_pos,
@@ -849,23 +759,10 @@ static hf_status ep_forward_slabs(hf_moe_ctx* c, LayerBuf& L, const void* x, hf_
         // it drained and the two would run one after the other)
         const int pack_grid = early ? std::min(c->nsm, copy_grid(c->nsm, std::max(1, T * k)))
                                     : copy_grid(c->nsm, std::max(1, T * k));
-        const size_t bulk_smem = size_t(2) * kPackBulkWarps * rowb;
-        if (!early && ep_pack_bulk() && rowb % 16 == 0 && bulk_smem <= size_t(200) << 10) {
-            HF_CUDA(ensure_smem(reinterpret_cast<const void*>(k_ep_pack_bulk), int(bulk_smem)));
-            const int grid =
-                std::max(1, std::min(c->nsm, (T * k + kPackBulkWarps - 1) / kPackBulkWarps));
-            k_ep_pack_bulk<<<grid, kPackBulkWarps * 32, bulk_smem, sp>>>(
-                c->perm_src, c->ids, c->slot_pos, c->plan_src + c->pl_src.offsets,
-                static_cast<const char*>(x), int(rowb), T * k, k, El, cap, c->rank, W, cnt_src,
-                e.peers, c->sched + 6, seq, fused ? e.rowmap : nullptr, has_shared ? T : 0,
-                c->timeout_ns, err);
-        } else {
-            k_ep_pack_p2p<<<pack_grid, 256, 0, sp>>>(
-                c->perm_src, c->ids, c->slot_pos, c->plan_src + c->pl_src.offsets,
-                static_cast<const uint4*>(x), int(rowb / 16), T * k, k, El, cap, c->rank, W,
-                cnt_src, e.peers, c->sched + 6, seq, fused ? e.rowmap : nullptr,
-                has_shared ? T : 0);
-        }
+        k_ep_pack_p2p<<<pack_grid, 256, 0, sp>>>(
+            c->perm_src, c->ids, c->slot_pos, c->plan_src + c->pl_src.offsets,
+            static_cast<const uint4*>(x), int(rowb / 16), T * k, k, El, cap, c->rank, W, cnt_src,
+            e.peers, c->sched + 6, seq, fused ? e.rowmap : nullptr, has_shared ? T : 0);
         HF_CUDA(cudaGetLastError());
         px.done(1);
         if (early) {

@@ -89,39 +89,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
         : "memory");
 }
 
-// ------------------------------------------------------------------ bulk copies (untiled)
-// Both addresses 16-byte aligned, size a multiple of 16 bytes. A load
-// completes on `bar` in bytes; stores are tracked by bulk groups.
-__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-        ::"r"(smem_u32(dst_smem)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
-        "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void bulk_store(void* dst, const void* src_smem, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
-                 ::"l"(reinterpret_cast<uint64_t>(dst)), "r"(smem_u32(src_smem)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_commit() {
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-// At most N of this thread's committed store groups still read shared memory.
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-// At most N of this thread's committed store groups are incomplete.
-template <int N>
-__device__ __forceinline__ void bulk_wait() {
-    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async;" ::: "memory");
-}
-
 // ------------------------------------------------------------------ tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
