@@ -100,7 +100,11 @@ def main():
     ep.close()
     dist.barrier()
     dist.destroy_process_group()
-    print("EPRECOVERY", rank, json.dumps(res), flush=True)
+    # one write() per line: the two ranks share the parent's pipe, and a line
+    # under the pipe buffer size is written whole
+    sys.stdout.flush()
+    sys.stdout.write(f"EPRECOVERY {rank} {json.dumps(res)}\n")
+    sys.stdout.flush()
     ok = (res["agreement"]["same"] and res["agreement"]["maxdiff"] <= 1e-5 and
           res["transport"] == "peer" and res["skip"]["recovered"] and
           res["skip"]["first_vs_single"] <= 1e-5 and

@@ -107,7 +107,11 @@ def main():
         one.close()
     dist.barrier()
     dist.destroy_process_group()
-    print("EPRESULT", rank, json.dumps(results), flush=True)
+    # one write() per line: the two ranks share the parent's pipe, and a line
+    # under the pipe buffer size is written whole
+    sys.stdout.flush()
+    sys.stdout.write(f"EPRESULT {rank} {json.dumps(results)}\n")
+    sys.stdout.flush()
     bad = [n for n, r in results.items()
            if not (r["out"] and r["ids"] and r["slots"] and r["shared"] and r["oracle"])]
     sys.exit(1 if bad else 0)
