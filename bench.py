@@ -376,6 +376,53 @@ def _h2d_rate(torch, nbytes=1 << 30, reps=5):
     return nbytes * reps / (a.elapsed_time(b) / 1e3) / 1e9
 
 
+def probe_a2a(sizes_mb):
+    """NCCL all-to-all bandwidth for comparison with the expert-parallel
+    dispatch (run under torchrun, one rank per GPU): per rank `mb` MB of bf16
+    split evenly over the ranks, 10 timed calls after 3, CUDA events, max over
+    ranks. Without a GPU it runs on gloo and the CPU (a check of the plumbing
+    only; its numbers mean nothing)."""
+    import torch
+    import torch.distributed as dist
+    cuda = torch.cuda.is_available()
+    dist.init_process_group("nccl" if cuda else "gloo")
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = "cpu"
+    if cuda:
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dev = "cuda"
+    for mb in sizes_mb:
+        n = (int(mb * (1 << 20)) // 2) // world * world
+        a = torch.zeros(n, dtype=torch.bfloat16, device=dev)
+        b = torch.empty_like(a)
+        for _ in range(3):
+            dist.all_to_all_single(b, a)
+        if cuda:
+            torch.cuda.synchronize()
+        dist.barrier()
+        t0 = time.time()
+        if cuda:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        for _ in range(10):
+            dist.all_to_all_single(b, a)
+        if cuda:
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / 10
+        else:
+            ms = (time.time() - t0) * 1e3 / 10
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            out = n * 2 * (world - 1) / world
+            print(json.dumps({"probe": "a2a", "mb_per_rank": mb, "world": world,
+                              "ms": round(float(t.item()), 4),
+                              "gbs_out_per_rank": round(out / float(t.item()) / 1e6, 1),
+                              "device": dev}), flush=True)
+    dist.destroy_process_group()
+
+
 def probe_ingest(E, nshards, repeat):
     import shutil
     import tempfile
@@ -680,9 +727,12 @@ def main():
                     help="profiling case: override the (routed and shared) intermediate size")
     ap.add_argument("--gemv-max", type=int, default=0,
                     help="AUTO path: segments up to this many tokens use the GEMV (0 = default)")
-    ap.add_argument("--probe", default="", choices=["", "gemv", "ingest"],
+    ap.add_argument("--probe", default="", choices=["", "gemv", "ingest", "a2a"],
                     help="instead of the layer benchmark: the GEMV twin on the attention "
-                         "shapes, or checkpoint ingest throughput")
+                         "shapes, checkpoint ingest throughput, or (under torchrun) NCCL "
+                         "all-to-all bandwidth")
+    ap.add_argument("--probe-mb", type=float, nargs="+", default=[32, 116, 512],
+                    help="a2a probe: MB per rank")
     ap.add_argument("--probe-experts", type=int, default=32)
     ap.add_argument("--probe-shards", type=int, default=4)
     ap.add_argument("--probe-repeat", type=int, default=3)
@@ -692,6 +742,9 @@ def main():
         return
     if args.probe == "ingest":
         probe_ingest(args.probe_experts, args.probe_shards, args.probe_repeat)
+        return
+    if args.probe == "a2a":
+        probe_a2a(args.probe_mb)
         return
     args.warmup = max(3, args.warmup)
     wl = WORKLOADS[args.config]
