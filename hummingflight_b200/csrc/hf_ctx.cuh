@@ -104,6 +104,8 @@ struct hf_moe_ctx {
     uint16_t* xp_hi = nullptr;   // GEMM path: activations gathered by position
     uint16_t* xp_lo = nullptr;
     hf::GemmMaps maps1{}, maps2{};  // activation-side tensor maps (GEMM1, GEMM2)
+    // the same with kPairBoxB-row activation boxes, for the CTA-pair passes
+    hf::GemmMaps maps1w{}, maps2w{};
     // host-buffer API staging
     void* x_dev = nullptr;
     float* out_dev = nullptr;

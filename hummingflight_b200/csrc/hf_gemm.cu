@@ -298,9 +298,13 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
             // token rows of B this CTA loads: all of the tile (one CTA) or its
             // half of the MMA's N (pair; N rounded up to 32)
             const int half = PAIR ? ((t.n + 31) & ~31) / 2 : 0;
-            const int nb = PAIR ? half / kBoxRowsB : (t.n + kBoxRowsB - 1) / kBoxRowsB;
+            // rows of one activation box (the launcher checks box <= kBRows);
+            // a last box may reach past the tile: those rows are loaded (or
+            // zero-filled past the tensor) but not read by the MMA
+            const int box = a.box_b > 0 ? a.box_b : kBoxRowsB;
+            const int nb = PAIR ? (half + box - 1) / box : (t.n + box - 1) / box;
             const int brow0 = t.seg + t.n0 + (PAIR ? int(rank) * half : 0);
-            const uint32_t bytes = (NUM_A * kTileABytes + NUM_B * nb * (kBoxRowsB * 128)) * (PAIR ? 2 : 1);
+            const uint32_t bytes = (NUM_A * kTileABytes + NUM_B * nb * (box * 128)) * (PAIR ? 2 : 1);
             const CUtensorMap* mA = t.shared ? &tmA_sh : &tmA;
             const CUtensorMap* mA1 = (t.shared && a.which == 1) ? &tmA_sh2 : mA;
             const CUtensorMap* mB0 = (a.which == 2 && t.shared) ? &tmB0_sh : &tmB0;
@@ -321,10 +325,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                     tma_load_2d_pair(st, mA, fb, kb * 64, rA0);
                     if (NUM_A == 2) tma_load_2d_pair(st + kTileABytes, mA1, fb, kb * 64, rA1);
                     for (int j = 0; j < nb; ++j) {
-                        const int row = brow0 + j * kBoxRowsB;
-                        tma_load_2d_pair(sb + j * (kBoxRowsB * 128), mB0, fb, kb * 64, row);
+                        const int row = brow0 + j * box;
+                        tma_load_2d_pair(sb + j * (box * 128), mB0, fb, kb * 64, row);
                         if (NUM_B == 2)
-                            tma_load_2d_pair(sb + C::kBRows * 128 + j * (kBoxRowsB * 128), mB1, fb,
+                            tma_load_2d_pair(sb + C::kBRows * 128 + j * (box * 128), mB1, fb,
                                              kb * 64, row);
                     }
                 } else {
@@ -332,10 +336,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
                     tma_load_2d(st, mA, &full[s], kb * 64, rA0);
                     if (NUM_A == 2) tma_load_2d(st + kTileABytes, mA1, &full[s], kb * 64, rA1);
                     for (int j = 0; j < nb; ++j) {
-                        const int row = brow0 + j * kBoxRowsB;
-                        tma_load_2d(sb + j * (kBoxRowsB * 128), mB0, &full[s], kb * 64, row);
+                        const int row = brow0 + j * box;
+                        tma_load_2d(sb + j * (box * 128), mB0, &full[s], kb * 64, row);
                         if (NUM_B == 2)
-                            tma_load_2d(sb + BN * 128 + j * (kBoxRowsB * 128), mB1, &full[s],
+                            tma_load_2d(sb + BN * 128 + j * (box * 128), mB1, &full[s],
                                         kb * 64, row);
                     }
                 }
@@ -782,6 +786,11 @@ static hf_status launch_one(const GemmMaps& m, const GemmArgs& a, int grid, cuda
     if (args.plan_smem) smem += plan_bytes;
     else if (!a.plan) return fail(HF_ERR_ARG, "plan-free GEMM needs its shared-memory plan slot");
     if (!a.sched) return fail(HF_ERR_ARG, "GEMM launch without a tile-scheduler counter");
+    // an activation box must fit this CTA's B region of a stage, and the wide
+    // boxes only come with the pair tiles' wide maps
+    if (a.box_b != 0 && a.box_b != kBoxRowsB &&
+        !(PAIR && a.box_b == kPairBoxB && C::kBRows >= kPairBoxB))
+        return fail(HF_ERR_ARG, "GEMM activation box does not fit the tile");
     HF_CUDA(ensure_smem(reinterpret_cast<const void*>(kern), smem));
     if (PAIR) grid = pair_grid(reinterpret_cast<const void*>(kern), smem, grid);
     kern<<<grid, kGemmThreads, smem, st>>>(m.A, m.A_sh, m.A_sh2, m.B0, m.B1, m.B0_sh, m.B1_sh, args);

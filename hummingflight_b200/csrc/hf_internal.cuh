@@ -363,7 +363,13 @@ struct GemmArgs {
     // GEMM2 (no resid, nsplit == 1): outputs as one FP16 plane holding
     // y * 2^-kYF16Shift (y and yrow[] then address __half elements)
     int y16;
+    // rows of one activation (B) box of the tensor maps passed: 16, or
+    // kPairBoxB on CTA-pair passes given the wide maps (0 means 16)
+    int box_b;
 };
+// activation box rows of the wide maps (a CTA of a 256-token pair tile loads
+// its 128 token rows in 2 boxes instead of 8)
+constexpr int kPairBoxB = 64;
 // mid is stored as FP16 times 2^-6: finite up to 65504 * 64 ~ 4.2e6, full
 // 11-bit precision from 2^-8 up; smaller values keep an absolute error
 // below 2^-19

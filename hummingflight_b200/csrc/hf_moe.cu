@@ -234,6 +234,14 @@ hf_status run_route(hf_moe_ctx* c, LayerBuf& L, const RouteArgs& ra, cudaStream_
     return HF_OK;
 }
 
+static bool gemm_wide_b() {
+    static const bool on = [] {
+        const char* e = std::getenv("HF_GEMM_WIDE_B");
+        return !(e && std::atoi(e) == 0);
+    }();
+    return on;
+}
+
 hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStream_t st) {
     if (w.maybe_gemm) {
         GatherArgs gx{};
@@ -283,6 +291,9 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         p2.done(1);
     }
     GemmArgs gm{};
+    // CTA-pair passes load their activations in kPairBoxB-row boxes (tuning
+    // knob HF_GEMM_WIDE_B=0 keeps 16-row boxes)
+    const bool wide = w.pair && gemm_wide_b();
     if (w.maybe_gemm) {
         gm.plan = w.plan;
         gm.pl = w.pl;
@@ -303,7 +314,8 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.sched = c->sched;
         gm.down_f16 = w.down_f16;
         gm.groups = L.groups + w.groups_base;
-        GemmMaps m1 = c->maps1;
+        gm.box_b = wide ? kPairBoxB : 0;
+        GemmMaps m1 = wide ? c->maps1w : c->maps1;
         m1.A = L.gu;
         m1.A_sh = L.sh_gate;
         m1.A_sh2 = L.sh_up;
@@ -326,7 +338,10 @@ hf_status run_experts(hf_moe_ctx* c, LayerBuf& L, const ExpertWork& w, cudaStrea
         gm.sig_slot = w.sig_slot;
         gm.sig_seq = w.sig_seq;
         gm.y16 = w.y16;
-        GemmMaps m2 = c->maps2;
+        // the down pass runs on pairs only with its 512-row tiles
+        const bool wide2 = wide && w.m2 == 512;
+        gm.box_b = wide2 ? kPairBoxB : 0;
+        GemmMaps m2 = wide2 ? c->maps2w : c->maps2;
         m2.A = L.dn;
         m2.A_sh = L.sh_down;
         m2.A_sh2 = L.sh_down;
@@ -559,6 +574,18 @@ hf_status hf_moe_create(hf_moe_ctx** out, const hf_moe_config* cfg) {
         M(&x->maps2.B1, x->mid_lo, x->I, x->inter_max);
         M(&x->maps2.B0_sh, x->mid_hi, x->Is > 0 ? x->Is : x->I, x->inter_max);
         M(&x->maps2.B1_sh, x->mid_lo, x->Is > 0 ? x->Is : x->I, x->inter_max);
+        // the same views with kPairBoxB-row boxes (CTA-pair passes)
+        auto W = [&](CUtensorMap* m, const void* b, int cols, int pitch) {
+            if (s == HF_OK) s = make_map_bf16(m, b, cols, slots, pitch, kPairBoxB);
+        };
+        W(&x->maps1w.B0, x->xp_hi, x->H, x->H);
+        W(&x->maps1w.B1, x->xp_lo, x->H, x->H);
+        x->maps1w.B0_sh = x->maps1w.B0;
+        x->maps1w.B1_sh = x->maps1w.B1;
+        W(&x->maps2w.B0, x->mid_hi, x->I, x->inter_max);
+        W(&x->maps2w.B1, x->mid_lo, x->I, x->inter_max);
+        W(&x->maps2w.B0_sh, x->mid_hi, x->Is > 0 ? x->Is : x->I, x->inter_max);
+        W(&x->maps2w.B1_sh, x->mid_lo, x->Is > 0 ? x->Is : x->I, x->inter_max);
         if (s != HF_OK) {
             std::string m = g_last_error;
             free_ctx(x);
