@@ -385,6 +385,13 @@ hf_status st_parse(hf_st_file* f, const hf_st_options& o, hf_st_stats& s) {
                     break;
                 }
                 t.shape.push_back(int64_t(u));
+                // a product past 2^64 would wrap and could then match the byte
+                // span by accident: such a shape describes no tensor (the
+                // reference's size_t product wraps here; this parser rejects)
+                if (u != 0 && numel > UINT64_MAX / u) {
+                    shape_ok = false;
+                    break;
+                }
                 numel *= u;
             }
         }
@@ -673,6 +680,9 @@ hf_status hf_st_layer_shards(const char* dir, int model_layer, char* buf, size_t
             for (const auto& kv : wm->obj)
                 if (kv.second.kind == JVal::Str && kv.first.compare(0, pre.size(), pre) == 0)
                     names.insert(kv.second.str);
+            if (names.empty())
+                return fail(HF_ERR_ARG, "hf_st_layer_shards: the index names no tensor of model.layers." +
+                                            std::to_string(model_layer) + ".mlp");
             out.clear();
             for (const std::string& n : names) {
                 const std::string p = (fs::path(dir) / n).string();

@@ -78,10 +78,11 @@ HF_API hf_status hf_st_upload(const hf_st_file* f, int i, void* dev_dst, uint64_
  * `model_layer`'s MLP tensors (model.layers.<L>.mlp.*), as WeightIndex::build
  * finds them (weight_index.cpp:79-130): the directory's *.safetensors files,
  * sorted; when model.safetensors.index.json is there and has a weight_map,
- * only the shards it names for those tensors (none if it names none). The
- * paths are written NUL-separated into buf; *num_shards receives their count.
- * HF_ERR_ARG: no shard in dir, an index entry naming a missing shard, or buf
- * too small (*num_shards is still set). No device is touched. */
+ * only the shards it names for those tensors. The paths are written
+ * NUL-separated into buf; *num_shards receives their count. HF_ERR_ARG: no
+ * shard in dir, an index whose weight_map names no tensor of that layer's MLP
+ * (a wrong layer number), an index entry naming a missing shard, or buf too
+ * small (*num_shards is still set). No device is touched. */
 HF_API hf_status hf_st_layer_shards(const char* dir, int model_layer, char* buf,
                                     size_t buf_bytes, int* num_shards);
 

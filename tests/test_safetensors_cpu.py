@@ -57,6 +57,26 @@ def test_parser_matches_reference(tmp_path, case):
     f.close()
 
 
+def test_shape_product_past_64_bits_is_rejected(tmp_path):
+    """A shape whose element count wraps 64 bits to a small number that matches
+    the byte span (641 * 6700417 * 65535 * 65537 = 2^64 - 1, squared = 1 mod
+    2^64, times 4 elements = the 8 bytes given) is rejected as a shape error.
+    The reference's parser multiplies in size_t without this guard
+    (safetensors.cpp:153-164, 208) and would accept it, so this case is not in
+    the reference-generated golden set."""
+    from st_cases import build, entry, header_text
+    S = st()
+    wrap = [641, 6700417, 65535, 65537] * 2 + [4]
+    good = entry("ok.weight", "BF16", [4], [8, 16])
+    bad = entry("wrapped.weight", "BF16", wrap, [0, 8])
+    blob = build(header_text([bad, good]), bytes(16))
+    f = open_case(tmp_path, "wrapped", "strict", blob)
+    assert f is not None
+    assert [t.name for t in f.tensors()] == ["ok.weight"]
+    assert f.stats_dict()["shape_rejected"] == 1
+    f.close()
+
+
 def test_read_returns_the_file_bytes(tmp_path):
     S = st()
     rng = np.random.default_rng(9)
@@ -132,7 +152,8 @@ def test_layer_shards_follow_the_index(tmp_path):
     idx.write_text(js.dumps({"metadata": {"total_size": 1}, "weight_map": wm}))
     assert S.layer_shards(str(tmp_path), 3) == all3[1:]
     assert S.layer_shards(str(tmp_path), 30) == all3[:1]
-    assert S.layer_shards(str(tmp_path), 7) == []
+    with pytest.raises(HfError, match="names no tensor of model.layers.7.mlp"):
+        S.layer_shards(str(tmp_path), 7)              # a wrong layer number is an error
     wm["model.layers.7.mlp.gate.weight"] = "model-00009-of-00009.safetensors"
     idx.write_text(js.dumps({"weight_map": wm}))
     with pytest.raises(HfError, match="missing shard"):
