@@ -128,3 +128,32 @@ def test_block_and_rmsnorm_arguments_checked_before_any_device_call():
     assert L.hf_rmsnorm(p, None, 1e-5, T, H, q, 7, None) == _lib.HF_ERR_ARG
     assert L.hf_rmsnorm(p + 4, None, 1e-5, T, H, q, _lib.HF_F32, None) == _lib.HF_ERR_ARG
     assert L.hf_rmsnorm(p, None, 1e-5, 0, H, q, _lib.HF_F32, None) == _lib.HF_OK
+
+
+def test_route_noalloc_arguments_checked_before_any_device_call():
+    """hf_moe_route_noalloc rejects sizes beyond its fixed in-library scratch
+    (T <= 128, E <= 256, k <= 8) and bad arguments on the host, before it looks
+    up the scratch array's device address (the fake pointers below are never
+    dereferenced)."""
+    L = _lib.lib()
+    p = 0x10000
+    names = ["router", "bias", "x", "dt", "T", "H", "E", "k", "scale", "norm", "shared",
+             "ids", "w", "counts", "offsets", "perm", "st"]
+    ok = [p, None, p, _lib.HF_BF16, 16, 256, 64, 8, 2.5, 1, 1, p, p, p, p, p, None]
+
+    def call(**kw):
+        a = list(ok)
+        for k, v in kw.items():
+            a[names.index(k)] = v
+        return L.hf_moe_route_noalloc(*a)
+
+    for bad in (dict(T=129), dict(T=-1), dict(E=257), dict(E=0)):
+        assert call(**bad) == _lib.HF_ERR_ARG, bad
+        assert b"static scratch" in L.hf_last_error(), bad
+    assert call(k=9) == _lib.HF_ERR_ARG
+    assert call(k=0) == _lib.HF_ERR_ARG
+    assert call(H=60) == _lib.HF_ERR_ARG              # not a multiple of 8
+    assert call(dt=7) == _lib.HF_ERR_ARG
+    assert call(perm=None) == _lib.HF_ERR_ARG
+    assert call(router=None) == _lib.HF_ERR_ARG
+    assert call(x=p + 8) == _lib.HF_ERR_ARG           # not 16-byte aligned
