@@ -5,8 +5,10 @@
 // {dtype, shape, data_offsets}; the same validation rules and rejection
 // counters as the reference, with a small JSON reader of our own (the
 // reference uses picojson). Where picojson decides the outcome, the reader
-// does the same: numbers are values (4.0 is a valid size), a repeated key
-// keeps its last value, text after the header object is ignored.
+// does the same: numbers are spelled and valued as picojson reads them ("08"
+// and "16." are numbers, 4.0 is a valid size), data offsets are truncated as
+// the reference's uint64_t conversion does, a repeated key keeps its last
+// value, text after the header object is ignored.
 //
 // Copying (what ExpertGpuCache's pinned ping-pong staging does per expert,
 // compute/cuda_backend.cpp:190-364, done for a whole layer at once): the
@@ -147,38 +149,37 @@ private:
         }
         return false;
     }
+    // Numbers follow picojson's reading, which decides what the reference
+    // accepts: a number starts with a digit or '-', runs over the characters
+    // [0-9+-eE.], and is valid when strtod consumes the whole run -- so "08",
+    // "16." and "-.5" are numbers and "1e" is not. A number beyond the double
+    // range makes the header invalid (picojson throws on it, so the reference
+    // cannot open such a file). A run of digits (with an optional '-') also
+    // keeps its exact integer value.
+    static bool num_char(char c) {
+        return (c >= '0' && c <= '9') || c == '+' || c == '-' || c == 'e' || c == 'E' || c == '.';
+    }
     bool number(JVal& v) {
+        if (p_ >= e_ || !((*p_ >= '0' && *p_ <= '9') || *p_ == '-')) return false;
         const char* s = p_;
-        bool neg = false;
-        if (p_ < e_ && *p_ == '-') {
-            neg = true;
-            ++p_;
-        }
-        if (p_ >= e_ || *p_ < '0' || *p_ > '9') return false;
-        if (*p_ == '0' && p_ + 1 < e_ && p_[1] >= '0' && p_[1] <= '9') return false;
-        bool integral = true, overflow = false;
+        while (p_ < e_ && num_char(*p_)) ++p_;
+        const std::string run(s, p_);
+        char* end = nullptr;
+        v.num = std::strtod(run.c_str(), &end);
+        if (end != run.c_str() + run.size() || !std::isfinite(v.num)) return false;
+        const bool neg = run[0] == '-';
+        bool digits = run.size() > (neg ? 1u : 0u), overflow = false;
         uint64_t u = 0;
-        while (p_ < e_ && *p_ >= '0' && *p_ <= '9') {
-            const uint64_t d = uint64_t(*p_ - '0');
+        for (size_t i = neg ? 1 : 0; i < run.size() && digits; ++i) {
+            if (run[i] < '0' || run[i] > '9') {
+                digits = false;
+                break;
+            }
+            const uint64_t d = uint64_t(run[i] - '0');
             if (u > (UINT64_MAX - d) / 10) overflow = true;
             else u = u * 10 + d;
-            ++p_;
         }
-        if (p_ < e_ && *p_ == '.') {
-            integral = false;
-            ++p_;
-            if (p_ >= e_ || *p_ < '0' || *p_ > '9') return false;
-            while (p_ < e_ && *p_ >= '0' && *p_ <= '9') ++p_;
-        }
-        if (p_ < e_ && (*p_ == 'e' || *p_ == 'E')) {
-            integral = false;
-            ++p_;
-            if (p_ < e_ && (*p_ == '+' || *p_ == '-')) ++p_;
-            if (p_ >= e_ || *p_ < '0' || *p_ > '9') return false;
-            while (p_ < e_ && *p_ >= '0' && *p_ <= '9') ++p_;
-        }
-        v.num = std::strtod(std::string(s, p_).c_str(), nullptr);
-        if (integral && !overflow) {
+        if (digits && !overflow) {
             v.kind = JVal::Int;
             v.neg = neg;
             v.u = u;
@@ -276,6 +277,20 @@ constexpr uint64_t kMaxHeader = 100ull << 20;  // the format's own header limit
 
 // A JSON number used as a size: a non-negative integral value (4, 4.0, 4e0,
 // -0 all read as the reference's doubles do).
+// A data offset as the reference converts it (uint64_t of the parsed double):
+// truncated toward zero, so 16.9 is 16 and -0.5 is 0. Values whose truncation
+// is negative or past 2^64 have no defined conversion there and are rejected.
+bool as_offset(const JVal& v, uint64_t& out) {
+    if (v.kind == JVal::Int) {
+        if (v.neg && v.u != 0) return false;
+        out = v.u;
+        return true;
+    }
+    if (v.kind != JVal::Num || !(v.num > -1.0) || !(v.num < 18446744073709551616.0)) return false;
+    out = uint64_t(v.num);
+    return true;
+}
+
 bool as_size(const JVal& v, uint64_t& out) {
     if (v.kind == JVal::Int) {
         if (v.neg && v.u != 0) return false;
@@ -400,7 +415,7 @@ hf_status st_parse(hf_st_file* f, const hf_st_options& o, hf_st_stats& s) {
             continue;
         }
         if (!jo || jo->kind != JVal::Arr || jo->arr.size() != 2 ||
-            !as_size(jo->arr[0], t.begin) || !as_size(jo->arr[1], t.end) || t.end <= t.begin) {
+            !as_offset(jo->arr[0], t.begin) || !as_offset(jo->arr[1], t.end) || t.end <= t.begin) {
             reject(s.bounds_rejected);
             continue;
         }

@@ -59,21 +59,28 @@ class SafeTensors:
         return int(_lib.lib().hf_st_count(self._h))
 
     def info(self, i: int) -> TensorInfo:
+        """Tensor i. Names are the header's bytes; bytes that are not UTF-8
+        become surrogate escapes, so find(name) still matches them."""
         name, dtype = ctypes.c_char_p(), ctypes.c_char_p()
         nd = ctypes.c_int()
-        cap = 64
-        shape = (ctypes.c_int64 * cap)()
         off, nb = ctypes.c_uint64(), ctypes.c_uint64()
-        call("hf_st_tensor", self._h, i, ctypes.byref(name), ctypes.byref(dtype), ctypes.byref(nd),
-             shape, cap, ctypes.byref(off), ctypes.byref(nb))
-        return TensorInfo(name.value.decode(), dtype.value.decode(),
+        cap = 8
+        while True:
+            shape = (ctypes.c_int64 * cap)()
+            call("hf_st_tensor", self._h, i, ctypes.byref(name), ctypes.byref(dtype),
+                 ctypes.byref(nd), shape, cap, ctypes.byref(off), ctypes.byref(nb))
+            if nd.value <= cap:
+                break
+            cap = nd.value  # more dimensions than the buffer: ask again with room for all
+        return TensorInfo(name.value.decode("utf-8", "surrogateescape"),
+                          dtype.value.decode("utf-8", "surrogateescape"),
                           tuple(shape[d] for d in range(nd.value)), off.value, nb.value)
 
     def tensors(self) -> List[TensorInfo]:
         return [self.info(i) for i in range(len(self))]
 
     def find(self, name: str) -> int:
-        return int(_lib.lib().hf_st_find(self._h, name.encode()))
+        return int(_lib.lib().hf_st_find(self._h, name.encode("utf-8", "surrogateescape")))
 
     def read(self, name: str) -> np.ndarray:
         i = self.find(name)
