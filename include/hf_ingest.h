@@ -61,7 +61,8 @@ HF_API hf_status hf_st_close(hf_st_file* f);
 HF_API int hf_st_count(const hf_st_file* f);
 /* Tensor i: name, dtype ("BF16", "F32", ...), its number of dims (the first
  * shape_cap of them go to shape), absolute file offset of its data and its
- * byte size. Strings live as long as the file. */
+ * byte size. Strings live as long as the file; they are C strings, so a name
+ * whose JSON spells \u0000 ends there. */
 HF_API hf_status hf_st_tensor(const hf_st_file* f, int i, const char** name, const char** dtype,
                               int* ndim, int64_t* shape, int shape_cap, uint64_t* file_offset,
                               uint64_t* bytes);

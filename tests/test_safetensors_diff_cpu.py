@@ -6,7 +6,8 @@ from the reference tree by `make -C oracle st`. This test mutates the parser
 cases of tests/st_cases.py with a seeded generator -- bit flips, JSON
 punctuation, truncations, repeated spans, rewritten header lengths, number
 spellings picojson accepts or refuses ("08", "16.", "-.5", "1e2", "1e", ".5",
-"+4", ...), junk after the header -- and opens every mutant with both parsers
+"+4", ...), string escapes (surrogate pairs, lone surrogates, bad \\u digits,
+raw control and non-UTF-8 bytes), junk after the header -- and opens every mutant with both parsers
 under the strict and the loose options. Both must agree on whether the file
 opens, on every counter, and on every accepted tensor (name, dtype, shape,
 absolute offset, byte size).
@@ -42,6 +43,9 @@ PUNCT = b'{}[]":,0123456789-.eE\\u \t\n'
 NUMBERS = [b"08", b"16.", b"-.5", b"1e2", b"4.0", b"-0", b"0.5", b"16.9", b"1E1", b"007", b"2e-1",
            b"8.", b"-0.0", b"1.e1", b"0e0", b"24.99", b"1e+1", b"-", b"1e", b".5", b"+4", b"1-2",
            b"1..2", b"0x8", b"1e1e1"]
+ESCAPES = [b"\\u00e9", b"\\ud83d\\ude00", b"\\ud83d", b"\\udc00", b"\\ud83dx", b"\\x", b"\\/",
+           b"\\b", b"\\u12", b"\\uZZZZ", b"\x01", b"\x7f", b"\xc3\xa9", b"\xff", b'\\"', b"\\\\",
+           b"\\u0000", b"\\ud800\\u0041"]
 NUM = re.compile(rb"[0-9-][0-9+\-eE.]*")
 
 
@@ -49,7 +53,7 @@ def mutate(blob: bytes, rng: random.Random) -> bytes:
     b = bytearray(blob)
     for _ in range(1 + rng.randrange(4)):
         n = len(b)
-        op = rng.randrange(7)
+        op = rng.randrange(8)
         if op == 0 and n:
             b[rng.randrange(n)] ^= 1 << rng.randrange(8)
         elif op == 1 and n:
@@ -71,6 +75,11 @@ def mutate(blob: bytes, rng: random.Random) -> bytes:
             if digits:
                 i = rng.choice(digits)
                 b[i:i + 1] = rng.choice(NUMBERS)
+        elif op == 7:
+            quotes = [i for i in range(8, n) if b[i] == 0x22]
+            if quotes:
+                i = rng.choice(quotes) + 1
+                b[i:i] = rng.choice(ESCAPES)
     return bytes(b)
 
 
@@ -116,9 +125,10 @@ def reference(path, opts):
     j = json.loads(out.splitlines()[-1])
     if not j["ok"]:
         return {"ok": False}
+    # names come back through the C ABI as C strings: one holding \u0000 ends there
     return {"ok": True, "stats": j["stats"],
-            "tensors": sorted((t["name"], t["dtype"], t["shape"], t["offset"], t["bytes"])
-                              for t in j["tensors"])}
+            "tensors": sorted((t["name"].split("\0")[0], t["dtype"], t["shape"], t["offset"],
+                               t["bytes"]) for t in j["tensors"])}
 
 
 @pytest.mark.parametrize("seed", [11, 12, 13])
