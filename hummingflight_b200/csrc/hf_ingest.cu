@@ -27,6 +27,7 @@
 #include <fstream>
 #include <set>
 #include <chrono>
+#include <clocale>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -163,7 +164,13 @@ private:
         if (p_ >= e_ || !((*p_ >= '0' && *p_ <= '9') || *p_ == '-')) return false;
         const char* s = p_;
         while (p_ < e_ && num_char(*p_)) ++p_;
-        const std::string run(s, p_);
+        // '.' becomes the C library's decimal point for strtod, as in picojson
+        // (the host program may have set a locale that writes decimals with ',')
+        std::string run;
+        for (const char* q = s; q < p_; ++q) {
+            if (*q == '.') run += std::localeconv()->decimal_point;
+            else run += *q;
+        }
         char* end = nullptr;
         v.num = std::strtod(run.c_str(), &end);
         if (end != run.c_str() + run.size() || !std::isfinite(v.num)) return false;
@@ -277,6 +284,19 @@ constexpr uint64_t kMaxHeader = 100ull << 20;  // the format's own header limit
 
 // A JSON number used as a size: a non-negative integral value (4, 4.0, 4e0,
 // -0 all read as the reference's doubles do).
+bool as_size(const JVal& v, uint64_t& out) {
+    if (v.kind == JVal::Int) {
+        if (v.neg && v.u != 0) return false;
+        out = v.u;
+        return true;
+    }
+    if (v.kind != JVal::Num || !(v.num >= 0.0) || v.num != std::floor(v.num) ||
+        v.num > 9007199254740992.0)
+        return false;
+    out = uint64_t(v.num);
+    return true;
+}
+
 // A data offset as the reference converts it (uint64_t of the parsed double):
 // truncated toward zero, so 16.9 is 16 and -0.5 is 0. Values whose truncation
 // is negative or past 2^64 have no defined conversion there and are rejected.
@@ -287,19 +307,6 @@ bool as_offset(const JVal& v, uint64_t& out) {
         return true;
     }
     if (v.kind != JVal::Num || !(v.num > -1.0) || !(v.num < 18446744073709551616.0)) return false;
-    out = uint64_t(v.num);
-    return true;
-}
-
-bool as_size(const JVal& v, uint64_t& out) {
-    if (v.kind == JVal::Int) {
-        if (v.neg && v.u != 0) return false;
-        out = v.u;
-        return true;
-    }
-    if (v.kind != JVal::Num || !(v.num >= 0.0) || v.num != std::floor(v.num) ||
-        v.num > 9007199254740992.0)
-        return false;
     out = uint64_t(v.num);
     return true;
 }
