@@ -12,7 +12,8 @@
 // fail). It also feeds hf_st_layer_shards mutated checkpoint indexes and the
 // expert-parallel planners random loads and counts, checking the invariants
 // their callers rely on (a placement is a permutation with E/W experts per
-// rank; an exchange plan places every received row exactly once).
+// rank; an exchange plan places every received row exactly once) and context
+// creation random configurations (refused on the host, never a crash).
 //
 // Usage: host_fuzz <corpus dir> <scratch dir> <iterations> <seed>
 // Exit 0 when every check held; a sanitizer report aborts the program.
@@ -221,6 +222,43 @@ static void fuzz_planners(std::mt19937_64& rng, int iters) {
     }
 }
 
+// Context creation validates its configuration on the host before touching a
+// device: on a machine without a GPU every config below is refused with
+// HF_ERR_ARG or, when it is valid, HF_ERR_UNSUPPORTED (never a crash). Skipped
+// where a device exists (valid configs would allocate for real).
+static void fuzz_configs(std::mt19937_64& rng, int iters) {
+    hf_moe_config probe{64, 8, 2, 32, 32, 2.5f, 1, 1, 4, 0, 0, 0, 0, 1, nullptr};
+    hf_moe_ctx* pc = nullptr;
+    if (hf_moe_create(&pc, &probe) == HF_OK) {
+        hf_moe_destroy(pc);
+        return;
+    }
+    const int pick[] = {-1, 0, 1, 7, 8, 9, 64, 255, 256, 1024, 1025, 6144, 1 << 30, 2147483647};
+    for (int it = 0; it < iters; ++it) {
+        auto r = [&] { return pick[rng() % (sizeof(pick) / sizeof(pick[0]))]; };
+        hf_moe_config c{};
+        c.hidden_size = r();
+        c.num_experts = r();
+        c.num_experts_per_tok = r();
+        c.moe_intermediate_size = r();
+        c.shared_intermediate_size = r();
+        c.routed_scaling_factor = 2.5f;
+        c.norm_topk_prob = 1;
+        c.num_layers = r();
+        c.max_tokens = r();
+        c.device = int(rng() % 3) - 1;
+        c.path = int(rng() % 5) - 1;
+        c.gemv_max_tokens = r();
+        c.ep_world = 1;
+        hf_moe_ctx* ctx = nullptr;
+        const hf_status s = hf_moe_create(&ctx, &c);
+        CHECK(s == HF_ERR_ARG || s == HF_ERR_UNSUPPORTED, "create returned %d", int(s));
+        CHECK(ctx == nullptr, "a failed create returned a context");
+        const size_t w = hf_dense_mlp_workspace_size(r(), r(), r());
+        (void)w;
+    }
+}
+
 int main(int argc, char** argv) {
     if (argc != 5) {
         std::fprintf(stderr, "usage: %s <corpus dir> <scratch dir> <iterations> <seed>\n", argv[0]);
@@ -275,6 +313,7 @@ int main(int argc, char** argv) {
     std::remove(tmp.c_str());
     fuzz_layer_shards(scratch, rng, iters / 10 + 1);
     fuzz_planners(rng, iters / 10 + 1);
+    fuzz_configs(rng, iters / 10 + 1);
     std::printf("%s: %d seeds, %d mutants, %ld opens accepted, %ld tensors walked, %d failed checks\n",
                 g_failures ? "FAIL" : "OK", int(seeds.size()), iters, g_opened, g_tensors, g_failures);
     return g_failures ? 1 : 0;
